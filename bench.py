@@ -1,0 +1,370 @@
+"""Benchmark of the B200 FP8 MoE layer (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload mixtral|dsv3|qwen3|tiny] [--impl reference]
+
+A step is one forward of the MoE FFN layer of the workload through the scheme
+API (``SchemeInstance.run()``): quant -> all-gather -> align -> GEMM1 -> GEMM2 ->
+combine -> reduce-scatter.  Default workload: the Mixtral-8x7B shape of the
+BASELINE configs (T=4096 tokens, H=4096, I=14336, E=8, top-2) with TP=N over the
+N GPUs (strong scaling: the layer's T tokens are fixed, sharded T/N per rank).
+Inputs are seeded synthetic tensors with the config's shapes and value
+distributions (no dataset); the weights (>= 176 MB per rank) are larger than L2,
+and L2 is also flushed (256 MB write) between timed steps, outside the events.
+
+``value``: tokens/s of the whole layer (T / step time, step time = per-step max
+over ranks, mean over steps), device-timed with CUDA events on inputs resident
+in HBM.  ``e2e``: the same metric through ``SchemeInstance.run()`` with the
+inputs copied from pinned host memory and the output copied back inside the
+timed region.  ``roofline``: GEMM1 (gate/up, the dominant kernel) FP8 FLOPs of
+the routed (unpadded) pairs over its event-timed duration, against the measured
+FP8 dense peak in ``profiles/peaks.json``.  ``cpu_baseline``: the reference
+algorithm (``oracle.golden.golden_moe``, the numpy restatement of
+``moe_bench/verify.py:14-47``) timed on this host on a bounded token sample.
+``--impl reference`` times only that CPU path (rank 0; other ranks exit 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    # name: (preset, scheme code, human label)
+    "mixtral": ("mixtral", "d1", "mixtral-8x7b-moe-layer TP"),
+    "dsv3": ("dsv3", "d2", "deepseek-v3-moe-layer EP (+shared)"),
+    "qwen3": ("qwen3", "d1", "qwen3-30b-a3b-moe-layer TP decode"),
+    "tiny": ("tiny", "d1", "tiny-moe-layer"),
+}
+
+
+def _peaks() -> dict:
+    out = {}
+    mp = ROOT / "MEASURED_PEAKS.json"
+    if mp.exists():
+        out.update(json.loads(mp.read_text()))
+    pp = ROOT / "profiles" / "peaks.json"
+    if pp.exists():
+        out.update(json.loads(pp.read_text()))
+    return out
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def gemm1_flops(topk_ids, expert_map, inter_local: int, hidden: int) -> float:
+    """Algorithmic FP8 FLOPs of GEMM1 on this rank: 2 * (routed local pairs) * 2I_r * H (pads not counted)."""
+    ids = topk_ids.reshape(-1)
+    pairs = int(ids.numel()) if expert_map is None else int((expert_map[ids.long()] >= 0).sum().item())
+    return 2.0 * pairs * 2 * inter_local * hidden
+
+
+def layer_flops(cfg, topk_ids, expert_map, world: int, parallel: str) -> float:
+    """Per-rank algorithmic FLOPs of the layer (routed + shared), unpadded."""
+    s = cfg.shape
+    ids = topk_ids.reshape(-1)
+    if parallel == "TP":
+        f = 6.0 * s.K * s.intermediate * ids.numel() / world
+    else:
+        pairs = ids.numel() if expert_map is None else int((expert_map[ids.long()] >= 0).sum().item())
+        f = 6.0 * s.K * s.intermediate * pairs
+    if s.shared_experts:
+        tok = s.M_aligned(world) if parallel == "TP" else s.M_aligned(world) // world
+        f += 6.0 * s.K * s.shared_intermediate * tok / (world if parallel == "TP" else 1)
+    return f
+
+
+class CpuGolden:
+    """The numpy restatement of the reference golden (``moe_bench/verify.py:14-47``) on this host.
+
+    Weights are held as bf16 bit patterns and widened per expert inside the loop,
+    as the reference golden does (``w1_bf16[expert].float()``); the sample is the
+    first ``n`` tokens of the same layer (every expert they route to is computed).
+    """
+
+    def __init__(self, bundle):
+        import numpy as np
+        import torch
+
+        from td_benchmark_b200.weights import dequantize_block128
+
+        ck = bundle.ckpt
+
+        def bits(qt):
+            return None if qt is None else dequantize_block128(qt.fp8, qt.scale).view(torch.int16).cpu().numpy().view(
+                np.uint16)
+
+        self.w1, self.w2, self.sw1, self.sw2 = bits(ck.w1), bits(ck.w2), bits(ck.shared_w1), bits(ck.shared_w2)
+        self.hid = bundle.hidden_full.float().cpu().numpy()
+        self.ids = bundle.routing.topk_ids_full.cpu().numpy()
+        self.wts = bundle.routing.topk_weights_full.cpu().numpy()
+        self.cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+    def run(self, n: int) -> float:
+        from oracle import golden as ogolden
+
+        t0 = time.perf_counter()
+        ogolden.golden_moe(self.hid[:n], self.ids[:n], self.wts[:n], self.w1, self.w2, self.sw1, self.sw2)
+        return time.perf_counter() - t0
+
+    def calibrate(self, budget_s: float) -> int:
+        """Largest power-of-two token sample (>= 16) whose run fits the budget."""
+        n = min(16, self.hid.shape[0])
+        t = self.run(n)
+        while 2 * t < budget_s and n < self.hid.shape[0]:
+            n = min(self.hid.shape[0], n * 2)
+            t = self.run(n)
+        return n
+
+    def describe(self, n: int, runs: int, mean_t: float) -> dict:
+        return {"value": n / mean_t, "unit": "tokens/s", "cores": self.cores, "kind": "port",
+                "sample": f"first {n} of {self.hid.shape[0]} tokens through the full layer (numpy fp32 golden of "
+                          f"moe_bench/verify.py:14-47, BLAS threads = host cores); mean of {runs} run(s), "
+                          f"{mean_t:.2f} s each"}
+
+
+def run_reference(args) -> int:
+    import torch
+
+    from td_benchmark_b200 import configs, data
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    preset, _, label = WORKLOADS[args.workload]
+    over = {"M": args.tokens} if args.tokens else {}
+    cfg = configs.preset(preset, **over)
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    gold = CpuGolden(data.build_bundle(cfg, device=dev))
+    n = gold.calibrate(budget_s=min(15.0, 150.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        gold.run(n)
+    times = [gold.run(n) for _ in range(args.steps)]
+    mean_t = sum(times) / len(times)
+    cb = gold.describe(n, len(times), mean_t)
+    s = cfg.shape
+    line = {"impl": "reference", "metric": "moe_layer_tokens_per_s", "value": cb["value"], "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean_t * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded, BASELINE value distributions)",
+            "config": {"workload": label, "tokens": s.M, "hidden": s.K, "intermediate": s.intermediate,
+                       "experts": s.E, "top_k": s.top_k},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="mixtral", choices=sorted(WORKLOADS))
+    ap.add_argument("--tokens", type=int, default=None, help="override the workload's token count")
+    ap.add_argument("--impl", default="b2m", choices=["b2m", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from td_benchmark_b200 import configs, data
+    from td_benchmark_b200.context import init_context
+    from td_benchmark_b200.schemes import REGISTRY
+    from td_benchmark_b200.schemes.b200 import build_layer
+
+    ctx = init_context(backend="nccl", timeout_s=300.0)
+    world, rank = ctx.world_size, ctx.rank
+    dev = ctx.device
+    preset, code, label = WORKLOADS[args.workload]
+    over = {"M": args.tokens} if args.tokens else {}
+    cfg = configs.preset(preset, **over)
+    spec = REGISTRY[code][0]
+    bundle = data.build_bundle(cfg, rank=rank, world_size=world, device=dev)
+    layer, level = build_layer(spec, cfg, ctx, bundle)
+    T = layer.T
+    x = bundle.hidden_local.contiguous()
+    ids = bundle.routing.topk_ids_full.contiguous()
+    wts = bundle.routing.topk_weights_full.contiguous()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-timed steps (inputs resident)
+    for _ in range(args.warmup):
+        layer.forward(x, ids, wts)
+    torch.cuda.synchronize()
+    layer.check()
+    barrier()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    layer.events = []
+    with ClockSampler(dev.index) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            layer.forward(x, ids, wts)
+            ends[i].record()
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    layer.check()
+    local = torch.tensor([s.elapsed_time(e) for s, e in zip(starts, ends)], dtype=torch.float64, device=dev)
+    g1 = []
+    evs = layer.events
+    layer.events = None
+    for i in range(0, len(evs), 3):
+        (_, a), (_, b) = evs[i], evs[i + 1]
+        g1.append(a.elapsed_time(b))
+    if world > 1:
+        dist.all_reduce(local, op=dist.ReduceOp.MAX)
+    per_step = local.cpu().tolist()
+    ms = sum(per_step) / len(per_step)
+
+    # ---- end-to-end through the scheme API with host buffers
+    x_h = x.cpu().pin_memory()
+    ids_h = ids.cpu().pin_memory()
+    wts_h = wts.cpu().pin_memory()
+    out_h = torch.empty(layer.out_local.shape, dtype=torch.bfloat16).pin_memory()
+    x_d, ids_d, wts_d = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(wts)
+
+    def e2e_step():
+        x_d.copy_(x_h, non_blocking=True)
+        ids_d.copy_(ids_h, non_blocking=True)
+        wts_d.copy_(wts_h, non_blocking=True)
+        out = layer.forward(x_d, ids_d, wts_d)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        e_s[i].record()
+        e2e_step()
+        e_e[i].record()
+    torch.cuda.synchronize()
+    barrier()
+    e_local = torch.tensor([s.elapsed_time(e) for s, e in zip(e_s, e_e)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_local, op=dist.ReduceOp.MAX)
+    e_ms = float(e_local.mean().item())
+    h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * 4 + wts_h.numel() * 4
+    d2h = out_h.numel() * out_h.element_size()
+
+    # ---- roofline of GEMM1 on this rank
+    peaks = _peaks()
+    fp8_peak = peaks.get("fp8_tflops")
+    peak_src = "measured (profiles/peaks.json)"
+    if not fp8_peak:
+        fp8_peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
+        peak_src = "2 x measured bf16 (MEASURED_PEAKS.json); no FP8 measurement yet"
+    g1_ms = sum(g1) / len(g1)
+    f1 = gemm1_flops(ids, layer.expert_map, layer.w.inter, layer.H)
+    achieved = f1 / (g1_ms * 1e-3) / 1e12
+    traffic = None
+    tp = ROOT / "profiles" / "traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get(f"gemm1/{args.workload}/{world}")
+    lf = layer_flops(cfg, ids, layer.expert_map, world, spec.parallel)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gold = CpuGolden(bundle)
+        n = gold.calibrate(budget_s=15.0)
+        cpu = gold.describe(n, 1, gold.run(n))
+
+    if rank == 0:
+        s = cfg.shape
+        line = {
+            "metric": "moe_layer_tokens_per_s", "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp8-e4m3 (fp32 accum)",
+            "data": "synthetic (seeded, BASELINE value distributions)",
+            "config": {"workload": label, "tokens": T, "hidden": s.K, "intermediate": s.intermediate,
+                       "experts": s.E, "top_k": s.top_k, "parallelism": f"{spec.parallel.lower()}{world}",
+                       "scheme": code, "shard_level": level, "routing": cfg.routing.imbalance_kind,
+                       "l2": "weights > L2 and 256 MB L2 flush between timed steps"},
+            "e2e": {"value": T / (e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e_ms},
+            "gpu_launches": layer.kernel_launches() * args.steps,
+            "roofline": {"bound": "tensor", "kernel": "gemm1 (gate/up, tcgen05 kind::f8f6f4)",
+                         "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s", "frac": achieved / fp8_peak,
+                         "peak_source": peak_src, "traffic": traffic, "gemm1_ms": g1_ms,
+                         "layer_tflops": lf / (ms * 1e-3) / 1e12,
+                         "layer_frac_of_fp8_peak": lf / (ms * 1e-3) / 1e12 / fp8_peak},
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,145 @@
+/* b2m — B200-native FP8 MoE FFN layer kernels, C ABI.
+ *
+ * The path these entry points implement is the one stmoonar/td_benchmark times as
+ * scheme b2 (moe_bench/overlap/overlap_forward.py:348-622): token-sharded bf16
+ * activations -> 1x128 FP8 group quant -> all-gather -> moe_align_block_size ->
+ * gate/up grouped GEMM + SiLU*mul -> down grouped GEMM with top-k weights ->
+ * top-k combine -> reduce-scatter.
+ *
+ * Conventions
+ *  - Plain pointers and sizes only.  Every pointer is a device pointer unless its
+ *    comment says "host".  Outputs are caller-allocated; no entry point allocates
+ *    device memory except the b2m_symm_* set-up calls, which exist to allocate.
+ *  - Work is enqueued on `stream` (a cudaStream_t passed as void*), asynchronously.
+ *  - Return value: B2M_OK (0) or a positive error class; b2m_last_error() gives the
+ *    message of the last failing call on the calling host thread.
+ *  - Kernels that wait on the pipeline or on peers write a non-zero code into the
+ *    caller's `dev_status` word (int32 on the device, may be NULL) instead of
+ *    trapping; read it after the stream is synchronised.
+ *  - sm_100a (B200) only.
+ */
+#ifndef B2M_H_
+#define B2M_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes (host) */
+#define B2M_OK 0
+#define B2M_ERR_ARG 1         /* bad shape, stride, alignment or null pointer */
+#define B2M_ERR_CUDA 2        /* a CUDA runtime/driver call failed */
+#define B2M_ERR_UNSUPPORTED 3 /* device is not sm_100 or a feature is missing */
+
+/* ---- device status codes (written to dev_status by kernels; first error wins) */
+#define B2M_STATUS_OK 0
+#define B2M_STATUS_TIMEOUT_PRODUCER 0x101 /* TMA producer waited too long for a free stage */
+#define B2M_STATUS_TIMEOUT_MMA 0x102      /* MMA issuer waited too long for operands/TMEM */
+#define B2M_STATUS_TIMEOUT_EPILOGUE 0x103 /* epilogue waited too long for an accumulator */
+#define B2M_STATUS_TIMEOUT_PEER 0x104     /* a peer rank's chunk flag never arrived */
+#define B2M_STATUS_TIMEOUT_DRAIN 0x105    /* teardown could not drain in-flight copies */
+#define B2M_STATUS_BAD_ROUTING 0x201      /* num_tokens_post_padded exceeds the block capacity */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int b2m_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* b2m_last_error(void);
+
+/* Upper bound for every bounded device-side wait, in nanoseconds (default 2e9).
+ * Process-wide; applies to launches made after the call. */
+int b2m_set_timeout_ns(uint64_t ns);
+
+/* ---------------------------------------------------------------------------
+ * K1  1x128 group FP8 (e4m3) quantisation of bf16 activations.
+ * Replaces vLLM per_token_group_fp8_quant as called through
+ * moe_kernel_quantize_input (moe_bench/overlap/overlap_forward.py:427-429) and
+ * follows the repo oracle moe_bench/verify.py:108-117 exactly:
+ *   scale[r,g] = max(amax(|x[r, 128g : 128g+128]|) / 448, 1e-12)   (IEEE division)
+ *   q[r,c]     = e4m3_rne(clamp(x[r,c] / scale[r, c/128], -448, 448))
+ * x: bf16 [rows, cols] with row stride ldx (elements); q: e4m3 bytes, row stride
+ * ldq; scale: fp32 [rows, ceil(cols/128)] with row stride ld_scale.
+ * Ragged cols (not a multiple of 128) are handled as if zero padded. */
+int b2m_quant_g128(const void* x, int64_t rows, int64_t cols, int64_t ldx, void* q, int64_t ldq,
+                   float* scale, int64_t ld_scale, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * K2  moe_align_block_size.
+ * Replaces vllm.model_executor.layers.fused_moe.moe_align_block_size
+ * (called at moe_bench/overlap/overlap_forward.py:420-422; contract in vLLM
+ * moe_align_block_size.py:19-104).  topk_ids: int32 [numel] (flattened [T, k]).
+ * Outputs: sorted_token_ids [sorted_cap] (pairs of each expert in ascending flat
+ * index, each expert segment padded to a multiple of block_size with the pad id
+ * `numel`, tail also `numel`); expert_ids [expert_ids_cap] (expert of each block,
+ * remapped through expert_map when non-NULL, -1 for non-local experts and for the
+ * tail); num_tokens_post_padded [1].  Required capacities: sorted_cap >=
+ * numel + E*(block_size-1) (or numel*block_size when numel < E) and
+ * expert_ids_cap >= cdiv(sorted_cap, block_size).  num_experts <= 1024. */
+int b2m_align(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int32_t block_size,
+              const int32_t* expert_map, int32_t* sorted_token_ids, int64_t sorted_cap, int32_t* expert_ids,
+              int64_t expert_ids_cap, int32_t* num_tokens_post_padded, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Gate/up weight layout for K3.  The reference stores w1 as [E, 2I, H] with all
+ * gate rows before all up rows (moe_bench/schemes/runtime.py:154-159).  K3 wants,
+ * per expert, 128-row blocks interleaved gate0, up0, gate1, up1, ... so one
+ * 256-row tile holds matching gate and up rows; its block scales [E, 2I/128, H/128]
+ * are permuted the same way.  I (inter) must be a multiple of 128. */
+int b2m_w1_interleave(const void* w1, const float* w1_scale, int32_t num_experts, int32_t inter,
+                      int64_t hidden, void* w1_out, float* w1_scale_out, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * K3  gate/up grouped GEMM with fused SiLU*mul and 1x128 requant (tcgen05 + TMEM + TMA).
+ * Replaces invoke_moe_kernel_k_split/fused_moe_kernel_accumulate
+ * (moe_bench/overlap/kernels.py:36-214, :317-452) + torch.ops._C.silu_and_mul +
+ * the second moe_kernel_quantize_input (overlap_forward.py:530-561).
+ * For each 128-row block b of sorted_token_ids with expert e = expert_ids[b] >= 0,
+ * row p = sorted position, pair = sorted_token_ids[p], token = pair / top_k:
+ *   gu[p, n] = sum_kb (sum_k A[token,k] W1[e,n,k]) * a_scale[token,kb] * w1_scale[e,n/128,kb]
+ *   h[p, j]  = silu(gu[p, j]) * gu[p, I + j]                      (fp32)
+ *   out_q[p, j] / out_scale_t[j/128, p] = 1x128 e4m3 quant of h (rule of K1)
+ * Pad rows (pair >= numel) read zeros.  Blocks with expert -1 are skipped.
+ * a_fp8: e4m3 [a_rows, hidden] (row stride hidden); a_scale: fp32 [a_rows, hidden/128];
+ * w1: interleaved e4m3 [E, 2I, hidden]; w1_scale: interleaved fp32 [E, 2I/128, hidden/128];
+ * out_q: e4m3 [rows_cap, I]; out_scale_t: fp32 [I/128, rows_cap] (K-block major).
+ * hidden % 128 == 0, I % 128 == 0, rows_cap % 128 == 0 and rows_cap >= the
+ * sorted_token_ids capacity. */
+int b2m_gemm1(const void* a_fp8, const float* a_scale, int64_t a_rows, int64_t hidden, const void* w1,
+              const float* w1_scale, int32_t num_experts, int32_t inter, const int32_t* sorted_token_ids,
+              const int32_t* expert_ids, const int32_t* num_tokens_post_padded, int64_t rows_cap, int64_t numel,
+              int32_t top_k, void* out_q, float* out_scale_t, int32_t* dev_status, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * K4  down grouped GEMM with the routed top-k weight in the epilogue.
+ * Replaces invoke_moe_kernel_n_split -> vLLM fused_moe_kernel with
+ * MUL_ROUTED_WEIGHT=True (moe_bench/overlap/kernels.py:221-310,
+ * overlap_forward.py:564-579):
+ *   y[p, n] = w(pair) * sum_kb (sum_j Q[p,j] W2[e,n,j]) * a_scale_t[kb,p] * w2_scale[e,n/128,kb]
+ *   out[pair, n] = bf16(y[p, n])       for every non-pad row p of a block with expert e >= 0
+ * w(pair) = topk_weights[pair] (flat [T*k] fp32), or 1 when topk_weights is NULL.
+ * a_fp8 / a_scale_t: K3's out_q / out_scale_t; w2: e4m3 [E, hidden, I];
+ * w2_scale: fp32 [E, ceil(hidden/128), I/128]; out: bf16 [numel, hidden] indexed by pair.
+ * hidden % 128 == 0, I % 128 == 0. */
+int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int32_t inter, const void* w2,
+              const float* w2_scale, int32_t num_experts, int64_t hidden, const int32_t* sorted_token_ids,
+              const int32_t* expert_ids, const int32_t* num_tokens_post_padded, int64_t numel,
+              const float* topk_weights, void* out_bf16, int32_t* dev_status, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Top-k combine (+ shared expert add).
+ * Replaces the torch.sum over top-k and the shared add of
+ * moe_bench/overlap/overlap_forward.py:581-597:
+ *   out[t, :] = bf16( sum_j staged[t*k + j, :] + shared[t, :] )     (fp32 sum, j ascending)
+ * A slot j is skipped when expert_map is non-NULL and expert_map[topk_ids[t*k+j]] < 0.
+ * staged: bf16 [tokens*k, hidden]; shared: bf16 [tokens, hidden] or NULL;
+ * out: bf16 [tokens, ld_out]. */
+int b2m_combine(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, const int32_t* topk_ids,
+                const int32_t* expert_map, const void* shared, void* out, int64_t ld_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2M_H_ */

@@ -1,0 +1,158 @@
+// K2: moe_align_block_size — histogram, scan and deterministic scatter in one CTA.
+//
+// Contract: vLLM moe_align_block_size (moe_align_block_size.py:19-104), called by
+// the reference at moe_bench/overlap/overlap_forward.py:420-422.  Pairs of one
+// expert are emitted in ascending flat index, which makes the output unique.
+//
+// One CTA of 32 warps.  Warp w owns the contiguous pair range
+// [w*chunk, (w+1)*chunk).  Pass A: per-warp per-expert counts (warp_cnt[w][e]) from
+// __match_any_sync groups — no atomics, so the result does not depend on timing.
+// Scan: padded counts -> expert segment starts; per-(warp, expert) bases are the
+// segment start plus the counts of lower warps.  Pass C: each warp walks its range
+// again in order and places every pair at base + rank inside its match group.
+#include "b2m_common.cuh"
+#include "b2m_host.h"
+
+namespace b2m {
+namespace {
+
+constexpr int kAlignWarps = 32;
+constexpr int kAlignThreads = kAlignWarps * 32;
+constexpr int kMaxExperts = 1024;
+
+__global__ void __launch_bounds__(kAlignThreads, 1)
+    align_kernel(const int32_t* __restrict__ topk_ids, int64_t numel, int32_t num_experts, int32_t bs,
+                 const int32_t* __restrict__ expert_map, int32_t* __restrict__ sorted_ids, int64_t sorted_cap,
+                 int32_t* __restrict__ expert_ids, int64_t expert_ids_cap, int32_t* __restrict__ ntpp_out) {
+  extern __shared__ int32_t sm[];
+  int32_t* warp_cnt = sm;                                  // [32][E] counts, then bases
+  int32_t* counts = warp_cnt + kAlignWarps * num_experts;  // [E]
+  int32_t* starts = counts + num_experts;                  // [E]
+  __shared__ int32_t s_total;
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int64_t chunk = (numel + kAlignWarps - 1) / kAlignWarps;
+  const int64_t lo = warp * chunk;
+  const int64_t hi = lo + chunk < numel ? lo + chunk : numel;
+
+  for (int i = tid; i < kAlignWarps * num_experts; i += kAlignThreads) warp_cnt[i] = 0;
+  __syncthreads();
+
+  // Pass A: per-warp counts.
+  int32_t* my_cnt = warp_cnt + warp * num_experts;
+  for (int64_t i0 = lo; i0 < hi; i0 += 32) {
+    const int64_t i = i0 + lane;
+    int32_t e = i < hi ? __ldg(topk_ids + i) : -1;
+    if (e >= num_experts) e = -1;  // out-of-range ids take no slot
+    const uint32_t grp = __match_any_sync(0xffffffffu, e);
+    const int leader = __ffs(grp) - 1;
+    if (e >= 0 && lane == leader) my_cnt[e] += __popc(grp);
+    __syncwarp();
+  }
+  __syncthreads();
+
+  // Totals and padded sizes.
+  for (int e = tid; e < num_experts; e += kAlignThreads) {
+    int32_t c = 0;
+    for (int w = 0; w < kAlignWarps; ++w) c += warp_cnt[w * num_experts + e];
+    counts[e] = c;
+  }
+  __syncthreads();
+
+  // Exclusive scan of padded counts (warp 0, 32 experts per step).
+  if (warp == 0) {
+    int32_t carry = 0;
+    for (int e0 = 0; e0 < num_experts; e0 += 32) {
+      const int e = e0 + lane;
+      const int32_t c = e < num_experts ? counts[e] : 0;
+      const int32_t p = (c + bs - 1) / bs * bs;
+      int32_t incl = p;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int32_t v = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += v;
+      }
+      if (e < num_experts) starts[e] = carry + incl - p;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) s_total = carry;
+  }
+  __syncthreads();
+  const int32_t total = s_total;
+
+  // Per-(warp, expert) bases.
+  for (int e = tid; e < num_experts; e += kAlignThreads) {
+    int32_t run = starts[e];
+    for (int w = 0; w < kAlignWarps; ++w) {
+      const int32_t c = warp_cnt[w * num_experts + e];
+      warp_cnt[w * num_experts + e] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+
+  // Pass C: ordered scatter.
+  for (int64_t i0 = lo; i0 < hi; i0 += 32) {
+    const int64_t i = i0 + lane;
+    int32_t e = i < hi ? __ldg(topk_ids + i) : -1;
+    if (e >= num_experts) e = -1;
+    const uint32_t grp = __match_any_sync(0xffffffffu, e);
+    const int leader = __ffs(grp) - 1;
+    const int rank = __popc(grp & ((1u << lane) - 1u));
+    if (e >= 0) sorted_ids[my_cnt[e] + rank] = static_cast<int32_t>(i);
+    __syncwarp();
+    if (e >= 0 && lane == leader) my_cnt[e] += __popc(grp);
+    __syncwarp();
+  }
+
+  // Pads inside segments, block -> expert table.
+  const int32_t pad_id = static_cast<int32_t>(numel);
+  for (int e = tid; e < num_experts; e += kAlignThreads) {
+    const int32_t c = counts[e];
+    const int32_t st = starts[e];
+    const int32_t p = (c + bs - 1) / bs * bs;
+    for (int32_t s = st + c; s < st + p; ++s) sorted_ids[s] = pad_id;
+    const int32_t mapped = expert_map ? __ldg(expert_map + e) : e;
+    for (int32_t b = st / bs; b < (st + p) / bs; ++b) expert_ids[b] = mapped;
+  }
+  // Tails.
+  for (int64_t s = total + tid; s < sorted_cap; s += kAlignThreads) sorted_ids[s] = pad_id;
+  for (int64_t b = total / bs + tid; b < expert_ids_cap; b += kAlignThreads) expert_ids[b] = -1;
+  if (tid == 0) *ntpp_out = total;
+}
+
+}  // namespace
+}  // namespace b2m
+
+extern "C" int b2m_align(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int32_t block_size,
+                         const int32_t* expert_map, int32_t* sorted_token_ids, int64_t sorted_cap,
+                         int32_t* expert_ids, int64_t expert_ids_cap, int32_t* num_tokens_post_padded,
+                         void* stream) {
+  using namespace b2m;
+  B2M_TRY(require_sm100(nullptr));
+  if (num_experts <= 0 || num_experts > kMaxExperts)
+    return fail(B2M_ERR_ARG, "align: num_experts=%d outside [1, %d]", num_experts, kMaxExperts);
+  if (block_size <= 0 || numel < 0) return fail(B2M_ERR_ARG, "align: bad block_size/numel");
+  if (numel >= (int64_t(1) << 31) - int64_t(num_experts) * block_size)
+    return fail(B2M_ERR_ARG, "align: numel=%lld overflows int32 indices", (long long)numel);
+  int64_t need = numel + int64_t(num_experts) * (block_size - 1);
+  if (numel < num_experts && numel * block_size < need) need = numel * block_size;
+  if (sorted_cap < need)
+    return fail(B2M_ERR_ARG, "align: sorted_cap=%lld < required %lld", (long long)sorted_cap, (long long)need);
+  if (expert_ids_cap < (sorted_cap + block_size - 1) / block_size)
+    return fail(B2M_ERR_ARG, "align: expert_ids_cap=%lld < cdiv(sorted_cap, block_size)",
+                (long long)expert_ids_cap);
+  if (!sorted_token_ids || !expert_ids || !num_tokens_post_padded || (numel > 0 && !topk_ids))
+    return fail(B2M_ERR_ARG, "align: null pointer");
+  const size_t smem = (size_t(kAlignWarps) + 2) * num_experts * sizeof(int32_t);
+  if (smem > 48 * 1024)
+    B2M_TRY(check_cuda(
+        cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+        "align: cudaFuncSetAttribute"));
+  align_kernel<<<1, kAlignThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      topk_ids, numel, num_experts, block_size, expert_map, sorted_token_ids, sorted_cap, expert_ids,
+      expert_ids_cap, num_tokens_post_padded);
+  return check_cuda(cudaGetLastError(), "align launch");
+}

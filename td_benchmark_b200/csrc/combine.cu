@@ -1,0 +1,127 @@
+// Top-k combine (+ shared expert add) and the gate/up weight interleave used at set-up.
+#include "b2m_common.cuh"
+#include "b2m_host.h"
+
+namespace b2m {
+namespace {
+
+constexpr int kCombineThreads = 256;
+
+__device__ __forceinline__ void acc_bf16x8(const uint4& u, float (&a)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    a[2 * i] += __uint_as_float(w[i] << 16);
+    a[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float (&a)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a[2 * i], a[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// out[t, :] = bf16(sum_j staged[t*k + j, :] + shared[t, :]); one thread per 8 columns.
+__global__ void __launch_bounds__(kCombineThreads)
+    combine_kernel(const __nv_bfloat16* __restrict__ staged, int64_t tokens, int top_k, int64_t hidden,
+                   const int32_t* __restrict__ topk_ids, const int32_t* __restrict__ expert_map,
+                   const __nv_bfloat16* __restrict__ shared, __nv_bfloat16* __restrict__ out, int64_t ld_out) {
+  const int64_t vec_per_row = hidden / 8;
+  const int64_t total = tokens * vec_per_row;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * kCombineThreads + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * kCombineThreads) {
+    const int64_t t = v / vec_per_row;
+    const int64_t c = (v - t * vec_per_row) * 8;
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = 0; j < top_k; ++j) {
+      const int64_t pair = t * top_k + j;
+      if (expert_map && __ldg(expert_map + __ldg(topk_ids + pair)) < 0) continue;
+      acc_bf16x8(__ldg(reinterpret_cast<const uint4*>(staged + pair * hidden + c)), a);
+    }
+    if (shared) acc_bf16x8(__ldg(reinterpret_cast<const uint4*>(shared + t * hidden + c)), a);
+    *reinterpret_cast<uint4*>(out + t * ld_out + c) = pack_bf16x8(a);
+  }
+}
+
+// w1 [E, 2I, H] (gate rows then up rows) -> [E, 2I, H] with 128-row blocks ordered
+// gate0, up0, gate1, up1, ...; scales [E, 2I/128, KB] permuted the same way.
+__global__ void interleave_rows_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t experts,
+                                       int64_t inter, int64_t hidden) {
+  const int64_t vec_per_row = hidden / 16;
+  const int64_t rows = experts * 2 * inter;
+  const int64_t total = rows * vec_per_row;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t drow = v / vec_per_row;
+    const int64_t cv = v - drow * vec_per_row;
+    const int64_t e = drow / (2 * inter);
+    const int64_t r = drow - e * 2 * inter;  // destination row inside the expert
+    const int64_t blk = r / 128, within = r % 128;
+    const int64_t g = blk & 1, j = blk >> 1;
+    const int64_t srow = e * 2 * inter + g * inter + j * 128 + within;
+    reinterpret_cast<uint4*>(dst)[drow * vec_per_row + cv] =
+        __ldg(reinterpret_cast<const uint4*>(src) + srow * vec_per_row + cv);
+  }
+}
+
+__global__ void interleave_scales_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t experts,
+                                         int64_t nblk_half, int64_t kb) {
+  const int64_t total = experts * 2 * nblk_half * kb;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t k = i % kb;
+    const int64_t db = (i / kb) % (2 * nblk_half);
+    const int64_t e = i / (kb * 2 * nblk_half);
+    const int64_t g = db & 1, j = db >> 1;
+    dst[i] = src[(e * 2 * nblk_half + g * nblk_half + j) * kb + k];
+  }
+}
+
+}  // namespace
+}  // namespace b2m
+
+extern "C" int b2m_combine(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden,
+                           const int32_t* topk_ids, const int32_t* expert_map, const void* shared, void* out,
+                           int64_t ld_out, void* stream) {
+  using namespace b2m;
+  int num_sms = 0;
+  B2M_TRY(require_sm100(&num_sms));
+  if (tokens < 0 || top_k <= 0 || hidden <= 0) return fail(B2M_ERR_ARG, "combine: bad shape");
+  if (tokens == 0) return B2M_OK;
+  if (hidden % 8 || ld_out % 8 || ld_out < hidden)
+    return fail(B2M_ERR_ARG, "combine: hidden (%lld) and ld_out (%lld) must be multiples of 8", (long long)hidden,
+                (long long)ld_out);
+  if (!staged || !out || (expert_map && !topk_ids)) return fail(B2M_ERR_ARG, "combine: null pointer");
+  if (!aligned16(staged) || !aligned16(out) || (shared && !aligned16(shared)))
+    return fail(B2M_ERR_ARG, "combine: pointers must be 16-byte aligned");
+  const int64_t total = tokens * (hidden / 8);
+  int64_t blocks = (total + kCombineThreads - 1) / kCombineThreads;
+  if (blocks > int64_t(num_sms) * 8) blocks = int64_t(num_sms) * 8;
+  combine_kernel<<<static_cast<unsigned>(blocks), kCombineThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, topk_ids, expert_map,
+      static_cast<const __nv_bfloat16*>(shared), static_cast<__nv_bfloat16*>(out), ld_out);
+  return check_cuda(cudaGetLastError(), "combine launch");
+}
+
+extern "C" int b2m_w1_interleave(const void* w1, const float* w1_scale, int32_t num_experts, int32_t inter,
+                                 int64_t hidden, void* w1_out, float* w1_scale_out, void* stream) {
+  using namespace b2m;
+  int num_sms = 0;
+  B2M_TRY(require_sm100(&num_sms));
+  if (num_experts <= 0 || inter <= 0 || inter % 128 || hidden <= 0 || hidden % 128)
+    return fail(B2M_ERR_ARG, "w1_interleave: inter (%d) and hidden (%lld) must be positive multiples of 128", inter,
+                (long long)hidden);
+  if (!w1 || !w1_scale || !w1_out || !w1_scale_out) return fail(B2M_ERR_ARG, "w1_interleave: null pointer");
+  if (!aligned16(w1) || !aligned16(w1_out)) return fail(B2M_ERR_ARG, "w1_interleave: weights must be 16B aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  interleave_rows_kernel<<<num_sms * 8, 256, 0, s>>>(static_cast<const uint8_t*>(w1), static_cast<uint8_t*>(w1_out),
+                                                      num_experts, inter, hidden);
+  B2M_TRY(check_cuda(cudaGetLastError(), "interleave rows launch"));
+  interleave_scales_kernel<<<num_sms, 256, 0, s>>>(w1_scale, w1_scale_out, num_experts, inter / 128, hidden / 128);
+  return check_cuda(cudaGetLastError(), "interleave scales launch");
+}

@@ -1,0 +1,238 @@
+"""FP8 MoE FFN layer on the b2m kernels (per rank).
+
+``MoELayer`` owns the prepared weights and every buffer the forward needs, sized
+once for the layer's token count, so the timed forward allocates nothing.  The
+forward is the path of the reference's scheme b2
+(``moe_bench/overlap/overlap_forward.py:348-622``) and its unfused twins a1/a2
+(``moe_bench/schemes/vllm_tp.py:50-64``, ``vllm_ep.py:53-71``):
+
+    quant(x_local) -> [all-gather] -> align(topk_ids) -> GEMM1(+SiLU*mul+requant)
+      -> GEMM2(*w) -> combine over top-k (+shared) -> [reduce-scatter]
+
+The exchange steps are pluggable (``Exchange``): ``NullExchange`` for one GPU,
+``NcclExchange`` (torch.distributed all_gather_into_tensor / reduce_scatter_tensor,
+the unfused comparison scheme) and the peer-memory exchange in ``symm.py``.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+
+BM = 128
+
+
+@dataclass
+class ExpertWeights:
+    """One set of expert weights in the kernels' layouts."""
+    w1i: torch.Tensor        # e4m3 [E, 2I, H], 128-row interleaved gate/up
+    w1i_scale: torch.Tensor  # fp32 [E, 2I/128, H/128] (same interleave)
+    w2: torch.Tensor         # e4m3 [E, H, I]
+    w2_scale: torch.Tensor   # fp32 [E, H/128, I/128]
+
+    @property
+    def num_experts(self) -> int:
+        return self.w1i.shape[0]
+
+    @property
+    def inter(self) -> int:
+        return self.w1i.shape[1] // 2
+
+    @property
+    def hidden(self) -> int:
+        return self.w1i.shape[2]
+
+    @classmethod
+    def prepare(cls, w1: torch.Tensor, w1_scale: torch.Tensor, w2: torch.Tensor, w2_scale: torch.Tensor
+                ) -> "ExpertWeights":
+        """From the reference layouts (``moe_bench/schemes/runtime.py:27-104``): w1 [E, 2I, H] gate-then-up."""
+        w1 = w1.contiguous()
+        w1i, w1i_s = ops.w1_interleave(w1, w1_scale.float().contiguous())
+        return cls(w1i, w1i_s, w2.contiguous(), w2_scale.float().contiguous())
+
+
+class _Routing:
+    """Alignment buffers for one routing (sized for numel pairs)."""
+
+    def __init__(self, numel: int, num_experts: int, device):
+        self.numel = numel
+        self.cap, self.nblk = ops.align_sizes(numel, num_experts, BM)
+        self.rows_cap = self.nblk * BM
+        self.sorted_ids = torch.empty(self.cap, dtype=torch.int32, device=device)
+        self.expert_ids = torch.empty(self.nblk, dtype=torch.int32, device=device)
+        self.ntpp = torch.empty(1, dtype=torch.int32, device=device)
+
+
+class SharedExpert:
+    """Dense SwiGLU FFN on the same kernels (one expert, every token routed to it).
+
+    Mirrors ``moe_bench/schemes/shared_expert.py`` (StaticSharedExpert): the
+    alignment (identity order) and all buffers are built once; a call takes the
+    already-quantised input (``shared_expert.py:91-102``) and returns bf16 [rows, H].
+    """
+
+    def __init__(self, weights: ExpertWeights, rows: int, device):
+        self.w = weights
+        self.rows = rows
+        self.route = _Routing(rows, 1, device)
+        nb = (rows + BM - 1) // BM
+        ids = torch.full((self.route.cap,), rows, dtype=torch.int32)
+        ids[:rows] = torch.arange(rows, dtype=torch.int32)
+        self.route.sorted_ids.copy_(ids)
+        eids = torch.full((self.route.nblk,), -1, dtype=torch.int32)
+        eids[:nb] = 0
+        self.route.expert_ids.copy_(eids)
+        self.route.ntpp.fill_(nb * BM)
+        self.inter_q = torch.empty((self.route.rows_cap, weights.inter), dtype=ops.FP8, device=device)
+        self.inter_st = torch.empty((weights.inter // 128, self.route.rows_cap), dtype=torch.float32, device=device)
+        self.out = torch.empty((rows, weights.hidden), dtype=torch.bfloat16, device=device)
+
+    def __call__(self, xq: torch.Tensor, xs: torch.Tensor, status: torch.Tensor | None) -> torch.Tensor:
+        r = self.route
+        ops.gemm1(xq, xs, self.w.w1i, self.w.w1i_scale, r.sorted_ids, r.expert_ids, r.ntpp, r.numel, 1, r.rows_cap,
+                  self.inter_q, self.inter_st, status)
+        ops.gemm2(self.inter_q, self.inter_st, self.w.w2, self.w.w2_scale, r.sorted_ids, r.expert_ids, r.ntpp,
+                  r.numel, None, self.out, status)
+        return self.out
+
+
+class NullExchange:
+    """One rank: the gathered tokens are the local tokens, the partial is the output."""
+    world_size = 1
+    rank = 0
+
+    def all_gather(self, xq_local, xs_local, xq_full, xs_full):  # pragma: no cover - trivial
+        raise AssertionError("single-rank layer gathers nothing")
+
+    def reduce_scatter(self, partial, out_local):  # pragma: no cover - trivial
+        raise AssertionError("single-rank layer scatters nothing")
+
+
+class NcclExchange:
+    """Unfused comparison: NCCL all-gather of FP8 bytes + fp32 scales, NCCL bf16 reduce-scatter.
+
+    Same collectives as the reference's b2 (``overlap_forward.py:494-505``, ``:603-608``),
+    issued as one call each instead of per chunk.
+    """
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.world_size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def all_gather(self, xq_local, xs_local, xq_full, xs_full):
+        self.dist.all_gather_into_tensor(xq_full.view(torch.uint8), xq_local.view(torch.uint8), group=self.group)
+        self.dist.all_gather_into_tensor(xs_full, xs_local, group=self.group)
+
+    def reduce_scatter(self, partial, out_local):
+        self.dist.reduce_scatter_tensor(out_local, partial, group=self.group)
+
+
+class MoELayer:
+    """Per-rank FP8 MoE layer.
+
+    ``tokens``: gathered token count T (= world_size * local tokens); ``top_k``;
+    ``weights``: this rank's expert weights (TP: I/P columns of every expert; EP:
+    the local experts); ``expert_map``: int32 [E_global] global->local id (-1 when
+    not local) for EP, None for TP; ``shared``: shared-expert weights, applied on
+    the gathered tokens before the reduce-scatter (TP, ``overlap_forward.py:513-525``)
+    or on the local tokens after it (EP, ``vllm_ep.py:67-69``).
+    """
+
+    def __init__(self, weights: ExpertWeights, tokens: int, top_k: int, global_num_experts: int,
+                 expert_map: torch.Tensor | None = None, shared: ExpertWeights | None = None,
+                 exchange=None, device=None):
+        self.w = weights
+        self.exchange = exchange or NullExchange()
+        self.P = self.exchange.world_size
+        if tokens % self.P:
+            raise ValueError(f"tokens={tokens} must be divisible by world_size={self.P}")
+        self.T = tokens
+        self.T_local = tokens // self.P
+        self.top_k = top_k
+        self.E = global_num_experts
+        self.H = weights.hidden
+        self.device = torch.device(device) if device is not None else weights.w1i.device
+        self.expert_map = expert_map
+        self.ep = expert_map is not None
+        dev = self.device
+        self.numel = tokens * top_k
+        self.route = _Routing(self.numel, global_num_experts, dev)
+        H = self.H
+        self.xq = torch.empty((tokens, H), dtype=ops.FP8, device=dev)
+        self.xs = torch.empty((tokens, H // 128), dtype=torch.float32, device=dev)
+        self.inter_q = torch.empty((self.route.rows_cap, weights.inter), dtype=ops.FP8, device=dev)
+        self.inter_st = torch.empty((weights.inter // 128, self.route.rows_cap), dtype=torch.float32, device=dev)
+        self.staged = torch.empty((self.numel, H), dtype=torch.bfloat16, device=dev)
+        self.partial = torch.empty((tokens, H), dtype=torch.bfloat16, device=dev)
+        self.out_local = torch.empty((self.T_local, H), dtype=torch.bfloat16, device=dev)
+        self.status = ops.new_status(dev)
+        self.events: list | None = None   # set to [] to record (name, cuda.Event) around the GEMMs
+        self.shared = None
+        self.shared_local = None
+        if shared is not None:
+            rows = self.T_local if self.ep else tokens
+            self.shared = SharedExpert(shared, rows, dev)
+
+    # -- stages (exposed for tests and staged timing)
+    def quant_and_gather(self, x_local: torch.Tensor) -> None:
+        if self.P == 1:
+            ops.quant_g128(x_local, self.xq, self.xs)
+            return
+        r0 = self.exchange.rank * self.T_local
+        xq_l = self.xq[r0:r0 + self.T_local]
+        xs_l = self.xs[r0:r0 + self.T_local]
+        ops.quant_g128(x_local, xq_l, xs_l)
+        self.exchange.all_gather(xq_l, xs_l, self.xq, self.xs)
+
+    def _event(self, name: str) -> None:
+        if self.events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(torch.cuda.current_stream(self.device))
+            self.events.append((name, ev))
+
+    def experts(self, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> None:
+        r = self.route
+        ops.moe_align_block_size(topk_ids, BM, self.E, self.expert_map, out=(r.sorted_ids, r.expert_ids, r.ntpp))
+        self._event("gemm1_start")
+        ops.gemm1(self.xq, self.xs, self.w.w1i, self.w.w1i_scale, r.sorted_ids, r.expert_ids, r.ntpp, self.numel,
+                  self.top_k, r.rows_cap, self.inter_q, self.inter_st, self.status)
+        self._event("gemm1_end")
+        ops.gemm2(self.inter_q, self.inter_st, self.w.w2, self.w.w2_scale, r.sorted_ids, r.expert_ids, r.ntpp,
+                  self.numel, topk_weights.reshape(-1), self.staged, self.status)
+        self._event("gemm2_end")
+
+    def kernel_launches(self) -> int:
+        """b2m kernels one forward launches (quant, align, GEMM1, GEMM2, combine, shared expert)."""
+        n = 5
+        if self.shared is not None:
+            n += 2 + (1 if self.ep else 0)
+        return n
+
+    def forward(self, x_local: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
+        """x_local bf16 [T/P, H]; topk_ids int32 / topk_weights fp32 [T, k] (all tokens) -> bf16 [T/P, H]."""
+        self.quant_and_gather(x_local)
+        self.experts(topk_ids, topk_weights)
+        shared_out = None
+        if self.shared is not None and not self.ep:
+            shared_out = self.shared(self.xq, self.xs, self.status)
+        ids = topk_ids if self.ep else None
+        if self.P == 1 and not (self.ep and self.shared is not None):
+            return ops.combine(self.staged, self.top_k, ids, self.expert_map, shared_out, self.out_local)
+        ops.combine(self.staged, self.top_k, ids, self.expert_map, shared_out, self.partial)
+        if self.P == 1:
+            self.out_local.copy_(self.partial)
+        else:
+            self.exchange.reduce_scatter(self.partial, self.out_local)
+        if self.shared is not None and self.ep:
+            r0 = self.exchange.rank * self.T_local
+            sh = self.shared(self.xq[r0:r0 + self.T_local], self.xs[r0:r0 + self.T_local], self.status)
+            ops.combine(self.out_local, 1, None, None, sh, self.out_local)
+        return self.out_local
+
+    def check(self) -> None:
+        ops.check_status(self.status, "MoELayer")

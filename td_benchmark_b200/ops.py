@@ -1,0 +1,170 @@
+"""torch-tensor wrappers over the b2m C ABI.
+
+Each wrapper checks shapes/dtypes/devices, then enqueues the kernel on the
+current CUDA stream of the tensors' device.  Outputs may be passed in (the layer
+pre-allocates everything once); when omitted they are allocated here.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+FP8 = torch.float8_e4m3fn
+BLOCK = 128
+
+STATUS_NAMES = {
+    0x101: "TIMEOUT_PRODUCER", 0x102: "TIMEOUT_MMA", 0x103: "TIMEOUT_EPILOGUE", 0x104: "TIMEOUT_PEER",
+    0x105: "TIMEOUT_DRAIN", 0x201: "BAD_ROUTING",
+}
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _cuda(t: torch.Tensor, name: str) -> None:
+    _need(t.is_cuda, f"{name} must be a CUDA tensor")
+
+
+def new_status(device) -> torch.Tensor:
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+def check_status(status: torch.Tensor, what: str = "b2m kernel") -> None:
+    """Synchronise on the status word and raise if a kernel recorded an error."""
+    code = int(status.item())
+    if code:
+        status.zero_()
+        raise RuntimeError(f"{what}: device status 0x{code:x} ({STATUS_NAMES.get(code, 'unknown')})")
+
+
+def quant_g128(x: torch.Tensor, q: torch.Tensor | None = None, scale: torch.Tensor | None = None
+               ) -> tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [rows, cols] -> (e4m3 [rows, cols], fp32 [rows, ceil(cols/128)])."""
+    _cuda(x, "x")
+    _need(x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1, "x must be 2D bf16 with unit column stride")
+    rows, cols = x.shape
+    groups = (cols + BLOCK - 1) // BLOCK
+    if q is None:
+        q = torch.empty((rows, cols), dtype=FP8, device=x.device)
+    if scale is None:
+        scale = torch.empty((rows, groups), dtype=torch.float32, device=x.device)
+    _need(q.shape == (rows, cols) and q.stride(1) == 1 and q.element_size() == 1, "bad q buffer")
+    _need(scale.shape[0] == rows and scale.shape[1] >= groups and scale.stride(1) == 1 and
+          scale.dtype == torch.float32, "bad scale buffer")
+    _lib.call("b2m_quant_g128", x.data_ptr(), rows, cols, x.stride(0), q.data_ptr(), q.stride(0),
+              scale.data_ptr(), scale.stride(0), _stream(x.device))
+    return q, scale
+
+
+def align_sizes(numel: int, num_experts: int, block_size: int) -> tuple[int, int]:
+    """Buffer sizes of moe_align_block_size (vLLM moe_align_block_size.py:74-88)."""
+    max_padded = numel + num_experts * (block_size - 1)
+    if numel < num_experts:
+        max_padded = min(numel * block_size, max_padded)
+    return max_padded, (max_padded + block_size - 1) // block_size
+
+
+def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int,
+                         expert_map: torch.Tensor | None = None,
+                         out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None
+                         ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Same signature and outputs as vLLM's ``moe_align_block_size`` (without the padding flags)."""
+    _cuda(topk_ids, "topk_ids")
+    _need(topk_ids.dtype == torch.int32 and topk_ids.is_contiguous(), "topk_ids must be contiguous int32")
+    numel = topk_ids.numel()
+    cap, nblk = align_sizes(numel, num_experts, block_size)
+    if out is None:
+        sorted_ids = torch.empty(cap, dtype=torch.int32, device=topk_ids.device)
+        expert_ids = torch.empty(nblk, dtype=torch.int32, device=topk_ids.device)
+        ntpp = torch.empty(1, dtype=torch.int32, device=topk_ids.device)
+    else:
+        sorted_ids, expert_ids, ntpp = out
+    if expert_map is not None:
+        _need(expert_map.dtype == torch.int32 and expert_map.numel() >= num_experts, "expert_map must be int32 [E]")
+    _lib.call("b2m_align", topk_ids.data_ptr(), numel, num_experts, block_size, _ptr(expert_map),
+              sorted_ids.data_ptr(), sorted_ids.numel(), expert_ids.data_ptr(), expert_ids.numel(),
+              ntpp.data_ptr(), _stream(topk_ids.device))
+    return sorted_ids, expert_ids, ntpp
+
+
+def w1_interleave(w1: torch.Tensor, w1_scale: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """[E, 2I, H] gate-then-up -> 128-row interleaved gate/up layout (+ scales)."""
+    _cuda(w1, "w1")
+    e, n2, h = w1.shape
+    _need(n2 % 256 == 0 and h % 128 == 0 and w1.is_contiguous() and w1_scale.is_contiguous(),
+          "w1 must be contiguous [E, 2I, H] with I % 128 == 0 and H % 128 == 0")
+    _need(tuple(w1_scale.shape) == (e, n2 // 128, h // 128), "w1_scale must be [E, 2I/128, H/128]")
+    out = torch.empty_like(w1)
+    out_s = torch.empty_like(w1_scale)
+    _lib.call("b2m_w1_interleave", w1.data_ptr(), w1_scale.data_ptr(), e, n2 // 2, h, out.data_ptr(),
+              out_s.data_ptr(), _stream(w1.device))
+    return out, out_s
+
+
+def gemm1(a_q: torch.Tensor, a_scale: torch.Tensor, w1i: torch.Tensor, w1i_scale: torch.Tensor,
+          sorted_ids: torch.Tensor, expert_ids: torch.Tensor, ntpp: torch.Tensor, numel: int, top_k: int,
+          rows_cap: int, out_q: torch.Tensor | None = None, out_scale_t: torch.Tensor | None = None,
+          status: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gate/up grouped GEMM + SiLU*mul + 1x128 requant.  Returns (q [rows_cap, I], scale_t [I/128, rows_cap])."""
+    _cuda(a_q, "a_q")
+    a_rows, hidden = a_q.shape
+    e, n2, h2 = w1i.shape
+    inter = n2 // 2
+    _need(h2 == hidden and a_q.is_contiguous() and w1i.is_contiguous(), "A / W1 shape mismatch")
+    _need(a_scale.is_contiguous() and tuple(a_scale.shape) == (a_rows, hidden // 128), "a_scale must be [rows, H/128]")
+    _need(expert_ids.numel() * 128 >= rows_cap, "expert_ids shorter than rows_cap/128")
+    if out_q is None:
+        out_q = torch.empty((rows_cap, inter), dtype=FP8, device=a_q.device)
+    if out_scale_t is None:
+        out_scale_t = torch.empty((inter // 128, rows_cap), dtype=torch.float32, device=a_q.device)
+    _lib.call("b2m_gemm1", a_q.data_ptr(), a_scale.data_ptr(), a_rows, hidden, w1i.data_ptr(), w1i_scale.data_ptr(),
+              e, inter, sorted_ids.data_ptr(), expert_ids.data_ptr(), ntpp.data_ptr(), rows_cap, numel, top_k,
+              out_q.data_ptr(), out_scale_t.data_ptr(), _ptr(status), _stream(a_q.device))
+    return out_q, out_scale_t
+
+
+def gemm2(a_q: torch.Tensor, a_scale_t: torch.Tensor, w2: torch.Tensor, w2_scale: torch.Tensor,
+          sorted_ids: torch.Tensor, expert_ids: torch.Tensor, ntpp: torch.Tensor, numel: int,
+          topk_weights: torch.Tensor | None, out: torch.Tensor | None = None,
+          status: torch.Tensor | None = None) -> torch.Tensor:
+    """Down grouped GEMM, routed weight in the epilogue.  Returns bf16 [numel, H] indexed by flat pair."""
+    _cuda(a_q, "a_q")
+    rows_cap, inter = a_q.shape
+    e, hidden, i2 = w2.shape
+    _need(i2 == inter and w2.is_contiguous() and a_q.is_contiguous(), "A / W2 shape mismatch")
+    _need(tuple(a_scale_t.shape) == (inter // 128, rows_cap), "a_scale_t must be [I/128, rows_cap]")
+    if topk_weights is not None:
+        _need(topk_weights.dtype == torch.float32 and topk_weights.is_contiguous() and
+              topk_weights.numel() == numel, "topk_weights must be contiguous fp32 with numel entries")
+    if out is None:
+        out = torch.empty((numel, hidden), dtype=torch.bfloat16, device=a_q.device)
+    _lib.call("b2m_gemm2", a_q.data_ptr(), a_scale_t.data_ptr(), rows_cap, inter, w2.data_ptr(), w2_scale.data_ptr(),
+              e, hidden, sorted_ids.data_ptr(), expert_ids.data_ptr(), ntpp.data_ptr(), numel, _ptr(topk_weights),
+              out.data_ptr(), _ptr(status), _stream(a_q.device))
+    return out
+
+
+def combine(staged: torch.Tensor, top_k: int, topk_ids: torch.Tensor | None = None,
+            expert_map: torch.Tensor | None = None, shared: torch.Tensor | None = None,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 [T*k, H] -> bf16 [T, H]: fp32 sum over the k slots (+ shared), one rounding."""
+    _cuda(staged, "staged")
+    pairs, hidden = staged.shape
+    tokens = pairs // top_k
+    if out is None:
+        out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=staged.device)
+    _need(out.shape[0] >= tokens and out.stride(1) == 1, "bad combine output")
+    _lib.call("b2m_combine", staged.data_ptr(), tokens, top_k, hidden, _ptr(topk_ids), _ptr(expert_map),
+              _ptr(shared), out.data_ptr(), out.stride(0), _stream(staged.device))
+    return out

@@ -1,0 +1,102 @@
+"""B200 schemes: FP8 MoE layer on the b2m kernels behind the reference's builder contract.
+
+``build(cfg, ctx, data, scheme_cfg) -> SchemeInstance`` does all set-up — shard
+views (``moe_bench/schemes/runtime.py:27-104``), gate/up interleave, buffers,
+exchange — so the timed ``run()`` is only the forward (the reference learned this
+the hard way, ``docs/exp/EXP-024-cgroup-perf-rootcause.md:6-9``).  ``run()`` reads
+the precomputed full routing (``runtime.py:19-24``) and never the gate weight,
+returns bf16 [M/P, K] on ``ctx.device`` ordered on the caller's current stream.
+
+Codes:
+  d1  TP, NCCL all-gather (FP8 bytes + scales) -> b2m kernels -> NCCL reduce-scatter (bf16)
+  d2  EP, same exchange, local experts only (expert_map), shared expert on local tokens
+The NCCL schemes are the unfused comparison for the fused peer-memory schemes.
+"""
+from __future__ import annotations
+
+from typing import Any
+
+from .base import SchemeInstance, SchemeSpec, TunableSpec, make_lazy_instance, validate_tunables
+
+B200_TUNABLES = {
+    "check_status": TunableSpec(bool, False, "synchronise after every run() and raise on a device status code"),
+}
+
+
+def _spec(code: str, name: str, parallel: str, comm: str) -> SchemeSpec:
+    return SchemeSpec(code=code, name=name, family="b200", parallel=parallel, comm=comm, weight_dtype="fp8",
+                      act_quant="group128", requires_nvshmem=False, tunables_schema=dict(B200_TUNABLES))
+
+
+SPEC_D1 = _spec("d1", "B200-TP-NCCL", "TP", "quantize -> NCCL AG(fp8+scale) -> b2m GEMM1/GEMM2 -> NCCL RS(bf16)")
+SPEC_D2 = _spec("d2", "B200-EP-NCCL", "EP", "quantize -> NCCL AG(fp8+scale) -> b2m GEMMs(local experts) -> NCCL RS -> +shared")
+
+
+def require_data(data: Any) -> Any:
+    if data is None:
+        raise RuntimeError("Scheme execution requires a DataBundle; build-only tests may pass data=None.")
+    return data
+
+
+def build_layer(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, exchange: Any = None):
+    """Shard views + prepared weights + MoELayer for this rank."""
+    import torch
+
+    from ..layer import ExpertWeights, MoELayer, NcclExchange
+    from ..weights import ep_views, tp_views
+
+    bundle = require_data(data)
+    ckpt = bundle.ckpt
+    device = torch.device(ctx.device)
+    s = cfg.shape
+    T = s.M_aligned(ctx.world_size)
+    args = (ckpt.w1.fp8.to(device), ckpt.w1.scale.to(device), ckpt.w2.fp8.to(device), ckpt.w2.scale.to(device),
+            ctx.rank, ctx.world_size)
+    views = tp_views(*args) if spec.parallel == "TP" else ep_views(*args)
+    weights = ExpertWeights.prepare(views["w1"], views["w1_scale"], views["w2"], views["w2_scale"])
+    shared = None
+    if ckpt.shared_w1 is not None and ckpt.shared_w2 is not None:
+        sargs = (ckpt.shared_w1.fp8.to(device), ckpt.shared_w1.scale.to(device), ckpt.shared_w2.fp8.to(device),
+                 ckpt.shared_w2.scale.to(device))
+        sv = tp_views(*sargs, ctx.rank, ctx.world_size) if spec.parallel == "TP" else tp_views(*sargs, 0, 1)
+        shared = ExpertWeights.prepare(sv["w1"], sv["w1_scale"], sv["w2"], sv["w2_scale"])
+    if exchange is None and ctx.world_size > 1:
+        exchange = NcclExchange(ctx.group)
+    expert_map = views.get("expert_map")
+    layer = MoELayer(weights, T, s.top_k, s.E, expert_map=expert_map, shared=shared, exchange=exchange,
+                     device=device)
+    return layer, views["shard_level"]
+
+
+def build_instance(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, scheme_cfg: Any) -> SchemeInstance:
+    import torch
+
+    tunables = validate_tunables(spec, scheme_cfg.tunables)
+    bundle = require_data(data)
+    layer, level = build_layer(spec, cfg, ctx, bundle)
+    device = layer.device
+    topk_ids = bundle.routing.topk_ids_full.to(device=device, dtype=torch.int32).contiguous()
+    topk_weights = bundle.routing.topk_weights_full.to(device=device, dtype=torch.float32).contiguous()
+    x = bundle.hidden_local.to(device=device, dtype=torch.bfloat16).contiguous()
+    check = tunables["check_status"]
+
+    def run() -> Any:
+        out = layer.forward(x, topk_ids, topk_weights)
+        if check:
+            layer.check()
+        return out
+
+    def close() -> None:
+        layer.check()
+
+    diag = {"shard_level": level, "tokens": layer.T, "rows_cap": layer.route.rows_cap,
+            "experts_local": layer.w.num_experts, "inter_local": layer.w.inter}
+    return make_lazy_instance(spec, tunables, run, diagnostics=diag, close_impl=close)
+
+
+def build_d1(cfg: Any, ctx: Any, data: Any, scheme_cfg: Any) -> SchemeInstance:
+    return build_instance(SPEC_D1, cfg, ctx, data, scheme_cfg)
+
+
+def build_d2(cfg: Any, ctx: Any, data: Any, scheme_cfg: Any) -> SchemeInstance:
+    return build_instance(SPEC_D2, cfg, ctx, data, scheme_cfg)

@@ -1,0 +1,213 @@
+"""Kernel parity on a B200: CUDA path through the C ABI vs the CPU oracle."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import align as oalign
+from oracle import fp8 as ofp8
+from oracle import quant as oquant
+
+pytestmark = pytest.mark.gpu
+
+from tests.conftest import cuda_ok  # noqa: E402
+
+if not cuda_ok():
+    pytest.skip("needs an sm_100 GPU", allow_module_level=True)
+
+from td_benchmark_b200 import ops, weights  # noqa: E402
+
+DEV = torch.device("cuda", 0)
+
+
+def _bf16(shape, seed, scale=1.0):
+    return (torch.randn(shape, generator=torch.Generator().manual_seed(seed)) * scale).to(torch.bfloat16)
+
+
+# ---------------------------------------------------------------- K1 quant
+@pytest.mark.parametrize("rows,cols", [(1, 128), (7, 256), (512, 4096), (1024, 7168), (3, 129), (5, 300),
+                                       (33, 2048), (0, 256), (2, 384)])
+def test_quant_bit_exact(rows, cols):
+    x = _bf16((rows, cols), rows * 1000 + cols, 3.0)
+    if rows > 2:
+        x[1, :128] = 0                     # all-zero group -> scale 1e-12
+        x[2, 5] = 3.0e4                    # one huge value in a group
+    q, s = ops.quant_g128(x.to(DEV))
+    torch.cuda.synchronize()
+    qr, sr = oquant.quant_g128(x.float().numpy())
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy(), qr)
+    assert np.array_equal(s.cpu().numpy(), sr)
+
+
+def test_quant_strided_rows_and_offset_output():
+    big = _bf16((64, 1024), 5)
+    x = big[:, 256:768]                    # row stride 1024
+    q = torch.zeros((64, 640), dtype=torch.uint8, device=DEV)
+    s = torch.zeros((64, 8), dtype=torch.float32, device=DEV)
+    xd = big.to(DEV)[:, 256:768]
+    ops.quant_g128(xd, q[:, 64:576].view(torch.float8_e4m3fn), s[:, 2:6])
+    qr, sr = oquant.quant_g128(x.float().numpy())
+    assert np.array_equal(q[:, 64:576].cpu().numpy(), qr)
+    assert np.array_equal(s[:, 2:6].cpu().numpy(), sr)
+    assert q[:, :64].abs().sum() == 0 and s[:, :2].abs().sum() == 0
+
+
+# ---------------------------------------------------------------- K2 align
+def _ids(T, k, E, seed, zipf=False):
+    g = torch.Generator().manual_seed(seed)
+    logits = torch.randn((T, E), generator=g)
+    if zipf:
+        logits += 2.0 * torch.log(torch.arange(1, E + 1, dtype=torch.float32) ** -1.2)
+    return torch.topk(logits, k, dim=-1).indices.to(torch.int32).contiguous()
+
+
+@pytest.mark.parametrize("T,k,E,bs,zipf", [(64, 2, 8, 128, False), (4096, 2, 8, 128, False),
+                                           (8192, 8, 256, 128, True), (32, 8, 128, 128, False),
+                                           (3, 2, 64, 128, False), (1, 1, 8, 16, False), (1000, 4, 33, 64, True),
+                                           (32768, 8, 256, 128, True), (0, 2, 8, 128, False)])
+def test_align_bit_exact(T, k, E, bs, zipf):
+    ids = _ids(T, k, E, T + E, zipf) if T else torch.zeros((0, k), dtype=torch.int32)
+    s, e, n = ops.moe_align_block_size(ids.to(DEV), bs, E)
+    sr, er, nr = oalign.moe_align_block_size(ids.numpy(), bs, E)
+    assert int(n.item()) == int(nr[0])
+    assert np.array_equal(s.cpu().numpy(), sr)
+    assert np.array_equal(e.cpu().numpy(), er)
+
+
+def test_align_expert_map():
+    E, P, r = 256, 8, 3
+    ids = _ids(2048, 8, E, 11, zipf=True)
+    emap = torch.full((E,), -1, dtype=torch.int32)
+    emap[r * 32:(r + 1) * 32] = torch.arange(32, dtype=torch.int32)
+    s, e, n = ops.moe_align_block_size(ids.to(DEV), 128, E, emap.to(DEV))
+    sr, er, nr = oalign.moe_align_block_size(ids.numpy(), 128, E, emap.numpy())
+    assert int(n.item()) == int(nr[0]) and np.array_equal(s.cpu().numpy(), sr) and np.array_equal(e.cpu().numpy(), er)
+
+
+def test_align_rejects_small_buffers():
+    from td_benchmark_b200._lib import B2MError
+    ids = _ids(64, 2, 8, 1).to(DEV)
+    with pytest.raises(B2MError, match="sorted_cap"):
+        ops.moe_align_block_size(ids, 128, 8, out=(torch.empty(10, dtype=torch.int32, device=DEV),
+                                                   torch.empty(10, dtype=torch.int32, device=DEV),
+                                                   torch.empty(1, dtype=torch.int32, device=DEV)))
+
+
+# ---------------------------------------------------------------- weight interleave
+def test_w1_interleave():
+    E, I, H = 3, 384, 256
+    w = torch.randn((E, 2 * I, H), generator=torch.Generator().manual_seed(2)) * 0.02
+    q, s = weights.quantize_block128(w)
+    qi, si = ops.w1_interleave(q.to(DEV), s.to(DEV))
+    qb = q.view(torch.uint8)
+    exp = torch.cat([torch.cat([qb[:, j * 128:(j + 1) * 128], qb[:, I + j * 128:I + (j + 1) * 128]], 1)
+                     for j in range(I // 128)], 1)
+    exp_s = torch.cat([torch.cat([s[:, j:j + 1], s[:, I // 128 + j:I // 128 + j + 1]], 1) for j in range(I // 128)], 1)
+    assert torch.equal(qi.view(torch.uint8).cpu(), exp)
+    assert torch.equal(si.cpu(), exp_s)
+
+
+# ---------------------------------------------------------------- K3 / K4 GEMMs
+def _gemm_problem(T, H, I, E, k, seed, zipf=False):
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn((T, H), generator=g)).to(torch.bfloat16)
+    w1 = torch.randn((E, 2 * I, H), generator=g) * 0.02
+    w2 = torch.randn((E, H, I), generator=g) * 0.02
+    w1q, w1s = weights.quantize_block128(w1)
+    w2q, w2s = weights.quantize_block128(w2)
+    ids = _ids(T, k, E, seed + 1, zipf)
+    wts = torch.rand((T, k), generator=g).float()
+    wts = wts / wts.sum(-1, keepdim=True)
+    return x, w1q, w1s, w2q, w2s, ids, wts
+
+
+def _deq_rows(codes_u8, scales):
+    return ofp8.decode_e4m3(codes_u8).astype(np.float64) * np.repeat(scales, 128, axis=-1)[..., :codes_u8.shape[-1]]
+
+
+def _deq_w(q, s):
+    qn = ofp8.decode_e4m3(q.view(torch.uint8).numpy()).astype(np.float64)
+    sn = np.repeat(np.repeat(s.numpy().astype(np.float64), 128, 1), 128, 2)
+    return qn * sn
+
+
+@pytest.mark.parametrize("T,H,I,E,k,zipf", [(200, 512, 256, 4, 2, False), (64, 256, 512, 8, 2, False),
+                                            (300, 1024, 384, 16, 4, True), (5, 256, 128, 8, 2, False)])
+def test_gemm1_gemm2_against_float64(T, H, I, E, k, zipf):
+    x, w1q, w1s, w2q, w2s, ids, wts = _gemm_problem(T, H, I, E, k, T + H, zipf)
+    xq, xs = ops.quant_g128(x.to(DEV))
+    w1i, w1is = ops.w1_interleave(w1q.to(DEV), w1s.to(DEV))
+    sorted_ids, eids, ntpp = ops.moe_align_block_size(ids.to(DEV), 128, E)
+    rows_cap = eids.numel() * 128
+    status = ops.new_status(DEV)
+    hq, hst = ops.gemm1(xq, xs, w1i, w1is, sorted_ids, eids, ntpp, T * k, k, rows_cap, status=status)
+    staged = ops.gemm2(hq, hst, w2q.to(DEV), w2s.to(DEV), sorted_ids, eids, ntpp, T * k, wts.reshape(-1).to(DEV),
+                       status=status)
+    torch.cuda.synchronize()
+    ops.check_status(status)
+    n = int(ntpp.item())
+    srt = sorted_ids.cpu().numpy()[:n]
+    valid = srt < T * k
+    # float64 reference of GEMM1 + silu*mul on the same quantised activations
+    a = _deq_rows(xq.view(torch.uint8).cpu().numpy(), xs.cpu().numpy())           # [T, H]
+    W1 = _deq_w(w1q, w1s)
+    W2 = _deq_w(w2q, w2s)
+    eid_rows = np.repeat(eids.cpu().numpy()[:n // 128], 128)
+    rows = np.nonzero(valid)[0]
+    toks = srt[rows] // k
+    gu = np.einsum("rh,rnh->rn", a[toks], W1[eid_rows[rows]])
+    h = gu[:, :I] / (1 + np.exp(-gu[:, :I])) * gu[:, I:]
+    hq_np = hq.view(torch.uint8).cpu().numpy()[rows]
+    hs_np = hst.cpu().numpy()[:, rows].T
+    h_gpu = _deq_rows(hq_np, hs_np)
+    # scales: amax/448 of nearly the same values
+    sref = np.maximum(np.abs(h).reshape(len(rows), I // 128, 128).max(-1) / 448.0, 1e-12)
+    np.testing.assert_allclose(hs_np, sref, rtol=1e-4)
+    # codes: within one e4m3 step of the float64 value (quantisation + fp32 accumulation)
+    step = np.repeat(hs_np, 128, axis=1) * np.maximum(2.0 ** (np.floor(np.log2(np.maximum(np.abs(h) / np.repeat(hs_np, 128, axis=1), 2.0 ** -6))) - 3), 2.0 ** -9)
+    assert np.all(np.abs(h_gpu - h) <= step * 1.01 + 1e-30)
+    # pad rows of a valid block are zero codes
+    pad_rows = np.nonzero(~valid)[0]
+    if pad_rows.size:
+        assert hq.view(torch.uint8).cpu().numpy()[pad_rows].max() == 0
+    # GEMM2 on the GPU's own intermediate, float64 reference
+    pairs = srt[rows]
+    y = np.einsum("ri,rni->rn", h_gpu, W2[eid_rows[rows]]) * wts.reshape(-1).numpy()[pairs][:, None]
+    got = staged.float().cpu().numpy()[pairs]
+    np.testing.assert_allclose(got, y, rtol=2 ** -7, atol=1e-3 * np.abs(y).max())
+
+
+def test_gemm_skips_non_local_experts():
+    T, H, I, E, k = 128, 256, 128, 8, 2
+    x, w1q, w1s, w2q, w2s, ids, wts = _gemm_problem(T, H, I, E, k, 77)
+    emap = torch.full((E,), -1, dtype=torch.int32)
+    emap[2:4] = torch.tensor([0, 1], dtype=torch.int32)
+    xq, xs = ops.quant_g128(x.to(DEV))
+    w1i, w1is = ops.w1_interleave(w1q[2:4].contiguous().to(DEV), w1s[2:4].contiguous().to(DEV))
+    sorted_ids, eids, ntpp = ops.moe_align_block_size(ids.to(DEV), 128, E, emap.to(DEV))
+    rows_cap = eids.numel() * 128
+    staged = torch.full((T * k, H), float("nan"), dtype=torch.bfloat16, device=DEV)
+    hq, hst = ops.gemm1(xq, xs, w1i, w1is, sorted_ids, eids, ntpp, T * k, k, rows_cap)
+    ops.gemm2(hq, hst, w2q[2:4].contiguous().to(DEV), w2s[2:4].contiguous().to(DEV), sorted_ids, eids, ntpp, T * k,
+              wts.reshape(-1).to(DEV), out=staged)
+    out = ops.combine(staged, k, ids.to(DEV), emap.to(DEV))
+    torch.cuda.synchronize()
+    local = ((ids == 2) | (ids == 3)).reshape(-1)
+    st = staged.float().cpu()
+    assert torch.isfinite(st[local]).all() and torch.isnan(st[~local]).all()
+    assert torch.isfinite(out.float()).all()
+
+
+# ---------------------------------------------------------------- combine
+@pytest.mark.parametrize("T,k,H,shared", [(64, 2, 256, False), (100, 8, 1024, True), (1, 1, 128, True)])
+def test_combine_bit_exact(T, k, H, shared):
+    st = _bf16((T * k, H), 3)
+    sh = _bf16((T, H), 4) if shared else None
+    out = ops.combine(st.to(DEV), k, shared=None if sh is None else sh.to(DEV))
+    acc = np.zeros((T, H), np.float32)
+    s3 = st.float().numpy().reshape(T, k, H)
+    for j in range(k):
+        acc = (acc + s3[:, j]).astype(np.float32)
+    if sh is not None:
+        acc = (acc + sh.float().numpy()).astype(np.float32)
+    exp = ofp8.f32_to_bf16_bits(acc)
+    assert np.array_equal(out.view(torch.int16).cpu().numpy().astype(np.uint16), exp)

@@ -1,0 +1,106 @@
+"""Layer parity on a B200: the full b2m forward against the fp32 golden.
+
+Gates are the reference worker's (cos >= 0.995, masked rel_p99 <= 5.0,
+|scale - 1| <= 0.05, ``moe_bench/worker.py:108-110``) plus a max-abs bound:
+max |out - golden| <= 1.5 x (max |golden_fp8act - golden_bf16act|), the
+calibration rule of ``tests/calibrate_tolerance.py:17-25`` re-run at each shape.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import golden as ogolden
+from oracle import quant as oquant
+
+pytestmark = pytest.mark.gpu
+
+from tests.conftest import cuda_ok  # noqa: E402
+
+if not cuda_ok():
+    pytest.skip("needs an sm_100 GPU", allow_module_level=True)
+
+from tests import torch_ref  # noqa: E402
+from td_benchmark_b200 import configs, data  # noqa: E402
+from td_benchmark_b200.context import DistContext  # noqa: E402
+from td_benchmark_b200.layer import ExpertWeights, MoELayer  # noqa: E402
+from td_benchmark_b200.schemes import build_scheme  # noqa: E402
+from td_benchmark_b200.schemes.base import SchemeCfg  # noqa: E402
+
+DEV = torch.device("cuda", 0)
+
+
+def _gates(out, ref, calib):
+    rep = ogolden.compare_outputs(out, ref, **ogolden.GATES)
+    assert rep["pass"], rep
+    assert rep["max_abs"] <= 1.5 * calib, (rep["max_abs"], calib)
+    return rep
+
+
+def test_tiny_layer_vs_reference_fixture(golden_dir):
+    """The reference's own data bundle and golden output (BASELINE tiny shape + shared expert)."""
+    d = np.load(golden_dir / "golden_tiny.npz")
+    t = lambda a, dt=None: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)  # noqa: E731
+    fp8 = lambda a: t(a).view(torch.float8_e4m3fn)  # noqa: E731
+    w = ExpertWeights.prepare(fp8(d["w1_q"]), t(d["w1_s"]), fp8(d["w2_q"]), t(d["w2_s"]))
+    sw = ExpertWeights.prepare(fp8(d["sw1_q"]), t(d["sw1_s"]), fp8(d["sw2_q"]), t(d["sw2_s"]))
+    layer = MoELayer(w, 64, 2, 8, shared=sw)
+    x = torch.from_numpy(d["hidden"]).to(torch.bfloat16).to(DEV)
+    out = layer.forward(x, t(d["topk_ids"]), t(d["topk_weights"]))
+    torch.cuda.synchronize()
+    layer.check()
+    got = out.float().cpu().numpy()
+    w1 = oquant.dequant_block128(d["w1_q"], d["w1_s"])
+    w2 = oquant.dequant_block128(d["w2_q"], d["w2_s"])
+    sw1 = oquant.dequant_block128(d["sw1_q"], d["sw1_s"])
+    sw2 = oquant.dequant_block128(d["sw2_q"], d["sw2_s"])
+    hb = x.float().cpu().numpy()
+    g_fp8 = ogolden.golden_moe(hb, d["topk_ids"], d["topk_weights"], w1, w2, sw1, sw2, act_quant=True)
+    g_none = ogolden.golden_moe(hb, d["topk_ids"], d["topk_weights"], w1, w2, sw1, sw2, act_quant=False)
+    calib = float(np.abs(g_fp8 - g_none).max())
+    _gates(got, d["out_bf16in"], calib)
+    # against the reference golden on the unrounded fp32 hidden states, as the worker verifies
+    rep = ogolden.compare_outputs(got, d["out"], **ogolden.GATES)
+    assert rep["pass"], rep
+
+
+def _run_scheme(cfg, code="d1"):
+    bundle = data.build_bundle(cfg, device=DEV)
+    ctx = DistContext(rank=0, world_size=1, local_rank=0, device=DEV)
+    inst = build_scheme(cfg, ctx, bundle, SchemeCfg(code, {"check_status": True}))
+    out = inst.run()
+    out2 = inst.run()                                 # second call reuses every buffer
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
+    inst.close()
+    return bundle, out
+
+
+def test_tiny_config_vs_numpy_oracle():
+    cfg = configs.preset("tiny")
+    bundle, out = _run_scheme(cfg)
+    ck = bundle.ckpt
+    w1 = oquant.dequant_block128(ck.w1.fp8.view(torch.uint8).cpu().numpy(), ck.w1.scale.cpu().numpy())
+    w2 = oquant.dequant_block128(ck.w2.fp8.view(torch.uint8).cpu().numpy(), ck.w2.scale.cpu().numpy())
+    h = bundle.hidden_full.float().cpu().numpy()
+    ids, wts = bundle.routing.topk_ids_full.cpu().numpy(), bundle.routing.topk_weights_full.cpu().numpy()
+    g = ogolden.golden_moe(h, ids, wts, w1, w2, act_quant=True)
+    gn = ogolden.golden_moe(h, ids, wts, w1, w2, act_quant=False)
+    _gates(out.float().cpu().numpy(), g, float(np.abs(g - gn).max()))
+
+
+@pytest.mark.parametrize("name,over", [
+    ("qwen3", {"M": 32}), ("qwen3", {"M": 256}),
+    ("mixtral", {"M": 512}),
+    ("dsv3", {"M": 512}), ("dsv3", {"M": 2048, "imbalance_kind": "none"}),
+])
+def test_baseline_shapes_vs_torch_golden(name, over):
+    cfg = configs.preset(name, **over)
+    bundle, out = _run_scheme(cfg)
+    ck = bundle.ckpt
+    sw = None
+    if ck.shared_w1 is not None:
+        sw = (ck.shared_w1.fp8, ck.shared_w1.scale, ck.shared_w2.fp8, ck.shared_w2.scale)
+    g, calib = torch_ref.act_quant_error(bundle.hidden_full, bundle.routing.topk_ids_full,
+                                         bundle.routing.topk_weights_full, ck.w1.fp8, ck.w1.scale, ck.w2.fp8,
+                                         ck.w2.scale, sw)
+    _gates(out.float().cpu().numpy(), g.cpu().numpy(), calib)

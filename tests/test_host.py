@@ -1,0 +1,116 @@
+"""Host-side logic on CPU: weight prep, routing, configs, scheme plumbing."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant as oquant
+from td_benchmark_b200 import configs, data, weights
+from td_benchmark_b200.schemes import REGISTRY, SchemeConfigError, build_scheme
+from td_benchmark_b200.schemes.base import SchemeCfg, SchemeSpec, TunableSpec, make_lazy_instance, validate_tunables
+
+
+def test_torch_block_quant_matches_oracle():
+    w = torch.randn((3, 384, 256), generator=torch.Generator().manual_seed(0)) * 0.02
+    w[0, :128, :128] = 0
+    q, s = weights.quantize_block128(w)
+    q2, s2 = oquant.quant_block128(w.numpy())
+    assert np.array_equal(q.view(torch.uint8).numpy(), q2)
+    assert np.array_equal(s.numpy(), s2)
+    deq = weights.dequantize_block128(q, s)
+    assert np.array_equal(deq.float().numpy(), oquant.dequant_block128(q2, s2))
+
+
+def test_route_matches_reference_fixture(golden_dir):
+    d = np.load(golden_dir / "routing.npz")
+    hid = torch.from_numpy(d["hidden_bits"]).view(torch.bfloat16)
+    gate = torch.from_numpy(d["gate_bits"]).view(torch.bfloat16)
+    logits = hid.float() @ gate.float().T
+    ids, w = data.route(logits, 8, configs.RoutingCfg())
+    assert np.array_equal(ids.numpy(), d["ids_uniform"]) and np.array_equal(w.numpy(), d["w_uniform"])
+    ids, w = data.route(logits, 8, configs.RoutingCfg(imbalance_kind="zipf", zipf_s=1.2, gate_seed=42))
+    assert np.array_equal(ids.numpy(), d["ids_zipf"]) and np.array_equal(w.numpy(), d["w_zipf"])
+
+
+def test_bundle_deterministic_and_rank_sliced():
+    cfg = configs.preset("tiny")
+    b0 = data.build_bundle(cfg, rank=0, world_size=2)
+    b1 = data.build_bundle(cfg, rank=1, world_size=2)
+    full = data.build_bundle(cfg, rank=0, world_size=1)
+    assert torch.equal(torch.cat([b0.hidden_local, b1.hidden_local]), full.hidden_local)
+    assert torch.equal(b0.routing.topk_ids_full, full.routing.topk_ids_full)
+    assert torch.equal(b1.ckpt.w1.fp8.view(torch.uint8), full.ckpt.w1.fp8.view(torch.uint8))
+    assert full.routing.topk_ids_full.dtype == torch.int32
+    assert torch.allclose(full.routing.topk_weights_full.sum(-1), torch.ones(64))
+
+
+def test_zipf_routing_is_skewed():
+    cfg = configs.preset("dsv3", M=2048)
+    b = data.build_bundle(cfg, with_weights=False)
+    counts = torch.bincount(b.routing.topk_ids_full.flatten().long(), minlength=256).float()
+    assert counts.max() / counts.mean() > 5
+
+
+def test_presets_and_validation():
+    assert configs.PRESETS["mixtral"].shape.intermediate_per_tp(8) == 1792
+    assert configs.PRESETS["dsv3"].shape.local_E(8) == 32
+    with pytest.raises(configs.ConfigError, match="violates constraint"):
+        configs.ShapeCfg(M=8, K=100, E=4, top_k=2, n_gateup=256, n_down=128)
+    with pytest.raises(configs.ConfigError):
+        configs.preset("nope")
+    assert configs.preset("qwen3", M=32).shape.M == 32
+
+
+def _full_weights(E=4, I=256, H=256, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    w1q, w1s = weights.quantize_block128(torch.randn((E, 2 * I, H), generator=g) * 0.02)
+    w2q, w2s = weights.quantize_block128(torch.randn((E, H, I), generator=g) * 0.02)
+    return w1q, w1s, w2q, w2s
+
+
+def test_tp_views_aligned_slices_codes():
+    w1q, w1s, w2q, w2s = _full_weights(I=512)
+    v = weights.tp_views(w1q, w1s, w2q, w2s, rank=1, world_size=2)
+    assert v["shard_level"] == "L0" and v["inter"] == 256
+    assert torch.equal(v["w1"][:, :256].view(torch.uint8), w1q[:, 256:512].view(torch.uint8))
+    assert torch.equal(v["w1"][:, 256:].view(torch.uint8), w1q[:, 768:].view(torch.uint8))
+    assert torch.equal(v["w2"].view(torch.uint8), w2q[:, :, 256:].view(torch.uint8))
+    assert v["w1_scale"].shape == (4, 4, 2) and v["w2_scale"].shape == (4, 2, 2)
+
+
+def test_tp_views_ragged_pads_to_128():
+    # Qwen3 at TP=8: I/P = 96 -> zero padded to 128 ("L2", runtime.py:46-55)
+    w1q, w1s, w2q, w2s = _full_weights(E=2, I=768, H=256)
+    v = weights.tp_views(w1q, w1s, w2q, w2s, rank=3, world_size=8)
+    assert v["shard_level"] == "L2" and v["inter"] == 128
+    assert v["w1"].shape == (2, 256, 256) and v["w2"].shape == (2, 256, 128)
+    assert v["w1"][:, 96:128].float().abs().sum() == 0 and v["w2"][:, :, 96:].float().abs().sum() == 0
+
+
+def test_ep_views_expert_map():
+    w1q, w1s, w2q, w2s = _full_weights(E=8)
+    v = weights.ep_views(w1q, w1s, w2q, w2s, rank=2, world_size=4)
+    assert v["expert_map"].tolist() == [-1, -1, -1, -1, 0, 1, -1, -1]
+    assert torch.equal(v["w1"].view(torch.uint8), w1q[4:6].view(torch.uint8))
+
+
+def test_scheme_registry_and_tunables():
+    assert {"d1", "d2"} <= set(REGISTRY)
+    spec, _ = REGISTRY["d1"]
+    assert spec.weight_dtype == "fp8" and spec.act_quant == "group128" and not spec.requires_nvshmem
+    assert validate_tunables(spec, {}) == {"check_status": False}
+    with pytest.raises(SchemeConfigError, match="violate schema"):
+        validate_tunables(spec, {"nope": 1})
+    with pytest.raises(SchemeConfigError, match="expected bool"):
+        validate_tunables(spec, {"check_status": 1})
+    with pytest.raises(SchemeConfigError, match="not registered"):
+        build_scheme(None, None, None, SchemeCfg("zz", {}))
+    with pytest.raises(RuntimeError, match="requires a DataBundle"):
+        build_scheme(configs.preset("tiny"), None, None, SchemeCfg("d1", {}))
+
+
+def test_int_tunable_rejects_bool():
+    spec = SchemeSpec("x", "x", "f", "TP", "c", "fp8", "group128", False, {"n": TunableSpec(int, 2, "d")})
+    with pytest.raises(SchemeConfigError):
+        validate_tunables(spec, {"n": True})
+    inst = make_lazy_instance(spec, {"n": 2}, lambda: 7)
+    assert inst.run() == 7 and inst.run_staged().output == 7 and inst.diagnostics["scheme"] == "x"
