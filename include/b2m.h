@@ -65,6 +65,29 @@ int b2m_set_timeout_ns(uint64_t ns);
 int b2m_quant_g128(const void* x, int64_t rows, int64_t cols, int64_t ldx, void* q, int64_t ldq,
                    float* scale, int64_t ld_scale, void* stream);
 
+/* Same rule with the scales written K-block-major: scale_t[g * ld_scale_t + r]
+ * (the layout the grouped GEMMs read with one bulk copy per 128-row block). */
+int b2m_quant_g128_t(const void* x, int64_t rows, int64_t cols, int64_t ldx, void* q, int64_t ldq,
+                     float* scale_t, int64_t ld_scale_t, void* stream);
+
+/* K1 + dispatch: quantise bf16 tokens [tokens, hidden] (rule of K1) and write each
+ * token's codes and scales to the sorted rows of its top-k pairs:
+ *   a_sorted[pair_pos[t*k + j], :] = q[t, :],  a_scale_t[g, pair_pos[t*k + j]] = scale[t, g]
+ * (pairs with pair_pos < 0 are skipped).  This replaces the A-row gather the
+ * reference's fused_moe_kernel does through sorted_token_ids // top_k
+ * (moe_bench/overlap/kernels.py:123-125, :140-141) with one write pass, so the gate/up GEMM
+ * reads A with tiled TMA.  q_tok / scale_tok_t (nullable, together) also receive the
+ * token-order codes and K-block-major scales (ld_scale_tok_t >= tokens), as the
+ * shared expert needs.  hidden % 128 == 0; x rows 16-byte aligned. */
+int b2m_quant_dispatch(const void* x, int64_t tokens, int64_t hidden, int64_t ldx, const int32_t* pair_pos,
+                       int32_t top_k, void* a_sorted, float* a_scale_t, int64_t rows_cap, void* q_tok,
+                       float* scale_tok_t, int64_t ld_scale_tok_t, void* stream);
+
+/* Dispatch of already-quantised token rows (after an all-gather): xq e4m3 [tokens,
+ * hidden], xs fp32 [tokens, hidden/128] -> a_sorted / a_scale_t as b2m_quant_dispatch. */
+int b2m_dispatch_rows(const void* xq, const float* xs, int64_t tokens, int64_t hidden, const int32_t* pair_pos,
+                      int32_t top_k, void* a_sorted, float* a_scale_t, int64_t rows_cap, void* stream);
+
 /* ---------------------------------------------------------------------------
  * K2  moe_align_block_size.
  * Replaces vllm.model_executor.layers.fused_moe.moe_align_block_size
@@ -76,10 +99,12 @@ int b2m_quant_g128(const void* x, int64_t rows, int64_t cols, int64_t ldx, void*
  * remapped through expert_map when non-NULL, -1 for non-local experts and for the
  * tail); num_tokens_post_padded [1].  Required capacities: sorted_cap >=
  * numel + E*(block_size-1) (or numel*block_size when numel < E) and
- * expert_ids_cap >= cdiv(sorted_cap, block_size).  num_experts <= 1024. */
+ * expert_ids_cap >= cdiv(sorted_cap, block_size).  num_experts <= 1024.
+ * pair_pos (nullable, int32 [numel]) additionally receives the inverse map: the
+ * sorted position of every pair, or -1 when its expert is not local. */
 int b2m_align(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int32_t block_size,
               const int32_t* expert_map, int32_t* sorted_token_ids, int64_t sorted_cap, int32_t* expert_ids,
-              int64_t expert_ids_cap, int32_t* num_tokens_post_padded, void* stream);
+              int64_t expert_ids_cap, int32_t* num_tokens_post_padded, int32_t* pair_pos, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Gate/up weight layout for K3.  The reference stores w1 as [E, 2I, H] with all
@@ -95,21 +120,25 @@ int b2m_w1_interleave(const void* w1, const float* w1_scale, int32_t num_experts
  * Replaces invoke_moe_kernel_k_split/fused_moe_kernel_accumulate
  * (moe_bench/overlap/kernels.py:36-214, :317-452) + torch.ops._C.silu_and_mul +
  * the second moe_kernel_quantize_input (overlap_forward.py:530-561).
- * For each 128-row block b of sorted_token_ids with expert e = expert_ids[b] >= 0,
- * row p = sorted position, pair = sorted_token_ids[p], token = pair / top_k:
- *   gu[p, n] = sum_kb (sum_k A[token,k] W1[e,n,k]) * a_scale[token,kb] * w1_scale[e,n/128,kb]
+ * A is expert-sorted: row p of a_sorted holds the codes of the token of pair
+ * sorted_token_ids[p] (b2m_quant_dispatch / b2m_dispatch_rows); pad rows are
+ * don't-care (their outputs are never read back).  For each 128-row block b with
+ * expert e = expert_ids[b] >= 0 and each row p of it:
+ *   gu[p, n] = sum_kb (sum_k A[p,k] W1[e,n,k]) * a_scale_t[kb,p] * w1_scale[e,n/128,kb]
  *   h[p, j]  = silu(gu[p, j]) * gu[p, I + j]                      (fp32)
- *   out_q[p, j] / out_scale_t[j/128, p] = 1x128 e4m3 quant of h (rule of K1)
- * Pad rows (pair >= numel) read zeros.  Blocks with expert -1 are skipped.
- * a_fp8: e4m3 [a_rows, hidden] (row stride hidden); a_scale: fp32 [a_rows, hidden/128];
+ *   out_q[p, j] / out_scale_t[j/128, p] = 1x128 e4m3 quant of h
+ *     (scale rule of K1; codes from h * (1/scale), so a code can differ from the
+ *      IEEE-division result by one step in the rare tie case)
+ * Blocks with expert -1 are skipped.
+ * a_sorted: e4m3 [rows_cap, hidden]; a_scale_t: fp32 [hidden/128, rows_cap];
  * w1: interleaved e4m3 [E, 2I, hidden]; w1_scale: interleaved fp32 [E, 2I/128, hidden/128];
- * out_q: e4m3 [rows_cap, I]; out_scale_t: fp32 [I/128, rows_cap] (K-block major).
- * hidden % 128 == 0, I % 128 == 0, rows_cap % 128 == 0 and rows_cap >= the
- * sorted_token_ids capacity. */
-int b2m_gemm1(const void* a_fp8, const float* a_scale, int64_t a_rows, int64_t hidden, const void* w1,
-              const float* w1_scale, int32_t num_experts, int32_t inter, const int32_t* sorted_token_ids,
-              const int32_t* expert_ids, const int32_t* num_tokens_post_padded, int64_t rows_cap, int64_t numel,
-              int32_t top_k, void* out_q, float* out_scale_t, int32_t* dev_status, void* stream);
+ * out_q: e4m3 [rows_cap, I]; out_scale_t: fp32 [I/128, rows_cap].
+ * hidden % 128 == 0, I % 128 == 0, rows_cap % 128 == 0, expert_ids holds
+ * rows_cap/128 entries. */
+int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden, const void* w1,
+              const float* w1_scale, int32_t num_experts, int32_t inter, const int32_t* expert_ids,
+              const int32_t* num_tokens_post_padded, void* out_q, float* out_scale_t, int32_t* dev_status,
+              void* stream);
 
 /* ---------------------------------------------------------------------------
  * K4  down grouped GEMM with the routed top-k weight in the epilogue.

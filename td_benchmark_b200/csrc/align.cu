@@ -9,7 +9,9 @@
 // __match_any_sync groups — no atomics, so the result does not depend on timing.
 // Scan: padded counts -> expert segment starts; per-(warp, expert) bases are the
 // segment start plus the counts of lower warps.  Pass C: each warp walks its range
-// again in order and places every pair at base + rank inside its match group.
+// again in order and places every pair at base + rank inside its match group; the
+// optional inverse map pair_pos[pair] = sorted position (-1 for a non-local expert)
+// drives the row dispatch into the sorted operand layout of the gate/up GEMM.
 #include "b2m_common.cuh"
 #include "b2m_host.h"
 
@@ -23,7 +25,8 @@ constexpr int kMaxExperts = 1024;
 __global__ void __launch_bounds__(kAlignThreads, 1)
     align_kernel(const int32_t* __restrict__ topk_ids, int64_t numel, int32_t num_experts, int32_t bs,
                  const int32_t* __restrict__ expert_map, int32_t* __restrict__ sorted_ids, int64_t sorted_cap,
-                 int32_t* __restrict__ expert_ids, int64_t expert_ids_cap, int32_t* __restrict__ ntpp_out) {
+                 int32_t* __restrict__ expert_ids, int64_t expert_ids_cap, int32_t* __restrict__ ntpp_out,
+                 int32_t* __restrict__ pair_pos) {
   extern __shared__ int32_t sm[];
   int32_t* warp_cnt = sm;                                  // [32][E] counts, then bases
   int32_t* counts = warp_cnt + kAlignWarps * num_experts;  // [E]
@@ -102,6 +105,10 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
     const int leader = __ffs(grp) - 1;
     const int rank = __popc(grp & ((1u << lane) - 1u));
     if (e >= 0) sorted_ids[my_cnt[e] + rank] = static_cast<int32_t>(i);
+    if (pair_pos && i < hi) {
+      const bool local = e >= 0 && (expert_map == nullptr || __ldg(expert_map + e) >= 0);
+      pair_pos[i] = local ? my_cnt[e] + rank : -1;
+    }
     __syncwarp();
     if (e >= 0 && lane == leader) my_cnt[e] += __popc(grp);
     __syncwarp();
@@ -129,7 +136,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
 extern "C" int b2m_align(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int32_t block_size,
                          const int32_t* expert_map, int32_t* sorted_token_ids, int64_t sorted_cap,
                          int32_t* expert_ids, int64_t expert_ids_cap, int32_t* num_tokens_post_padded,
-                         void* stream) {
+                         int32_t* pair_pos, void* stream) {
   using namespace b2m;
   B2M_TRY(require_sm100(nullptr));
   if (num_experts <= 0 || num_experts > kMaxExperts)
@@ -144,7 +151,8 @@ extern "C" int b2m_align(const int32_t* topk_ids, int64_t numel, int32_t num_exp
   if (expert_ids_cap < (sorted_cap + block_size - 1) / block_size)
     return fail(B2M_ERR_ARG, "align: expert_ids_cap=%lld < cdiv(sorted_cap, block_size)",
                 (long long)expert_ids_cap);
-  if (!sorted_token_ids || !expert_ids || !num_tokens_post_padded || (numel > 0 && !topk_ids))
+  if ((sorted_cap > 0 && !sorted_token_ids) || (expert_ids_cap > 0 && !expert_ids) || !num_tokens_post_padded ||
+      (numel > 0 && !topk_ids))
     return fail(B2M_ERR_ARG, "align: null pointer");
   const size_t smem = (size_t(kAlignWarps) + 2) * num_experts * sizeof(int32_t);
   if (smem > 48 * 1024)
@@ -153,6 +161,6 @@ extern "C" int b2m_align(const int32_t* topk_ids, int64_t numel, int32_t num_exp
         "align: cudaFuncSetAttribute"));
   align_kernel<<<1, kAlignThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       topk_ids, numel, num_experts, block_size, expert_map, sorted_token_ids, sorted_cap, expert_ids,
-      expert_ids_cap, num_tokens_post_padded);
+      expert_ids_cap, num_tokens_post_padded, pair_pos);
   return check_cuda(cudaGetLastError(), "align launch");
 }

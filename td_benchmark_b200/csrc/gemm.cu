@@ -1,20 +1,27 @@
 // K3 / K4: FP8 grouped GEMMs over ragged expert segments on tcgen05 + TMEM + TMA.
 //
-// Both GEMMs share one persistent, warp-specialised kernel (one CTA per SM):
-//   warp 0      TMA producer.  B (weights) by 2D tiled TMA; A by TMA gather4 of the
-//               routed token rows (gate/up GEMM) or by 2D tiled TMA of the sorted
-//               intermediate (down GEMM).  4-stage smem ring, 48 KB per stage.
+// Both GEMMs share one persistent, warp-specialised kernel (one CTA per SM,
+// 384 threads, 4-stage shared-memory ring of 48 KB operand stages):
+//   warp 0      stage producer: A (2D tiled TMA of the expert-sorted rows: the token
+//               rows dispatched by b2m_quant_dispatch / b2m_dispatch_rows for the gate/up
+//               GEMM, the gate/up output for the down GEMM), its 128 row scales (one
+//               512-byte bulk copy of the K-block-major scale array), B (weights) by 2D
+//               tiled TMA, and the B block scales of the stage (prefetched 32 K blocks at
+//               a time across the warp's lanes).
 //   warp 1      TMEM allocator and single-thread MMA issuer: per 128-wide K block,
 //               4 x tcgen05.mma kind::f8f6f4 (M=128, N=256, K=32) into one of two
 //               TMEM accumulators (2 x 256 fp32 columns).
 //   warps 4-11  promotion + epilogue.  The reference applies block scales per 128-K
 //               step (moe_bench/overlap/kernels.py:179: acc += dot(a, b) * a_s * b_s);
 //               so does this kernel: each K block's partial product is read from TMEM
-//               (tcgen05.ld), multiplied by a_scale[row, kb] * b_scale[nblk, kb] and
-//               added to fp32 registers.  The double-buffered TMEM lets the tensor
-//               pipe run one K block ahead of the promotion.
-// Tiles are (128 sorted rows) x (256 output columns).  The tile space is walked
-// with a static stride of gridDim.x; blocks whose expert id is -1 are skipped.
+//               (tcgen05.ld), multiplied by a_scale[row, kb] * b_scale[nblk, kb] (read
+//               from the stage in shared memory) and added to fp32 registers with packed
+//               f32x2 FMAs.  The double-buffered TMEM lets the tensor pipe run one K
+//               block ahead; a stage is recycled once the MMA has consumed it and the
+//               epilogue warps have read its scales.
+// Tiles are (128 sorted rows) x (256 output columns), visited M-block fastest so
+// CTAs running together share the weight tile in L2.  The tile space is walked with
+// a static stride of gridDim.x; blocks whose expert id is -1 are skipped.
 //
 // Gate/up epilogue (replaces silu_and_mul + the second quant, overlap_forward.py:554-561):
 // the weight rows are interleaved at set-up so one tile holds gate columns
@@ -27,7 +34,7 @@
 // row of the top-k staging buffer.
 //
 // All waits are bounded (b2m_set_timeout_ns); on a timeout the kernel records the
-// site in dev_status, drains its own TMA copies and frees TMEM before returning.
+// site in dev_status, drains its own copies and MMAs and frees TMEM before returning.
 #include <cudaTypedefs.h>
 
 #include "b2m_common.cuh"
@@ -42,7 +49,8 @@ constexpr int A_BYTES = BM * BK;  // 16 KB
 constexpr int B_BYTES = BN * BK;  // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int NUM_THREADS = 384;
-constexpr int NUM_EPI_THREADS = 256;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int NUM_EPI_THREADS = NUM_EPI_WARPS * 32;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t IDESC = idesc_e4m3_f32(BM, BN);
 
@@ -55,7 +63,9 @@ struct Control {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
-  float amax[2][2][BM];  // [tile parity][column half][row]
+  alignas(16) float as[STAGES][BM];  // A row scales of each stage
+  alignas(16) float bs[STAGES][4];   // B block scales of each stage: rows [0,128) and [128,256) of the tile
+  float amax[2][2][BM];              // [tile parity][column half][row]
 };
 
 constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + sizeof(Control) + 1024;
@@ -72,9 +82,8 @@ struct GemmParams {
   int32_t num_nt;      // output tiles along N
   int32_t n_blocks;    // 128-row scale blocks per expert of B
   int32_t n_rows;      // rows of B per expert
-  int32_t a_rows;      // gate/up: token rows of A (row id a_rows reads zeros)
-  const float* a_scale;
-  int64_t a_scale_ld;  // gate/up: row stride of [a_rows, KB]; down: column count rows_cap of [KB, rows_cap]
+  const float* a_scale;  // [KB, rows_cap]: scale of sorted row p, K block kb at kb * rows_cap + p
+  int64_t a_scale_ld;    // rows_cap
   const float* b_scale;
   int64_t rows_cap;
   uint8_t* out_q;
@@ -87,30 +96,44 @@ struct GemmParams {
   uint64_t timeout_ns;
 };
 
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+// silu(x) = x * sigmoid(x).  The gate/up intermediate is requantised to e4m3 right
+// after, so the fast exponential and reciprocal are far inside its tolerance.
+__device__ __forceinline__ float silu(float x) { return x * __frcp_rn(1.0f + __expf(-x)); }
 
+// Shared tile walk of every role: returns false when the tile is skipped (expert -1).
+struct TileWalk {
+  int64_t num_tiles;
+  int num_mb;
+};
+
+// ---------------------------------------------------------------- warp 0: B (+A for the down GEMM)
 template <bool kGateUp>
-__device__ __forceinline__ void producer_warp(const CUtensorMap* map_a, const CUtensorMap* map_b,
-                                              const GemmParams& p, uint8_t* smem, Control* C, int64_t num_tiles,
-                                              int num_mb, int lane) {
+__device__ __forceinline__ void stage_producer(const CUtensorMap* map_a, const CUtensorMap* map_b,
+                                               const GemmParams& p, uint8_t* smem, Control* C, TileWalk tw,
+                                               int lane) {
   volatile int* abort = &C->abort;
   uint32_t kbg = 0;
   bool alive = true;
-  for (int64_t tile = blockIdx.x; tile < num_tiles && alive; tile += gridDim.x) {
-    const int mb = static_cast<int>(tile % num_mb);
-    const int nt = static_cast<int>(tile / num_mb);
+  const uint32_t tx = A_BYTES + B_BYTES + BM * 4;
+  for (int64_t tile = blockIdx.x; tile < tw.num_tiles && alive; tile += gridDim.x) {
+    const int mb = static_cast<int>(tile % tw.num_mb);
+    const int nt = static_cast<int>(tile / tw.num_mb);
     const int e = __ldg(p.expert_ids + mb);
     if (e < 0) continue;
-    int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
-    if (kGateUp) {
-      const int4 ids = __ldg(reinterpret_cast<const int4*>(p.sorted_ids + mb * BM) + lane);
-      r0 = ids.x < p.numel ? ids.x / p.top_k : p.a_rows;
-      r1 = ids.y < p.numel ? ids.y / p.top_k : p.a_rows;
-      r2 = ids.z < p.numel ? ids.z / p.top_k : p.a_rows;
-      r3 = ids.w < p.numel ? ids.w / p.top_k : p.a_rows;
-    }
+    const int blk0 = 2 * nt;
+    const int blk1 = 2 * nt + 1 < p.n_blocks ? 2 * nt + 1 : 2 * nt;  // the down GEMM's last tile may be half wide
+    const float* bs0 = p.b_scale + (static_cast<int64_t>(e) * p.n_blocks + blk0) * p.num_kb;
+    const float* bs1 = p.b_scale + (static_cast<int64_t>(e) * p.n_blocks + blk1) * p.num_kb;
     const int b_row = e * p.n_rows + nt * BN;
+    float pre0 = 0.0f, pre1 = 0.0f;
     for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
+      if ((kb & 31) == 0) {  // lane j holds the scales of K block kb + j
+        const int k = kb + lane;
+        pre0 = k < p.num_kb ? __ldg(bs0 + k) : 0.0f;
+        pre1 = k < p.num_kb ? __ldg(bs1 + k) : 0.0f;
+      }
+      const float s0 = __shfl_sync(0xffffffffu, pre0, kb & 31);
+      const float s1 = __shfl_sync(0xffffffffu, pre1, kb & 31);
       const int s = kbg % STAGES;
       const uint32_t ph = (kbg / STAGES) & 1;
       int ok = 1;
@@ -120,21 +143,20 @@ __device__ __forceinline__ void producer_warp(const CUtensorMap* map_a, const CU
         alive = false;
         break;
       }
-      uint8_t* sa = smem + s * STAGE_BYTES;
-      uint8_t* sb = sa + A_BYTES;
-      if (lane == 0) mbar_arrive_expect_tx(&C->full[s], STAGE_BYTES);
-      __syncwarp();
-      if (kGateUp) {
-        tma_gather4(sa + lane * 4 * BK, map_a, &C->full[s], kb * BK, r0, r1, r2, r3);
-      } else if (lane == 0) {
+      if (lane == 0) {
+        uint8_t* sa = smem + s * STAGE_BYTES;
+        C->bs[s][0] = s0;
+        C->bs[s][1] = s1;
+        mbar_arrive_expect_tx(&C->full[s], tx);
         tma_load_2d(sa, map_a, &C->full[s], kb * BK, mb * BM);
+        tma_load_2d(sa + A_BYTES, map_b, &C->full[s], kb * BK, b_row);
+        bulk_load(C->as[s], p.a_scale + static_cast<int64_t>(kb) * p.a_scale_ld + static_cast<int64_t>(mb) * BM,
+                  BM * 4, &C->full[s]);
       }
-      if (lane == 0) tma_load_2d(sb, map_b, &C->full[s], kb * BK, b_row);
       __syncwarp();
     }
   }
-  // Drain: every stage issued in the last STAGES iterations must have landed
-  // before the CTA may exit (the normal path has consumed them all already).
+  // Drain: the copies of the last STAGES stages must have landed before the CTA exits.
   if (lane == 0) {
     const uint32_t first = kbg > STAGES ? kbg - STAGES : 0;
     for (uint32_t i = first; i < kbg; ++i)
@@ -143,13 +165,14 @@ __device__ __forceinline__ void producer_warp(const CUtensorMap* map_a, const CU
   __syncwarp();
 }
 
-__device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, Control* C, int64_t num_tiles,
-                                           int num_mb, uint32_t tmem_base) {
+// ---------------------------------------------------------------- warp 1 lane 0: MMA issue
+__device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, Control* C, TileWalk tw,
+                                           uint32_t tmem_base) {
   volatile int* abort = &C->abort;
   uint32_t kbg = 0;
   bool alive = true;
-  for (int64_t tile = blockIdx.x; tile < num_tiles && alive; tile += gridDim.x) {
-    const int mb = static_cast<int>(tile % num_mb);
+  for (int64_t tile = blockIdx.x; tile < tw.num_tiles && alive; tile += gridDim.x) {
+    const int mb = static_cast<int>(tile % tw.num_mb);
     if (__ldg(p.expert_ids + mb) < 0) continue;
     for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
       const int s = kbg % STAGES;
@@ -171,100 +194,84 @@ __device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, C
       mma_commit(&C->tfull[b]);
     }
   }
-  // TMEM is freed after this CTA exits its roles: wait until every MMA issued here
-  // has completed (on the normal path they all have; after an abort some may not).
+  // TMEM is freed after the roles finish: wait until every MMA issued here has
+  // completed (on the normal path they all have; after an abort some may not).
   if (kbg > 0) {
     mma_commit(&C->mma_done);
     mbar_wait(&C->mma_done, 0, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
   }
 }
 
+// ---------------------------------------------------------------- warps 4-11: promotion + epilogue
 template <bool kGateUp>
-__device__ __forceinline__ void epilogue_warps(const GemmParams& p, Control* C, int64_t num_tiles, int num_mb,
-                                               uint32_t tmem_base, int warp, int lane) {
+__device__ __forceinline__ void epilogue_warps(const GemmParams& p, Control* C, TileWalk tw, uint32_t tmem_base,
+                                               int warp, int lane) {
   volatile int* abort = &C->abort;
-  const int q = warp & 3;          // TMEM lane quarter this warp may access
-  const int h = (warp - 4) >> 2;   // column half
-  const int r = q * 32 + lane;     // tile row
+  const int q = warp & 3;         // TMEM lane quarter this warp may access
+  const int h = (warp - 4) >> 2;  // column half
+  const int r = q * 32 + lane;    // tile row
   const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
   uint32_t kbg = 0;
   uint32_t tiles_done = 0;
   bool alive = true;
-  for (int64_t tile = blockIdx.x; tile < num_tiles && alive; tile += gridDim.x) {
-    const int mb = static_cast<int>(tile % num_mb);
-    const int nt = static_cast<int>(tile / num_mb);
-    const int e = __ldg(p.expert_ids + mb);
-    if (e < 0) continue;
-    const int64_t prow = static_cast<int64_t>(mb) * BM + r;
-    const int pair = __ldg(p.sorted_ids + prow);
-    const bool valid = pair < p.numel;
+  // Column chunks owned by this thread (32 fp32 columns each) and which stage scale they use.
+  const uint32_t c0 = kGateUp ? 64 * h : 128 * h;
+  const uint32_t c1 = c0 + 32;
+  const uint32_t c2 = kGateUp ? 128 + 64 * h : c0 + 64;
+  const uint32_t c3 = c2 + 32;
+  const int sidx_lo = kGateUp ? 0 : h;
+  const int sidx_hi = kGateUp ? 1 : h;
 
-    // Per-K-block scale pointers.
-    const float* as_ptr;
-    int64_t as_step;
-    const float* bs0;
-    const float* bs1;
-    bool bvalid = true;
-    if (kGateUp) {
-      as_ptr = valid ? p.a_scale + static_cast<int64_t>(pair / p.top_k) * p.a_scale_ld : nullptr;
-      as_step = 1;
-      bs0 = p.b_scale + (static_cast<int64_t>(e) * p.n_blocks + 2 * nt) * p.num_kb;  // gate block
-      bs1 = bs0 + p.num_kb;                                                         // up block
-    } else {
-      as_ptr = p.a_scale + prow;
-      as_step = p.a_scale_ld;
-      const int blk = 2 * nt + h;
-      bvalid = blk < p.n_blocks;
-      bs0 = p.b_scale + (static_cast<int64_t>(e) * p.n_blocks + (bvalid ? blk : 0)) * p.num_kb;
-      bs1 = bs0;
-    }
+  // Row info of the next tile is loaded one tile ahead.
+  int64_t tile = blockIdx.x;
+  auto next_valid = [&](int64_t t) {
+    while (t < tw.num_tiles && __ldg(p.expert_ids + static_cast<int>(t % tw.num_mb)) < 0) t += gridDim.x;
+    return t;
+  };
+  tile = next_valid(tile);
+  int pair_next = (!kGateUp && tile < tw.num_tiles) ? __ldg(p.sorted_ids + (tile % tw.num_mb) * BM + r) : 0;
+  for (; tile < tw.num_tiles && alive;) {
+    const int mb = static_cast<int>(tile % tw.num_mb);
+    const int nt = static_cast<int>(tile / tw.num_mb);
+    const int64_t prow = static_cast<int64_t>(mb) * BM + r;
+    const int pair = pair_next;
+    const bool valid = pair < p.numel;
+    float wrow = 1.0f;
+    if (!kGateUp && valid && p.topk_weights) wrow = __ldg(p.topk_weights + pair);
+    const int64_t tile_after = next_valid(tile + gridDim.x);
+    if (!kGateUp && tile_after < tw.num_tiles) pair_next = __ldg(p.sorted_ids + (tile_after % tw.num_mb) * BM + r);
 
     float acc[128];
 #pragma unroll
     for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
 
-    float na = as_ptr ? __ldg(as_ptr) : 0.0f;
-    float nb0 = __ldg(bs0), nb1 = __ldg(bs1);
     for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
-      const float sa = na, sb0 = nb0, sb1 = nb1;
-      if (kb + 1 < p.num_kb) {  // prefetch next K block's scales
-        na = as_ptr ? __ldg(as_ptr + (kb + 1) * as_step) : 0.0f;
-        nb0 = __ldg(bs0 + kb + 1);
-        nb1 = __ldg(bs1 + kb + 1);
-      }
+      const int s = kbg % STAGES;
       const int b = kbg & 1;
-      const uint32_t tph = (kbg >> 1) & 1;
-      int ok = mbar_wait(&C->tfull[b], tph, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE, abort);
+      int ok = mbar_wait(&C->tfull[b], (kbg >> 1) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE, abort);
+      // The stage's scales were published through full[s] (already complete for this kb).
+      ok = ok && mbar_wait(&C->full[s], (kbg / STAGES) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
+                           abort);
       if (!__all_sync(0xffffffffu, ok)) {
         alive = false;
         break;
       }
       tc_fence_after();
+      const float sa = C->as[s][r];
+      const float s_lo = sa * C->bs[s][sidx_lo];
+      const float s_hi = sa * C->bs[s][sidx_hi];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&C->empty[s]);
       const uint32_t base = tmem_base + lane_off + static_cast<uint32_t>(b * BN);
-      // Column chunks owned by this thread (32 fp32 columns each).
-      uint32_t c0, c1, c2, c3;
-      if (kGateUp) {
-        c0 = 64 * h;
-        c1 = 64 * h + 32;
-        c2 = 128 + 64 * h;
-        c3 = 128 + 64 * h + 32;
-      } else {
-        c0 = 128 * h;
-        c1 = c0 + 32;
-        c2 = c0 + 64;
-        c3 = c0 + 96;
-      }
-      const float s_lo = sa * sb0;
-      const float s_hi = sa * sb1;
       {
         float v0[32], v1[32];
         tmem_ld32(base + c0, v0);
         tmem_ld32(base + c1, v1);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = fmaf(v0[i], s_lo, acc[i]);
+        for (int i = 0; i < 32; i += 2) fma2(acc[i], acc[i + 1], v0[i], v0[i + 1], s_lo);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[32 + i] = fmaf(v1[i], s_lo, acc[32 + i]);
+        for (int i = 0; i < 32; i += 2) fma2(acc[32 + i], acc[33 + i], v1[i], v1[i + 1], s_lo);
       }
       {
         float v2[32], v3[32];
@@ -275,9 +282,9 @@ __device__ __forceinline__ void epilogue_warps(const GemmParams& p, Control* C, 
         __syncwarp();
         if (lane == 0) mbar_arrive(&C->tempty[b]);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[64 + i] = fmaf(v2[i], s_hi, acc[64 + i]);
+        for (int i = 0; i < 32; i += 2) fma2(acc[64 + i], acc[65 + i], v2[i], v2[i + 1], s_hi);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[96 + i] = fmaf(v3[i], s_hi, acc[96 + i]);
+        for (int i = 0; i < 32; i += 2) fma2(acc[96 + i], acc[97 + i], v3[i], v3[i + 1], s_hi);
       }
     }
     if (!alive) break;
@@ -299,31 +306,32 @@ __device__ __forceinline__ void epilogue_warps(const GemmParams& p, Control* C, 
       if (!__all_sync(0xffffffffu, ok)) break;
       amax = fmaxf(C->amax[par][0][r], C->amax[par][1][r]);
       const float scale = fmaxf(amax / 448.0f, 1e-12f);
+      const float inv = 1.0f / scale;  // one IEEE division per row; codes use x * (1/scale)
       uint8_t* dst = p.out_q + prow * p.inter + nt * 128 + 64 * h;
 #pragma unroll
       for (int i = 0; i < 64; i += 16) {
         uint4 w;
-        w.x = pack4_e4m3(clamp448(acc[i + 0] / scale), clamp448(acc[i + 1] / scale), clamp448(acc[i + 2] / scale),
-                         clamp448(acc[i + 3] / scale));
-        w.y = pack4_e4m3(clamp448(acc[i + 4] / scale), clamp448(acc[i + 5] / scale), clamp448(acc[i + 6] / scale),
-                         clamp448(acc[i + 7] / scale));
-        w.z = pack4_e4m3(clamp448(acc[i + 8] / scale), clamp448(acc[i + 9] / scale),
-                         clamp448(acc[i + 10] / scale), clamp448(acc[i + 11] / scale));
-        w.w = pack4_e4m3(clamp448(acc[i + 12] / scale), clamp448(acc[i + 13] / scale),
-                         clamp448(acc[i + 14] / scale), clamp448(acc[i + 15] / scale));
+        w.x = pack4_e4m3(clamp448(acc[i + 0] * inv), clamp448(acc[i + 1] * inv), clamp448(acc[i + 2] * inv),
+                         clamp448(acc[i + 3] * inv));
+        w.y = pack4_e4m3(clamp448(acc[i + 4] * inv), clamp448(acc[i + 5] * inv), clamp448(acc[i + 6] * inv),
+                         clamp448(acc[i + 7] * inv));
+        w.z = pack4_e4m3(clamp448(acc[i + 8] * inv), clamp448(acc[i + 9] * inv), clamp448(acc[i + 10] * inv),
+                         clamp448(acc[i + 11] * inv));
+        w.w = pack4_e4m3(clamp448(acc[i + 12] * inv), clamp448(acc[i + 13] * inv), clamp448(acc[i + 14] * inv),
+                         clamp448(acc[i + 15] * inv));
         *reinterpret_cast<uint4*>(dst + i) = w;
       }
       if (h == 0) p.out_scale_t[static_cast<int64_t>(nt) * p.rows_cap + prow] = scale;
     } else {
-      if (valid && bvalid) {
-        const float w = p.topk_weights ? __ldg(p.topk_weights + pair) : 1.0f;
+      const bool cols_valid = 2 * nt + h < p.n_blocks;
+      if (valid && cols_valid) {
         __nv_bfloat16* dst = p.out_bf16 + static_cast<int64_t>(pair) * p.hidden + nt * BN + 128 * h;
 #pragma unroll
         for (int i = 0; i < 128; i += 8) {
           uint32_t u[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const __nv_bfloat162 v = __floats2bfloat162_rn(acc[i + 2 * j] * w, acc[i + 2 * j + 1] * w);
+            const __nv_bfloat162 v = __floats2bfloat162_rn(acc[i + 2 * j] * wrow, acc[i + 2 * j + 1] * wrow);
             u[j] = *reinterpret_cast<const uint32_t*>(&v);
           }
           *reinterpret_cast<uint4*>(dst + i) = make_uint4(u[0], u[1], u[2], u[3]);
@@ -331,6 +339,7 @@ __device__ __forceinline__ void epilogue_warps(const GemmParams& p, Control* C, 
       }
     }
     ++tiles_done;
+    tile = tile_after;
   }
 }
 
@@ -350,16 +359,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0 && blockIdx.x == 0) set_status(p.status, B2M_STATUS_BAD_ROUTING);
     num_mb = 0;
   }
-  const int64_t num_tiles = static_cast<int64_t>(num_mb) * p.num_nt;
+  const TileWalk tw{static_cast<int64_t>(num_mb) * p.num_nt, num_mb > 0 ? num_mb : 1};
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&C->full[s], 1);
-      mbar_init(&C->empty[s], 1);
+      mbar_init(&C->empty[s], 1 + NUM_EPI_WARPS);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&C->tfull[b], 1);
-      mbar_init(&C->tempty[b], NUM_EPI_THREADS / 32);
+      mbar_init(&C->tempty[b], NUM_EPI_WARPS);
       mbar_init(&C->amax_bar[b], NUM_EPI_THREADS);
     }
     mbar_init(&C->mma_done, 1);
@@ -377,16 +386,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem_base = C->tmem_base;
 
   if (warp < 4) {
-    reg_dealloc<56>();
+    reg_dealloc<72>();
     if (warp == 0) {
-      producer_warp<kGateUp>(&map_a, &map_b, p, smem, C, num_tiles, num_mb, lane);
+      stage_producer<kGateUp>(&map_a, &map_b, p, smem, C, tw, lane);
     } else if (warp == 1) {
-      if (lane == 0) mma_thread(p, smem, C, num_tiles, num_mb, tmem_base);
+      if (lane == 0) mma_thread(p, smem, C, tw, tmem_base);
       __syncwarp();
     }
   } else {
-    reg_alloc<224>();
-    epilogue_warps<kGateUp>(p, C, num_tiles, num_mb, tmem_base, warp, lane);
+    reg_alloc<216>();
+    epilogue_warps<kGateUp>(p, C, tw, tmem_base, warp, lane);
   }
 
   tc_fence_before();
@@ -444,49 +453,42 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& 
 }  // namespace
 }  // namespace b2m
 
-extern "C" int b2m_gemm1(const void* a_fp8, const float* a_scale, int64_t a_rows, int64_t hidden, const void* w1,
-                         const float* w1_scale, int32_t num_experts, int32_t inter, const int32_t* sorted_token_ids,
-                         const int32_t* expert_ids, const int32_t* num_tokens_post_padded, int64_t rows_cap,
-                         int64_t numel, int32_t top_k, void* out_q, float* out_scale_t, int32_t* dev_status,
-                         void* stream) {
+extern "C" int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden,
+                         const void* w1, const float* w1_scale, int32_t num_experts, int32_t inter,
+                         const int32_t* expert_ids, const int32_t* num_tokens_post_padded, void* out_q,
+                         float* out_scale_t, int32_t* dev_status, void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
-  if (hidden <= 0 || hidden % 128 || inter <= 0 || inter % 128 || num_experts <= 0 || top_k <= 0 || a_rows < 0 ||
-      rows_cap <= 0 || rows_cap % BM || numel < 0)
-    return fail(B2M_ERR_ARG,
-                "gemm1: need hidden%%128==0 (%lld), inter%%128==0 (%d), rows_cap%%128==0 (%lld), E>0, top_k>0",
+  if (hidden <= 0 || hidden % 128 || inter <= 0 || inter % 128 || num_experts <= 0 || rows_cap <= 0 ||
+      rows_cap % BM)
+    return fail(B2M_ERR_ARG, "gemm1: need hidden%%128==0 (%lld), inter%%128==0 (%d), rows_cap%%128==0 (%lld), E>0",
                 (long long)hidden, inter, (long long)rows_cap);
-  if (!a_fp8 || !a_scale || !w1 || !w1_scale || !sorted_token_ids || !expert_ids || !num_tokens_post_padded ||
-      !out_q || !out_scale_t)
+  if (!a_sorted || !a_scale_t || !w1 || !w1_scale || !expert_ids || !num_tokens_post_padded || !out_q ||
+      !out_scale_t)
     return fail(B2M_ERR_ARG, "gemm1: null pointer");
-  if (!aligned16(a_fp8) || !aligned16(w1) || !aligned16(out_q) || !aligned16(sorted_token_ids))
-    return fail(B2M_ERR_ARG, "gemm1: A, W1, out_q and sorted_token_ids must be 16-byte aligned");
-  if (rows_cap / BM > INT32_MAX || a_rows >= INT32_MAX || numel >= INT32_MAX)
-    return fail(B2M_ERR_ARG, "gemm1: sizes overflow int32 indices");
+  if (!aligned16(a_sorted) || !aligned16(a_scale_t) || !aligned16(w1) || !aligned16(out_q))
+    return fail(B2M_ERR_ARG, "gemm1: A, A scales, W1 and out_q must be 16-byte aligned");
+  if (rows_cap / BM > INT32_MAX) return fail(B2M_ERR_ARG, "gemm1: sizes overflow int32 indices");
   CUtensorMap ma, mb;
-  // A rows are gathered 4 at a time; the map spans a_rows rows (at least one so it is valid).
-  B2M_TRY(encode_map_2d(&ma, a_fp8, hidden, a_rows > 0 ? a_rows : 1, hidden, BK, 1));
+  B2M_TRY(encode_map_2d(&ma, a_sorted, hidden, rows_cap, hidden, BK, BM));
   B2M_TRY(encode_map_2d(&mb, w1, hidden, static_cast<uint64_t>(num_experts) * 2 * inter, hidden, BK, BN));
   GemmParams p{};
-  p.sorted_ids = sorted_token_ids;
   p.expert_ids = expert_ids;
   p.ntpp = num_tokens_post_padded;
   p.max_blocks = static_cast<int32_t>(rows_cap / BM);
-  p.numel = static_cast<int32_t>(numel);
-  p.top_k = top_k;
   p.num_kb = static_cast<int32_t>(hidden / BK);
   p.num_nt = inter / 128;
   p.n_blocks = 2 * inter / 128;
   p.n_rows = 2 * inter;
-  p.a_rows = static_cast<int32_t>(a_rows);
-  p.a_scale = a_scale;
-  p.a_scale_ld = hidden / 128;
+  p.a_scale = a_scale_t;
+  p.a_scale_ld = rows_cap;
   p.b_scale = w1_scale;
   p.rows_cap = rows_cap;
   p.out_q = static_cast<uint8_t*>(out_q);
   p.out_scale_t = out_scale_t;
   p.inter = inter;
+  p.hidden = hidden;
   p.status = dev_status;
   p.timeout_ns = timeout_ns();
   return launch_gemm<true>(ma, mb, p, num_sms, static_cast<cudaStream_t>(stream));
@@ -506,8 +508,8 @@ extern "C" int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows
   if (!a_fp8 || !a_scale_t || !w2 || !w2_scale || !sorted_token_ids || !expert_ids || !num_tokens_post_padded ||
       !out_bf16)
     return fail(B2M_ERR_ARG, "gemm2: null pointer");
-  if (!aligned16(a_fp8) || !aligned16(w2) || !aligned16(out_bf16))
-    return fail(B2M_ERR_ARG, "gemm2: A, W2 and out must be 16-byte aligned");
+  if (!aligned16(a_fp8) || !aligned16(a_scale_t) || !aligned16(w2) || !aligned16(out_bf16))
+    return fail(B2M_ERR_ARG, "gemm2: A, A scales, W2 and out must be 16-byte aligned");
   if (rows_cap / BM > INT32_MAX || numel >= INT32_MAX) return fail(B2M_ERR_ARG, "gemm2: sizes overflow int32");
   CUtensorMap ma, mb;
   B2M_TRY(encode_map_2d(&ma, a_fp8, inter, rows_cap, inter, BK, BM));
@@ -523,7 +525,6 @@ extern "C" int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows
   p.num_nt = static_cast<int32_t>((hidden + BN - 1) / BN);
   p.n_blocks = static_cast<int32_t>(hidden / 128);
   p.n_rows = static_cast<int32_t>(hidden);
-  p.a_rows = 0;
   p.a_scale = a_scale_t;
   p.a_scale_ld = rows_cap;
   p.b_scale = w2_scale;

@@ -6,8 +6,10 @@ forward is the path of the reference's scheme b2
 (``moe_bench/overlap/overlap_forward.py:348-622``) and its unfused twins a1/a2
 (``moe_bench/schemes/vllm_tp.py:50-64``, ``vllm_ep.py:53-71``):
 
-    quant(x_local) -> [all-gather] -> align(topk_ids) -> GEMM1(+SiLU*mul+requant)
-      -> GEMM2(*w) -> combine over top-k (+shared) -> [reduce-scatter]
+    align(topk_ids) -> quant(x_local) -> [all-gather] -> dispatch rows to expert order
+      -> GEMM1(+SiLU*mul+requant) -> GEMM2(*w) -> combine over top-k (+shared) -> [reduce-scatter]
+
+On one GPU the quant and the dispatch are one kernel (b2m_quant_dispatch).
 
 The exchange steps are pluggable (``Exchange``): ``NullExchange`` for one GPU,
 ``NcclExchange`` (torch.distributed all_gather_into_tensor / reduce_scatter_tensor,
@@ -63,14 +65,16 @@ class _Routing:
         self.sorted_ids = torch.empty(self.cap, dtype=torch.int32, device=device)
         self.expert_ids = torch.empty(self.nblk, dtype=torch.int32, device=device)
         self.ntpp = torch.empty(1, dtype=torch.int32, device=device)
+        self.pair_pos = torch.empty(numel, dtype=torch.int32, device=device)
 
 
 class SharedExpert:
     """Dense SwiGLU FFN on the same kernels (one expert, every token routed to it).
 
     Mirrors ``moe_bench/schemes/shared_expert.py`` (StaticSharedExpert): the
-    alignment (identity order) and all buffers are built once; a call takes the
-    already-quantised input (``shared_expert.py:91-102``) and returns bf16 [rows, H].
+    alignment (identity order) and all buffers are built once.  Its A operand is the
+    token-order codes of the already-quantised input (``shared_expert.py:91-102``:
+    an FP8 input is used directly with its scales); ``run`` returns bf16 [rows, H].
     """
 
     def __init__(self, weights: ExpertWeights, rows: int, device):
@@ -85,14 +89,22 @@ class SharedExpert:
         eids[:nb] = 0
         self.route.expert_ids.copy_(eids)
         self.route.ntpp.fill_(nb * BM)
+        self.route.pair_pos.copy_(torch.arange(rows, dtype=torch.int32))
+        H = weights.hidden
+        self.a = torch.empty((self.route.rows_cap, H), dtype=ops.FP8, device=device)
+        self.as_t = torch.empty((H // 128, self.route.rows_cap), dtype=torch.float32, device=device)
         self.inter_q = torch.empty((self.route.rows_cap, weights.inter), dtype=ops.FP8, device=device)
         self.inter_st = torch.empty((weights.inter // 128, self.route.rows_cap), dtype=torch.float32, device=device)
-        self.out = torch.empty((rows, weights.hidden), dtype=torch.bfloat16, device=device)
+        self.out = torch.empty((rows, H), dtype=torch.bfloat16, device=device)
 
-    def __call__(self, xq: torch.Tensor, xs: torch.Tensor, status: torch.Tensor | None) -> torch.Tensor:
+    def load_rows(self, xq: torch.Tensor, xs: torch.Tensor) -> None:
+        """Take quantised token rows (row-major scales) as this expert's A operand."""
+        ops.dispatch_rows(xq, xs, self.route.pair_pos, 1, self.a, self.as_t)
+
+    def run(self, status: torch.Tensor | None) -> torch.Tensor:
         r = self.route
-        ops.gemm1(xq, xs, self.w.w1i, self.w.w1i_scale, r.sorted_ids, r.expert_ids, r.ntpp, r.numel, 1, r.rows_cap,
-                  self.inter_q, self.inter_st, status)
+        ops.gemm1(self.a, self.as_t, self.w.w1i, self.w.w1i_scale, r.expert_ids, r.ntpp, self.inter_q, self.inter_st,
+                  status)
         ops.gemm2(self.inter_q, self.inter_st, self.w.w2, self.w.w2_scale, r.sorted_ids, r.expert_ids, r.ntpp,
                   r.numel, None, self.out, status)
         return self.out
@@ -163,8 +175,10 @@ class MoELayer:
         self.numel = tokens * top_k
         self.route = _Routing(self.numel, global_num_experts, dev)
         H = self.H
-        self.xq = torch.empty((tokens, H), dtype=ops.FP8, device=dev)
+        self.xq = torch.empty((tokens, H), dtype=ops.FP8, device=dev)          # token order (all-gather target)
         self.xs = torch.empty((tokens, H // 128), dtype=torch.float32, device=dev)
+        self.a_sorted = torch.empty((self.route.rows_cap, H), dtype=ops.FP8, device=dev)  # expert order
+        self.as_t = torch.empty((H // 128, self.route.rows_cap), dtype=torch.float32, device=dev)
         self.inter_q = torch.empty((self.route.rows_cap, weights.inter), dtype=ops.FP8, device=dev)
         self.inter_st = torch.empty((weights.inter // 128, self.route.rows_cap), dtype=torch.float32, device=dev)
         self.staged = torch.empty((self.numel, H), dtype=torch.bfloat16, device=dev)
@@ -179,47 +193,62 @@ class MoELayer:
             self.shared = SharedExpert(shared, rows, dev)
 
     # -- stages (exposed for tests and staged timing)
-    def quant_and_gather(self, x_local: torch.Tensor) -> None:
-        if self.P == 1:
-            ops.quant_g128(x_local, self.xq, self.xs)
-            return
-        r0 = self.exchange.rank * self.T_local
-        xq_l = self.xq[r0:r0 + self.T_local]
-        xs_l = self.xs[r0:r0 + self.T_local]
-        ops.quant_g128(x_local, xq_l, xs_l)
-        self.exchange.all_gather(xq_l, xs_l, self.xq, self.xs)
-
     def _event(self, name: str) -> None:
         if self.events is not None:
             ev = torch.cuda.Event(enable_timing=True)
             ev.record(torch.cuda.current_stream(self.device))
             self.events.append((name, ev))
 
-    def experts(self, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> None:
+    def route_and_dispatch(self, x_local: torch.Tensor, topk_ids: torch.Tensor) -> None:
+        """Alignment, quantisation, (all-gather) and the row dispatch into expert order."""
         r = self.route
-        ops.moe_align_block_size(topk_ids, BM, self.E, self.expert_map, out=(r.sorted_ids, r.expert_ids, r.ntpp))
+        ops.moe_align_block_size(topk_ids, BM, self.E, self.expert_map, out=(r.sorted_ids, r.expert_ids, r.ntpp),
+                                 pair_pos=r.pair_pos)
+        if self.P == 1:
+            sh = self.shared
+            ops.quant_dispatch(x_local, r.pair_pos, self.top_k, self.a_sorted, self.as_t,
+                               None if sh is None else sh.a, None if sh is None else sh.as_t)
+            return
+        r0 = self.exchange.rank * self.T_local
+        xq_l = self.xq[r0:r0 + self.T_local]
+        xs_l = self.xs[r0:r0 + self.T_local]
+        ops.quant_g128(x_local, xq_l, xs_l)
+        if self.shared is not None and self.ep:
+            self.shared.load_rows(xq_l, xs_l)
+        self.exchange.all_gather(xq_l, xs_l, self.xq, self.xs)
+        ops.dispatch_rows(self.xq, self.xs, r.pair_pos, self.top_k, self.a_sorted, self.as_t)
+        if self.shared is not None and not self.ep:
+            self.shared.load_rows(self.xq, self.xs)
+
+    def experts(self, topk_weights: torch.Tensor) -> None:
+        r = self.route
         self._event("gemm1_start")
-        ops.gemm1(self.xq, self.xs, self.w.w1i, self.w.w1i_scale, r.sorted_ids, r.expert_ids, r.ntpp, self.numel,
-                  self.top_k, r.rows_cap, self.inter_q, self.inter_st, self.status)
+        ops.gemm1(self.a_sorted, self.as_t, self.w.w1i, self.w.w1i_scale, r.expert_ids, r.ntpp, self.inter_q,
+                  self.inter_st, self.status)
         self._event("gemm1_end")
         ops.gemm2(self.inter_q, self.inter_st, self.w.w2, self.w.w2_scale, r.sorted_ids, r.expert_ids, r.ntpp,
                   self.numel, topk_weights.reshape(-1), self.staged, self.status)
         self._event("gemm2_end")
 
     def kernel_launches(self) -> int:
-        """b2m kernels one forward launches (quant, align, GEMM1, GEMM2, combine, shared expert)."""
-        n = 5
-        if self.shared is not None:
-            n += 2 + (1 if self.ep else 0)
+        """b2m kernels one forward launches."""
+        if self.P == 1:
+            n = 5                       # align, quant+dispatch, GEMM1, GEMM2, combine
+            if self.shared is not None:
+                n += 2                  # shared GEMM1/GEMM2 (its A comes from the same quant pass)
+        else:
+            n = 6                       # align, quant, dispatch, GEMM1, GEMM2, combine
+            if self.shared is not None:
+                n += 3 + (1 if self.ep else 0)
         return n
 
     def forward(self, x_local: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
         """x_local bf16 [T/P, H]; topk_ids int32 / topk_weights fp32 [T, k] (all tokens) -> bf16 [T/P, H]."""
-        self.quant_and_gather(x_local)
-        self.experts(topk_ids, topk_weights)
+        self.route_and_dispatch(x_local, topk_ids)
+        self.experts(topk_weights)
         shared_out = None
         if self.shared is not None and not self.ep:
-            shared_out = self.shared(self.xq, self.xs, self.status)
+            shared_out = self.shared.run(self.status)
         ids = topk_ids if self.ep else None
         if self.P == 1 and not (self.ep and self.shared is not None):
             return ops.combine(self.staged, self.top_k, ids, self.expert_map, shared_out, self.out_local)
@@ -229,8 +258,7 @@ class MoELayer:
         else:
             self.exchange.reduce_scatter(self.partial, self.out_local)
         if self.shared is not None and self.ep:
-            r0 = self.exchange.rank * self.T_local
-            sh = self.shared(self.xq[r0:r0 + self.T_local], self.xs[r0:r0 + self.T_local], self.status)
+            sh = self.shared.run(self.status)
             ops.combine(self.out_local, 1, None, None, sh, self.out_local)
         return self.out_local
 

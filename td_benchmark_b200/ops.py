@@ -67,6 +67,52 @@ def quant_g128(x: torch.Tensor, q: torch.Tensor | None = None, scale: torch.Tens
     return q, scale
 
 
+def quant_g128_t(x: torch.Tensor, q: torch.Tensor, scale_t: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [rows, cols] -> e4m3 q [rows, cols] and K-block-major fp32 scale_t [cols/128, >= rows]."""
+    _cuda(x, "x")
+    _need(x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1, "x must be 2D bf16 with unit column stride")
+    rows, cols = x.shape
+    _need(scale_t.shape[0] == (cols + BLOCK - 1) // BLOCK and scale_t.shape[1] >= rows and scale_t.stride(1) == 1,
+          "scale_t must be [cols/128, >= rows]")
+    _lib.call("b2m_quant_g128_t", x.data_ptr(), rows, cols, x.stride(0), q.data_ptr(), q.stride(0),
+              scale_t.data_ptr(), scale_t.stride(0), _stream(x.device))
+    return q, scale_t
+
+
+def quant_dispatch(x: torch.Tensor, pair_pos: torch.Tensor, top_k: int, a_sorted: torch.Tensor,
+                   a_scale_t: torch.Tensor, q_tok: torch.Tensor | None = None,
+                   scale_tok_t: torch.Tensor | None = None) -> None:
+    """Quantise bf16 tokens and write codes/scales to the sorted rows of their pairs (+ optional token order)."""
+    _cuda(x, "x")
+    tokens, hidden = x.shape
+    rows_cap = a_sorted.shape[0]
+    _need(x.dtype == torch.bfloat16 and x.stride(1) == 1, "x must be bf16 with unit column stride")
+    _need(pair_pos.dtype == torch.int32 and pair_pos.numel() == tokens * top_k, "pair_pos must be int32 [T*k]")
+    _need(a_sorted.shape[1] == hidden and tuple(a_scale_t.shape) == (hidden // BLOCK, rows_cap),
+          "a_sorted [rows_cap, H] / a_scale_t [H/128, rows_cap] mismatch")
+    ld_tok = 0
+    if q_tok is not None:
+        _need(q_tok.shape[1] == hidden and q_tok.shape[0] >= tokens and scale_tok_t.shape[1] >= tokens,
+              "bad token-order outputs")
+        ld_tok = scale_tok_t.stride(0)
+    _lib.call("b2m_quant_dispatch", x.data_ptr(), tokens, hidden, x.stride(0), pair_pos.data_ptr(), top_k,
+              a_sorted.data_ptr(), a_scale_t.data_ptr(), rows_cap, _ptr(q_tok), _ptr(scale_tok_t), ld_tok,
+              _stream(x.device))
+
+
+def dispatch_rows(xq: torch.Tensor, xs: torch.Tensor, pair_pos: torch.Tensor, top_k: int, a_sorted: torch.Tensor,
+                  a_scale_t: torch.Tensor) -> None:
+    """Quantised token rows (+ row-major scales) -> sorted rows of their pairs."""
+    _cuda(xq, "xq")
+    tokens, hidden = xq.shape
+    rows_cap = a_sorted.shape[0]
+    _need(xq.is_contiguous() and xs.is_contiguous() and tuple(xs.shape) == (tokens, hidden // BLOCK),
+          "xq / xs must be contiguous [T, H] / [T, H/128]")
+    _need(pair_pos.dtype == torch.int32 and pair_pos.numel() == tokens * top_k, "pair_pos must be int32 [T*k]")
+    _lib.call("b2m_dispatch_rows", xq.data_ptr(), xs.data_ptr(), tokens, hidden, pair_pos.data_ptr(), top_k,
+              a_sorted.data_ptr(), a_scale_t.data_ptr(), rows_cap, _stream(xq.device))
+
+
 def align_sizes(numel: int, num_experts: int, block_size: int) -> tuple[int, int]:
     """Buffer sizes of moe_align_block_size (vLLM moe_align_block_size.py:74-88)."""
     max_padded = numel + num_experts * (block_size - 1)
@@ -77,9 +123,12 @@ def align_sizes(numel: int, num_experts: int, block_size: int) -> tuple[int, int
 
 def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int,
                          expert_map: torch.Tensor | None = None,
-                         out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None
+                         out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None,
+                         pair_pos: torch.Tensor | None = None
                          ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Same signature and outputs as vLLM's ``moe_align_block_size`` (without the padding flags)."""
+    """Same signature and outputs as vLLM's ``moe_align_block_size`` (without the padding flags).
+
+    ``pair_pos`` (int32 [numel], optional) also receives each pair's sorted position (-1: non-local)."""
     _cuda(topk_ids, "topk_ids")
     _need(topk_ids.dtype == torch.int32 and topk_ids.is_contiguous(), "topk_ids must be contiguous int32")
     numel = topk_ids.numel()
@@ -92,9 +141,11 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: i
         sorted_ids, expert_ids, ntpp = out
     if expert_map is not None:
         _need(expert_map.dtype == torch.int32 and expert_map.numel() >= num_experts, "expert_map must be int32 [E]")
+    if pair_pos is not None:
+        _need(pair_pos.dtype == torch.int32 and pair_pos.numel() == numel, "pair_pos must be int32 [numel]")
     _lib.call("b2m_align", topk_ids.data_ptr(), numel, num_experts, block_size, _ptr(expert_map),
               sorted_ids.data_ptr(), sorted_ids.numel(), expert_ids.data_ptr(), expert_ids.numel(),
-              ntpp.data_ptr(), _stream(topk_ids.device))
+              ntpp.data_ptr(), _ptr(pair_pos), _stream(topk_ids.device))
     return sorted_ids, expert_ids, ntpp
 
 
@@ -112,25 +163,28 @@ def w1_interleave(w1: torch.Tensor, w1_scale: torch.Tensor) -> tuple[torch.Tenso
     return out, out_s
 
 
-def gemm1(a_q: torch.Tensor, a_scale: torch.Tensor, w1i: torch.Tensor, w1i_scale: torch.Tensor,
-          sorted_ids: torch.Tensor, expert_ids: torch.Tensor, ntpp: torch.Tensor, numel: int, top_k: int,
-          rows_cap: int, out_q: torch.Tensor | None = None, out_scale_t: torch.Tensor | None = None,
-          status: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-    """Gate/up grouped GEMM + SiLU*mul + 1x128 requant.  Returns (q [rows_cap, I], scale_t [I/128, rows_cap])."""
-    _cuda(a_q, "a_q")
-    a_rows, hidden = a_q.shape
+def gemm1(a_sorted: torch.Tensor, a_scale_t: torch.Tensor, w1i: torch.Tensor, w1i_scale: torch.Tensor,
+          expert_ids: torch.Tensor, ntpp: torch.Tensor, out_q: torch.Tensor | None = None,
+          out_scale_t: torch.Tensor | None = None, status: torch.Tensor | None = None
+          ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gate/up grouped GEMM + SiLU*mul + 1x128 requant on expert-sorted A.
+
+    a_sorted e4m3 [rows_cap, H], a_scale_t fp32 [H/128, rows_cap] -> (q [rows_cap, I], scale_t [I/128, rows_cap])."""
+    _cuda(a_sorted, "a_sorted")
+    rows_cap, hidden = a_sorted.shape
     e, n2, h2 = w1i.shape
     inter = n2 // 2
-    _need(h2 == hidden and a_q.is_contiguous() and w1i.is_contiguous(), "A / W1 shape mismatch")
-    _need(a_scale.is_contiguous() and tuple(a_scale.shape) == (a_rows, hidden // 128), "a_scale must be [rows, H/128]")
+    _need(h2 == hidden and a_sorted.is_contiguous() and w1i.is_contiguous(), "A / W1 shape mismatch")
+    _need(a_scale_t.is_contiguous() and tuple(a_scale_t.shape) == (hidden // 128, rows_cap),
+          "a_scale_t must be [H/128, rows_cap]")
     _need(expert_ids.numel() * 128 >= rows_cap, "expert_ids shorter than rows_cap/128")
     if out_q is None:
-        out_q = torch.empty((rows_cap, inter), dtype=FP8, device=a_q.device)
+        out_q = torch.empty((rows_cap, inter), dtype=FP8, device=a_sorted.device)
     if out_scale_t is None:
-        out_scale_t = torch.empty((inter // 128, rows_cap), dtype=torch.float32, device=a_q.device)
-    _lib.call("b2m_gemm1", a_q.data_ptr(), a_scale.data_ptr(), a_rows, hidden, w1i.data_ptr(), w1i_scale.data_ptr(),
-              e, inter, sorted_ids.data_ptr(), expert_ids.data_ptr(), ntpp.data_ptr(), rows_cap, numel, top_k,
-              out_q.data_ptr(), out_scale_t.data_ptr(), _ptr(status), _stream(a_q.device))
+        out_scale_t = torch.empty((inter // 128, rows_cap), dtype=torch.float32, device=a_sorted.device)
+    _lib.call("b2m_gemm1", a_sorted.data_ptr(), a_scale_t.data_ptr(), rows_cap, hidden, w1i.data_ptr(),
+              w1i_scale.data_ptr(), e, inter, expert_ids.data_ptr(), ntpp.data_ptr(), out_q.data_ptr(),
+              out_scale_t.data_ptr(), _ptr(status), _stream(a_sorted.device))
     return out_q, out_scale_t
 
 
