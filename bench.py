@@ -37,12 +37,15 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 WORKLOADS = {
-    # name: (preset, scheme code, human label)
-    "mixtral": ("mixtral", "d1", "mixtral-8x7b-moe-layer TP"),
-    "dsv3": ("dsv3", "d2", "deepseek-v3-moe-layer EP (+shared)"),
-    "qwen3": ("qwen3", "d1", "qwen3-30b-a3b-moe-layer TP decode"),
-    "tiny": ("tiny", "d1", "tiny-moe-layer"),
+    # name: (preset, human label)
+    "mixtral": ("mixtral", "mixtral-8x7b-moe-layer TP"),
+    "dsv3": ("dsv3", "deepseek-v3-moe-layer EP (+shared)"),
+    "qwen3": ("qwen3", "qwen3-30b-a3b-moe-layer TP decode"),
+    "tiny": ("tiny", "tiny-moe-layer"),
 }
+# scheme code by (parallelism, exchange): d3/d4 fuse the all-gather / reduce-scatter
+# through peer memory; d1/d2 are the unfused NCCL comparison (identical at N=1).
+SCHEME = {("TP", "p2p"): "d3", ("EP", "p2p"): "d4", ("TP", "nccl"): "d1", ("EP", "nccl"): "d2"}
 
 
 def _peaks() -> dict:
@@ -183,7 +186,7 @@ def run_reference(args) -> int:
 
     if int(os.environ.get("RANK", "0")) != 0:
         return 0
-    preset, _, label = WORKLOADS[args.workload]
+    preset, label = WORKLOADS[args.workload]
     over = {"M": args.tokens} if args.tokens else {}
     cfg = configs.preset(preset, **over)
     dev = "cuda" if torch.cuda.is_available() else "cpu"
@@ -215,6 +218,8 @@ def main() -> int:
     ap.add_argument("--workload", default="mixtral", choices=sorted(WORKLOADS))
     ap.add_argument("--tokens", type=int, default=None, help="override the workload's token count")
     ap.add_argument("--impl", default="b2m", choices=["b2m", "reference"])
+    ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"],
+                    help="exchange of the multi-GPU layer: fused peer memory (default) or NCCL")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -233,9 +238,10 @@ def main() -> int:
     ctx = init_context(backend="nccl", timeout_s=300.0)
     world, rank = ctx.world_size, ctx.rank
     dev = ctx.device
-    preset, code, label = WORKLOADS[args.workload]
+    preset, label = WORKLOADS[args.workload]
     over = {"M": args.tokens} if args.tokens else {}
     cfg = configs.preset(preset, **over)
+    code = SCHEME[(cfg.parallel, args.comm)]
     spec = REGISTRY[code][0]
     bundle = data.build_bundle(cfg, rank=rank, world_size=world, device=dev)
     layer, level = build_layer(spec, cfg, ctx, bundle)
@@ -360,6 +366,7 @@ def main() -> int:
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    layer.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

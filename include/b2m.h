@@ -167,6 +167,53 @@ int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int32
 int b2m_combine(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, const int32_t* topk_ids,
                 const int32_t* expert_map, const void* shared, void* out, int64_t ld_out, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Peer-memory exchange (fused all-gather / reduce-scatter over NVLink).
+ * Replaces the NCCL all_gather_into_tensor of FP8 bytes + scales
+ * (moe_bench/overlap/overlap_forward.py:494-505) and reduce_scatter_tensor
+ * (:603-608).  Symmetric buffers are cudaMalloc blocks shared by CUDA IPC; flags
+ * are uint32 epochs (only grow) published with system-scope release stores and
+ * read with bounded acquire spins (timeout -> B2M_STATUS_TIMEOUT_PEER). */
+
+/* Set-up only: zeroed device allocation / free for symmetric buffers. */
+int b2m_symm_alloc(int64_t bytes, void** dev_ptr);
+int b2m_symm_free(void* dev_ptr);
+/* CUDA IPC: handle_out / handle are 64-byte host buffers. */
+int b2m_ipc_handle(void* dev_ptr, void* handle_out);
+int b2m_ipc_open(const void* handle, void** peer_ptr);
+int b2m_ipc_close(void* peer_ptr);
+
+/* All-gather push: quantise x [rows, hidden] (rule of K1) and store codes / scales
+ * into rows [row0, row0+rows) of every rank's gather buffers q_dst[r] (e4m3
+ * [T, hidden]) and s_dst[r] (fp32 [T, hidden/128]); then publish
+ * *flag_dst[r] = epoch (flag_dst[r] = this source's flag on rank r).  q_dst, s_dst,
+ * flag_dst are host arrays of `world` device pointers (own and peer).  counter: a
+ * device int32, zero before the first call, left zero by every call. */
+int b2m_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world, void* const* q_dst,
+                   void* const* s_dst, int64_t row0, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
+                   void* stream);
+
+/* b2m_dispatch_rows on the gather buffer, reading source rank s's rows
+ * (tokens [s*T/world, (s+1)*T/world)) only once flags[s] >= epoch (own rank first).
+ * top_k <= 8. */
+int b2m_dispatch_rows_wait(const void* xq, const float* xs, int64_t tokens, int64_t hidden, const int32_t* pair_pos,
+                           int32_t top_k, void* a_sorted, float* a_scale_t, int64_t rows_cap, const uint32_t* flags,
+                           int32_t world, int32_t rank, uint32_t epoch, int32_t* dev_status, void* stream);
+
+/* Reduce-scatter push: the combine of b2m_combine over all T tokens; token t's bf16
+ * partial row goes to owner q = t / (T/world), row rank*(T/world) + t - q*(T/world)
+ * of slot_dst[q] (bf16 [world*T/world, hidden] on rank q); then *flag_dst[q] = epoch. */
+int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, const int32_t* topk_ids,
+                     const int32_t* expert_map, const void* shared, int32_t world, int32_t rank,
+                     void* const* slot_dst, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
+                     void* stream);
+
+/* Owner side of the reduce-scatter: once flags[0..world) >= epoch,
+ * out[t, :] = bf16( sum_{r=0..world-1} slots[r*rows + t, :] + add[t, :] )  (fp32, rank order).
+ * add (bf16 [rows, hidden]) may be NULL. */
+int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world, const uint32_t* flags,
+                  uint32_t epoch, const void* add, void* out, int32_t* dev_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -227,6 +227,33 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// ------------------------------------------------------------------ system-scope flags (peer memory)
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// Bounded wait until *flag >= epoch (epochs only grow).  Returns false on timeout
+// after recording `code` in the status word.
+__device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t epoch, uint64_t timeout_ns,
+                                              int32_t* status, int32_t code) {
+  if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+  const uint64_t t0 = globaltimer();
+  while (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) < 0) {
+    if (globaltimer() - t0 > timeout_ns) {
+      set_status(status, code);
+      return false;
+    }
+    __nanosleep(128);
+  }
+  return true;
+}
+
 // ------------------------------------------------------------------ misc
 template <uint32_t N>
 __device__ __forceinline__ void reg_alloc() {
@@ -254,5 +281,38 @@ __device__ __forceinline__ uint32_t pack4_e4m3(float v0, float v1, float v2, flo
 }
 
 __device__ __forceinline__ float clamp448(float v) { return fminf(fmaxf(v, -448.0f), 448.0f); }
+
+// ------------------------------------------------------------------ group-128 quant pieces
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// Eight values of one 128-group held by a half-warp lane: IEEE division by the
+// group scale, clamp, e4m3 RNE (moe_bench/verify.py:115-116).
+__device__ __forceinline__ uint2 quant8(const float (&f)[8], float scale) {
+  uint2 r = make_uint2(0, 0);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    r.x |= static_cast<uint32_t>(f32_to_e4m3(clamp448(f[i] / scale))) << (8 * i);
+    r.y |= static_cast<uint32_t>(f32_to_e4m3(clamp448(f[4 + i] / scale))) << (8 * i);
+  }
+  return r;
+}
+
+// amax of a 128-group spread over the 16 lanes of a half-warp (8 values each).
+__device__ __forceinline__ float halfwarp_amax(const float (&f)[8]) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+#pragma unroll
+  for (int off = 8; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  return amax;
+}
+
 
 }  // namespace b2m

@@ -30,22 +30,6 @@ struct Dispatch {
   int64_t rows_cap;
 };
 
-__device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __uint_as_float(w[i] << 16);
-    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-  }
-}
-
-__device__ __forceinline__ uint32_t quant4(const float* f, float scale) {
-  uint32_t r = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) r |= static_cast<uint32_t>(f32_to_e4m3(clamp448(f[i] / scale))) << (8 * i);
-  return r;
-}
-
 // groups = rows * (cols/128); group g covers row g / gpr, columns (g % gpr)*128 ...
 // q / scale (token order) may be null when only the dispatched copy is wanted.
 __global__ void __launch_bounds__(kQuantThreads)
@@ -76,18 +60,11 @@ __global__ void __launch_bounds__(kQuantThreads)
     for (int u = 0; u < 2; ++u) {
       float f[8];
       bf16x8_to_f32(raw[u], f);
-      float amax = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
-#pragma unroll
-      for (int off = 8; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-      const float s = fmaxf(amax / 448.0f, 1e-12f);
+      const float s = fmaxf(halfwarp_amax(f) / 448.0f, 1e-12f);
       if (g[u] < groups) {
         const int64_t row = g[u] / gpr;
         const int64_t gi = g[u] - row * gpr;
-        uint2 out;
-        out.x = quant4(f, s);
-        out.y = quant4(f + 4, s);
+        const uint2 out = quant8(f, s);
         if (q) *reinterpret_cast<uint2*>(q + row * ldq + gi * 128 + hl * 8) = out;
         if (scale && hl == 0) scale[row * s_row + gi * s_col] = s;
         if (d.pair_pos) {

@@ -1,0 +1,340 @@
+// Peer-memory exchange: the fused all-gather and reduce-scatter of the MoE layer.
+//
+// The reference moves activations with NCCL all_gather_into_tensor (FP8 bytes +
+// fp32 scales, moe_bench/overlap/overlap_forward.py:494-505) and partial outputs
+// with reduce_scatter_tensor (:603-608).  Over NVSwitch every peer is one hop away,
+// so here each rank writes straight into its peers' memory:
+//
+//  all-gather   b2m_quant_push quantises the rank's tokens and stores the codes and
+//               scales into the same rows of every rank's gather buffer (16-byte P2P
+//               stores); the last CTA to finish publishes ag_flag[src] = epoch on every
+//               rank (system-scope release).  b2m_dispatch_rows_wait then moves rows
+//               into expert order, reading a source rank's rows only after its flag
+//               (own rows first, bounded acquire spin per source).
+//  reduce-scatter  b2m_combine_push sums each token's top-k rows (+ shared expert) and
+//               stores the bf16 partial row into the owning rank's slot for this source;
+//               the last CTA publishes rs_flag[src] = epoch on every owner.
+//               b2m_rs_reduce waits for all sources and sums the slots in rank order
+//               (deterministic, fp32, one rounding).
+//
+// Epochs only grow, so flags are never reset.  Buffers need no extra barrier between
+// calls: a rank starts call i+1 only after its reduce of call i saw every peer's
+// combine of call i, and a peer runs that combine only after it finished reading the
+// gather buffer of call i (stream order); symmetrically for the slots.
+//
+// Symmetric buffers are plain cudaMalloc blocks shared through CUDA IPC handles.
+#include "b2m_common.cuh"
+#include "b2m_host.h"
+
+#include <string.h>
+
+namespace b2m {
+namespace {
+
+constexpr int kMaxWorld = 8;
+constexpr int kThreads = 256;
+
+struct PeerPtrs {
+  void* p[kMaxWorld];
+};
+struct FlagPtrs {
+  uint32_t* p[kMaxWorld];
+};
+
+// Every thread fences its own peer stores, the CTA syncs, and the last CTA of the
+// grid publishes `epoch` to every flag (then re-arms the counter for the next launch).
+__device__ __forceinline__ void publish_when_grid_done(int32_t* counter, const FlagPtrs& flags, int world,
+                                                       uint32_t epoch) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(counter, 1);
+    if (prev == static_cast<int>(gridDim.x) - 1) {
+      fence_sys();
+      for (int r = 0; r < world; ++r) st_release_sys(flags.p[r], epoch);
+      atomicExch(counter, 0);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- all-gather push
+__global__ void __launch_bounds__(kThreads)
+    quant_push_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t rows, int64_t gpr, int world,
+                      PeerPtrs qdst, PeerPtrs sdst, int64_t row0, FlagPtrs flags, uint32_t epoch, int32_t* counter) {
+  const int lane = threadIdx.x & 31;
+  const int half = lane >> 4;
+  const int hl = lane & 15;
+  const int64_t cols = gpr * 128;
+  const int64_t groups = rows * gpr;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
+  for (int64_t base = warp * 2; base < groups; base += nwarps * 2) {
+    const int64_t g = base + half;
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    int64_t row = 0, gi = 0;
+    if (g < groups) {
+      row = g / gpr;
+      gi = g - row * gpr;
+      raw = __ldg(reinterpret_cast<const uint4*>(x + row * ldx + gi * 128 + hl * 8));
+    }
+    float f[8];
+    bf16x8_to_f32(raw, f);
+    const float s = fmaxf(halfwarp_amax(f) / 448.0f, 1e-12f);
+    if (g < groups) {
+      const uint2 q = quant8(f, s);
+      const int64_t dst_row = row0 + row;
+      for (int r = 0; r < world; ++r) {
+        *reinterpret_cast<uint2*>(static_cast<uint8_t*>(qdst.p[r]) + dst_row * cols + gi * 128 + hl * 8) = q;
+        if (hl == 0) static_cast<float*>(sdst.p[r])[dst_row * gpr + gi] = s;
+      }
+    }
+  }
+  publish_when_grid_done(counter, flags, world, epoch);
+}
+
+// ---------------------------------------------------------------- dispatch with arrival waits
+// One warp per token row.  Tokens are visited starting at this rank's own rows.
+__global__ void __launch_bounds__(kThreads)
+    dispatch_wait_kernel(const uint8_t* __restrict__ xq, const float* __restrict__ xs, int64_t tokens, int64_t cols,
+                         const int32_t* __restrict__ pair_pos, int top_k, uint8_t* __restrict__ a_sorted,
+                         float* __restrict__ as_t, int64_t rows_cap, const uint32_t* flags, int world, int rank,
+                         uint32_t epoch, int32_t* status, uint64_t timeout_ns) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
+  const int64_t per_rank = tokens / world;
+  const int64_t vec = cols / 16;
+  const int64_t kb = cols / 128;
+  uint32_t ready = 0;  // bit r: rank r's rows have arrived (for this warp)
+  bool ok = true;
+  for (int64_t i = warp; i < tokens && ok; i += nwarps) {
+    const int64_t t = (i + static_cast<int64_t>(rank) * per_rank) % tokens;
+    const int src = static_cast<int>(t / per_rank);
+    if (!(ready & (1u << src))) {
+      int good = 1;
+      if (lane == 0) good = wait_flag_geq(flags + src, epoch, timeout_ns, status, B2M_STATUS_TIMEOUT_PEER);
+      good = __shfl_sync(0xffffffffu, good, 0);
+      __syncwarp();  // lane 0's acquire orders the other lanes' reads of this source's rows
+      if (!good) {
+        ok = false;
+        break;
+      }
+      ready |= 1u << src;
+    }
+    int32_t pos[8];
+    for (int j = 0; j < top_k && j < 8; ++j) pos[j] = __ldg(pair_pos + t * top_k + j);
+    for (int64_t c = lane; c < vec; c += 32) {
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(xq + t * cols + c * 16));
+      for (int j = 0; j < top_k && j < 8; ++j)
+        if (pos[j] >= 0) reinterpret_cast<uint4*>(a_sorted + pos[j] * cols)[c] = v;
+    }
+    for (int64_t g = lane; g < kb; g += 32) {
+      const float sv = __ldcg(xs + t * kb + g);
+      for (int j = 0; j < top_k && j < 8; ++j)
+        if (pos[j] >= 0) as_t[g * rows_cap + pos[j]] = sv;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- reduce-scatter push
+__device__ __forceinline__ void acc_bf16x8(const uint4& u, float (&a)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    a[2 * i] += __uint_as_float(w[i] << 16);
+    a[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float (&a)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a[2 * i], a[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__global__ void __launch_bounds__(kThreads)
+    combine_push_kernel(const __nv_bfloat16* __restrict__ staged, int64_t tokens, int top_k, int64_t hidden,
+                        const int32_t* __restrict__ topk_ids, const int32_t* __restrict__ expert_map,
+                        const __nv_bfloat16* __restrict__ shared, int world, int rank, PeerPtrs slots, FlagPtrs flags,
+                        uint32_t epoch, int32_t* counter) {
+  const int64_t vec = hidden / 8;
+  const int64_t per_rank = tokens / world;
+  const int64_t total = tokens * vec;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t t = v / vec;
+    const int64_t c = (v - t * vec) * 8;
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = 0; j < top_k; ++j) {
+      const int64_t pair = t * top_k + j;
+      if (expert_map && __ldg(expert_map + __ldg(topk_ids + pair)) < 0) continue;
+      acc_bf16x8(__ldg(reinterpret_cast<const uint4*>(staged + pair * hidden + c)), a);
+    }
+    if (shared) acc_bf16x8(__ldg(reinterpret_cast<const uint4*>(shared + t * hidden + c)), a);
+    const int owner = static_cast<int>(t / per_rank);
+    const int64_t slot_row = static_cast<int64_t>(rank) * per_rank + (t - owner * per_rank);
+    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(slots.p[owner]) + slot_row * hidden + c) = pack_bf16x8(a);
+  }
+  publish_when_grid_done(counter, flags, world, epoch);
+}
+
+__global__ void __launch_bounds__(kThreads)
+    rs_reduce_kernel(const __nv_bfloat16* __restrict__ slots, int64_t rows, int64_t hidden, int world,
+                     const uint32_t* flags, uint32_t epoch, const __nv_bfloat16* __restrict__ add,
+                     __nv_bfloat16* __restrict__ out, int32_t* status, uint64_t timeout_ns) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if (threadIdx.x < world && !wait_flag_geq(flags + threadIdx.x, epoch, timeout_ns, status, B2M_STATUS_TIMEOUT_PEER))
+    s_ok = 0;
+  __syncthreads();
+  if (!s_ok) return;  // status already records the timeout
+  const int64_t vec = hidden / 8;
+  const int64_t total = rows * vec;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t t = v / vec;
+    const int64_t c = (v - t * vec) * 8;
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int r = 0; r < world; ++r)
+      acc_bf16x8(__ldcg(reinterpret_cast<const uint4*>(slots + (static_cast<int64_t>(r) * rows + t) * hidden + c)), a);
+    if (add) acc_bf16x8(*reinterpret_cast<const uint4*>(add + t * hidden + c), a);
+    *reinterpret_cast<uint4*>(out + t * hidden + c) = pack_bf16x8(a);
+  }
+}
+
+int grid_for(int64_t work, int num_sms, int per_sm) {
+  int64_t b = (work + kThreads - 1) / kThreads;
+  if (b > int64_t(num_sms) * per_sm) b = int64_t(num_sms) * per_sm;
+  return static_cast<int>(b < 1 ? 1 : b);
+}
+
+}  // namespace
+}  // namespace b2m
+
+extern "C" {
+
+int b2m_symm_alloc(int64_t bytes, void** dev_ptr) {
+  using namespace b2m;
+  if (bytes <= 0 || !dev_ptr) return fail(B2M_ERR_ARG, "symm_alloc: bad arguments");
+  B2M_TRY(check_cuda(cudaMalloc(dev_ptr, static_cast<size_t>(bytes)), "symm_alloc: cudaMalloc"));
+  return check_cuda(cudaMemset(*dev_ptr, 0, static_cast<size_t>(bytes)), "symm_alloc: cudaMemset");
+}
+
+int b2m_symm_free(void* dev_ptr) {
+  using namespace b2m;
+  if (!dev_ptr) return B2M_OK;
+  return check_cuda(cudaFree(dev_ptr), "symm_free: cudaFree");
+}
+
+int b2m_ipc_handle(void* dev_ptr, void* handle_out) {
+  using namespace b2m;
+  if (!dev_ptr || !handle_out) return fail(B2M_ERR_ARG, "ipc_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  B2M_TRY(check_cuda(cudaIpcGetMemHandle(&h, dev_ptr), "cudaIpcGetMemHandle"));
+  memcpy(handle_out, &h, sizeof(h));
+  return B2M_OK;
+}
+
+int b2m_ipc_open(const void* handle, void** peer_ptr) {
+  using namespace b2m;
+  if (!handle || !peer_ptr) return fail(B2M_ERR_ARG, "ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return check_cuda(cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+int b2m_ipc_close(void* peer_ptr) {
+  using namespace b2m;
+  if (!peer_ptr) return B2M_OK;
+  return check_cuda(cudaIpcCloseMemHandle(peer_ptr), "cudaIpcCloseMemHandle");
+}
+
+int b2m_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world, void* const* q_dst,
+                   void* const* s_dst, int64_t row0, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
+                   void* stream) {
+  using namespace b2m;
+  int num_sms = 0;
+  B2M_TRY(require_sm100(&num_sms));
+  if (world < 1 || world > kMaxWorld) return fail(B2M_ERR_ARG, "quant_push: world=%d outside [1, 8]", world);
+  if (rows <= 0 || hidden <= 0 || hidden % 128 || ldx < hidden || ldx % 8 || !x || !aligned16(x) || !counter ||
+      !q_dst || !s_dst || !flag_dst)
+    return fail(B2M_ERR_ARG, "quant_push: bad shape/pointers (hidden %% 128 == 0, 16-byte rows)");
+  PeerPtrs q{}, s{};
+  FlagPtrs f{};
+  for (int r = 0; r < world; ++r) {
+    if (!q_dst[r] || !s_dst[r] || !flag_dst[r]) return fail(B2M_ERR_ARG, "quant_push: null peer pointer %d", r);
+    q.p[r] = q_dst[r];
+    s.p[r] = s_dst[r];
+    f.p[r] = flag_dst[r];
+  }
+  const int64_t groups = rows * (hidden / 128);
+  quant_push_kernel<<<grid_for(groups * 16, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, rows, hidden / 128, world, q, s, row0, f, epoch, counter);
+  return check_cuda(cudaGetLastError(), "quant_push launch");
+}
+
+int b2m_dispatch_rows_wait(const void* xq, const float* xs, int64_t tokens, int64_t hidden, const int32_t* pair_pos,
+                           int32_t top_k, void* a_sorted, float* a_scale_t, int64_t rows_cap, const uint32_t* flags,
+                           int32_t world, int32_t rank, uint32_t epoch, int32_t* dev_status, void* stream) {
+  using namespace b2m;
+  int num_sms = 0;
+  B2M_TRY(require_sm100(&num_sms));
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || tokens % world || top_k < 1 || top_k > 8)
+    return fail(B2M_ERR_ARG, "dispatch_rows_wait: bad world/rank/top_k (top_k <= 8, tokens %% world == 0)");
+  if (!xq || !xs || !pair_pos || !a_sorted || !a_scale_t || !flags || hidden % 128 || !aligned16(xq) ||
+      !aligned16(a_sorted))
+    return fail(B2M_ERR_ARG, "dispatch_rows_wait: bad pointers/shape");
+  if (tokens == 0) return B2M_OK;
+  dispatch_wait_kernel<<<grid_for(tokens * 32, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(xq), xs, tokens, hidden, pair_pos, top_k, static_cast<uint8_t*>(a_sorted),
+      a_scale_t, rows_cap, flags, world, rank, epoch, dev_status, timeout_ns());
+  return check_cuda(cudaGetLastError(), "dispatch_rows_wait launch");
+}
+
+int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, const int32_t* topk_ids,
+                     const int32_t* expert_map, const void* shared, int32_t world, int32_t rank,
+                     void* const* slot_dst, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
+                     void* stream) {
+  using namespace b2m;
+  int num_sms = 0;
+  B2M_TRY(require_sm100(&num_sms));
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || tokens <= 0 || tokens % world ||
+      hidden % 8 || top_k <= 0)
+    return fail(B2M_ERR_ARG, "combine_push: bad shape (tokens %% world == 0, hidden %% 8 == 0)");
+  if (!staged || !counter || !slot_dst || !flag_dst || (expert_map && !topk_ids) || !aligned16(staged))
+    return fail(B2M_ERR_ARG, "combine_push: bad pointers");
+  PeerPtrs sl{};
+  FlagPtrs f{};
+  for (int r = 0; r < world; ++r) {
+    if (!slot_dst[r] || !flag_dst[r] || !aligned16(slot_dst[r]))
+      return fail(B2M_ERR_ARG, "combine_push: bad peer pointer %d", r);
+    sl.p[r] = slot_dst[r];
+    f.p[r] = flag_dst[r];
+  }
+  combine_push_kernel<<<grid_for(tokens * (hidden / 8), num_sms, 8), kThreads, 0,
+                        static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, topk_ids, expert_map,
+      static_cast<const __nv_bfloat16*>(shared), world, rank, sl, f, epoch, counter);
+  return check_cuda(cudaGetLastError(), "combine_push launch");
+}
+
+int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world, const uint32_t* flags,
+                  uint32_t epoch, const void* add, void* out, int32_t* dev_status, void* stream) {
+  using namespace b2m;
+  int num_sms = 0;
+  B2M_TRY(require_sm100(&num_sms));
+  if (world < 1 || world > kMaxWorld || rows <= 0 || hidden % 8 || !slots || !flags || !out ||
+      !aligned16(slots) || !aligned16(out) || (add && !aligned16(add)))
+    return fail(B2M_ERR_ARG, "rs_reduce: bad shape/pointers");
+  rs_reduce_kernel<<<grid_for(rows * (hidden / 8), num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(slots), rows, hidden, world, flags, epoch,
+      static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out), dev_status, timeout_ns());
+  return check_cuda(cudaGetLastError(), "rs_reduce launch");
+}
+
+}  // extern "C"

@@ -11,9 +11,10 @@ forward is the path of the reference's scheme b2
 
 On one GPU the quant and the dispatch are one kernel (b2m_quant_dispatch).
 
-The exchange steps are pluggable (``Exchange``): ``NullExchange`` for one GPU,
-``NcclExchange`` (torch.distributed all_gather_into_tensor / reduce_scatter_tensor,
-the unfused comparison scheme) and the peer-memory exchange in ``symm.py``.
+The exchange steps are pluggable: ``NullExchange`` for one GPU, ``NcclExchange``
+(torch.distributed all_gather_into_tensor / reduce_scatter_tensor, the unfused
+comparison scheme) and ``P2PExchange`` (fused all-gather / reduce-scatter through
+peer memory, ``csrc/symm.cu``).
 """
 from __future__ import annotations
 
@@ -111,15 +112,24 @@ class SharedExpert:
 
 
 class NullExchange:
-    """One rank: the gathered tokens are the local tokens, the partial is the output."""
+    """One rank: quantisation and dispatch in one pass, combine straight into the output."""
     world_size = 1
     rank = 0
+    name = "none"
 
-    def all_gather(self, xq_local, xs_local, xq_full, xs_full):  # pragma: no cover - trivial
-        raise AssertionError("single-rank layer gathers nothing")
+    def setup(self, layer: "MoELayer") -> None:
+        pass
 
-    def reduce_scatter(self, partial, out_local):  # pragma: no cover - trivial
-        raise AssertionError("single-rank layer scatters nothing")
+    def gather_dispatch(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
+        sh = layer.shared
+        ops.quant_dispatch(x_local, layer.route.pair_pos, layer.top_k, layer.a_sorted, layer.as_t,
+                           None if sh is None else sh.a, None if sh is None else sh.as_t)
+
+    def combine_scatter(self, layer: "MoELayer", ids, shared_out) -> torch.Tensor:
+        return ops.combine(layer.staged, layer.top_k, ids, layer.expert_map, shared_out, layer.out_local)
+
+    def close(self) -> None:
+        pass
 
 
 class NcclExchange:
@@ -128,6 +138,7 @@ class NcclExchange:
     Same collectives as the reference's b2 (``overlap_forward.py:494-505``, ``:603-608``),
     issued as one call each instead of per chunk.
     """
+    name = "nccl"
 
     def __init__(self, group=None):
         import torch.distributed as dist
@@ -136,12 +147,116 @@ class NcclExchange:
         self.world_size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
 
-    def all_gather(self, xq_local, xs_local, xq_full, xs_full):
-        self.dist.all_gather_into_tensor(xq_full.view(torch.uint8), xq_local.view(torch.uint8), group=self.group)
-        self.dist.all_gather_into_tensor(xs_full, xs_local, group=self.group)
+    def setup(self, layer: "MoELayer") -> None:
+        dev = layer.device
+        layer.xq = torch.empty((layer.T, layer.H), dtype=ops.FP8, device=dev)
+        layer.xs = torch.empty((layer.T, layer.H // 128), dtype=torch.float32, device=dev)
+        self.partial = torch.empty((layer.T, layer.H), dtype=torch.bfloat16, device=dev)
 
-    def reduce_scatter(self, partial, out_local):
-        self.dist.reduce_scatter_tensor(out_local, partial, group=self.group)
+    def gather_dispatch(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
+        r0 = self.rank * layer.T_local
+        xq_l, xs_l = layer.xq[r0:r0 + layer.T_local], layer.xs[r0:r0 + layer.T_local]
+        ops.quant_g128(x_local, xq_l, xs_l)
+        if layer.shared is not None and layer.ep:
+            layer.shared.load_rows(xq_l, xs_l)
+        self.dist.all_gather_into_tensor(layer.xq.view(torch.uint8), xq_l.view(torch.uint8), group=self.group)
+        self.dist.all_gather_into_tensor(layer.xs, xs_l, group=self.group)
+        ops.dispatch_rows(layer.xq, layer.xs, layer.route.pair_pos, layer.top_k, layer.a_sorted, layer.as_t)
+        if layer.shared is not None and not layer.ep:
+            layer.shared.load_rows(layer.xq, layer.xs)
+
+    def combine_scatter(self, layer: "MoELayer", ids, shared_out) -> torch.Tensor:
+        ops.combine(layer.staged, layer.top_k, ids, layer.expert_map, shared_out, self.partial)
+        self.dist.reduce_scatter_tensor(layer.out_local, self.partial, group=self.group)
+        if layer.shared is not None and layer.ep:
+            ops.combine(layer.out_local, 1, None, None, layer.shared.run(layer.status), layer.out_local)
+        return layer.out_local
+
+    def close(self) -> None:
+        pass
+
+
+class P2PExchange:
+    """Fused exchange over NVLink peer memory (``b2m_quant_push`` / ``b2m_dispatch_rows_wait`` /
+    ``b2m_combine_push`` / ``b2m_rs_reduce``): no NCCL on the data path.
+
+    The all-gather is the quant kernel storing into every rank's gather buffer; the
+    reduce-scatter is the combine kernel storing each token's partial into its
+    owner's slot, then an owner-side sum in rank order.  Flags are epochs.
+    """
+    name = "p2p"
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.world_size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.epoch = 0
+        self.ws = None
+
+    def setup(self, layer: "MoELayer") -> None:
+        from .symm import SymmetricWorkspace, ptr_array
+
+        P, T, H, Tl = self.world_size, layer.T, layer.H, layer.T_local
+        self.ws = SymmetricWorkspace({
+            "xq": T * H, "xs": T * (H // 128) * 4, "slots": T * H * 2,
+            "ag_flags": 4 * P, "rs_flags": 4 * P, "counters": 16,
+        }, self.group, layer.device)
+        ws = self.ws
+        layer.xq = ws.tensor("xq", (T, H), torch.uint8).view(ops.FP8)
+        layer.xs = ws.tensor("xs", (T, H // 128), torch.float32)
+        self.slots = ws.tensor("slots", (T, H), torch.bfloat16)   # [P source blocks of T/P rows, H]
+        self.ag_flags = ws.local("ag_flags")
+        self.rs_flags = ws.local("rs_flags")
+        self.counters = ws.local("counters")
+        self._q_dst = ptr_array([ws.peer("xq", r) for r in range(P)])
+        self._s_dst = ptr_array([ws.peer("xs", r) for r in range(P)])
+        self._ag_dst = ptr_array([ws.peer("ag_flags", r) + 4 * self.rank for r in range(P)])
+        self._slot_dst = ptr_array([ws.peer("slots", r) for r in range(P)])
+        self._rs_dst = ptr_array([ws.peer("rs_flags", r) + 4 * self.rank for r in range(P)])
+        self.dist.barrier(group=self.group)
+
+    def gather_dispatch(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
+        from . import _lib
+
+        self.epoch += 1
+        st = ops._stream(layer.device)
+        Tl, H = layer.T_local, layer.H
+        _lib.call("b2m_quant_push", x_local.data_ptr(), Tl, H, x_local.stride(0), self.world_size, self._q_dst,
+                  self._s_dst, self.rank * Tl, self._ag_dst, self.epoch, self.counters, st)
+        if layer.shared is not None and layer.ep:
+            r0 = self.rank * Tl
+            layer.shared.load_rows(layer.xq[r0:r0 + Tl], layer.xs[r0:r0 + Tl])
+        r = layer.route
+        _lib.call("b2m_dispatch_rows_wait", layer.xq.data_ptr(), layer.xs.data_ptr(), layer.T, H, r.pair_pos.data_ptr(),
+                  layer.top_k, layer.a_sorted.data_ptr(), layer.as_t.data_ptr(), r.rows_cap, self.ag_flags,
+                  self.world_size, self.rank, self.epoch, layer.status.data_ptr(), st)
+        if layer.shared is not None and not layer.ep:
+            sh = layer.shared
+            _lib.call("b2m_dispatch_rows_wait", layer.xq.data_ptr(), layer.xs.data_ptr(), layer.T, H,
+                      sh.route.pair_pos.data_ptr(), 1, sh.a.data_ptr(), sh.as_t.data_ptr(), sh.route.rows_cap,
+                      self.ag_flags, self.world_size, self.rank, self.epoch, layer.status.data_ptr(), st)
+
+    def combine_scatter(self, layer: "MoELayer", ids, shared_out) -> torch.Tensor:
+        from . import _lib
+
+        st = ops._stream(layer.device)
+        _lib.call("b2m_combine_push", layer.staged.data_ptr(), layer.T, layer.top_k, layer.H,
+                  None if ids is None else ids.data_ptr(),
+                  None if layer.expert_map is None else layer.expert_map.data_ptr(),
+                  None if shared_out is None else shared_out.data_ptr(), self.world_size, self.rank,
+                  self._slot_dst, self._rs_dst, self.epoch, self.counters + 4, st)
+        add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
+        _lib.call("b2m_rs_reduce", self.slots.data_ptr(), layer.T_local, layer.H, self.world_size, self.rs_flags,
+                  self.epoch, None if add is None else add.data_ptr(), layer.out_local.data_ptr(),
+                  layer.status.data_ptr(), st)
+        return layer.out_local
+
+    def close(self) -> None:
+        if self.ws is not None:
+            self.ws.close()
+            self.ws = None
 
 
 class MoELayer:
@@ -175,14 +290,12 @@ class MoELayer:
         self.numel = tokens * top_k
         self.route = _Routing(self.numel, global_num_experts, dev)
         H = self.H
-        self.xq = torch.empty((tokens, H), dtype=ops.FP8, device=dev)          # token order (all-gather target)
-        self.xs = torch.empty((tokens, H // 128), dtype=torch.float32, device=dev)
+        self.xq = self.xs = None   # token-order all-gather target, owned by the exchange
         self.a_sorted = torch.empty((self.route.rows_cap, H), dtype=ops.FP8, device=dev)  # expert order
         self.as_t = torch.empty((H // 128, self.route.rows_cap), dtype=torch.float32, device=dev)
         self.inter_q = torch.empty((self.route.rows_cap, weights.inter), dtype=ops.FP8, device=dev)
         self.inter_st = torch.empty((weights.inter // 128, self.route.rows_cap), dtype=torch.float32, device=dev)
         self.staged = torch.empty((self.numel, H), dtype=torch.bfloat16, device=dev)
-        self.partial = torch.empty((tokens, H), dtype=torch.bfloat16, device=dev)
         self.out_local = torch.empty((self.T_local, H), dtype=torch.bfloat16, device=dev)
         self.status = ops.new_status(dev)
         self.events: list | None = None   # set to [] to record (name, cuda.Event) around the GEMMs
@@ -191,6 +304,7 @@ class MoELayer:
         if shared is not None:
             rows = self.T_local if self.ep else tokens
             self.shared = SharedExpert(shared, rows, dev)
+        self.exchange.setup(self)
 
     # -- stages (exposed for tests and staged timing)
     def _event(self, name: str) -> None:
@@ -200,25 +314,11 @@ class MoELayer:
             self.events.append((name, ev))
 
     def route_and_dispatch(self, x_local: torch.Tensor, topk_ids: torch.Tensor) -> None:
-        """Alignment, quantisation, (all-gather) and the row dispatch into expert order."""
+        """Alignment, then quantisation + (all-gather) + row dispatch into expert order."""
         r = self.route
         ops.moe_align_block_size(topk_ids, BM, self.E, self.expert_map, out=(r.sorted_ids, r.expert_ids, r.ntpp),
                                  pair_pos=r.pair_pos)
-        if self.P == 1:
-            sh = self.shared
-            ops.quant_dispatch(x_local, r.pair_pos, self.top_k, self.a_sorted, self.as_t,
-                               None if sh is None else sh.a, None if sh is None else sh.as_t)
-            return
-        r0 = self.exchange.rank * self.T_local
-        xq_l = self.xq[r0:r0 + self.T_local]
-        xs_l = self.xs[r0:r0 + self.T_local]
-        ops.quant_g128(x_local, xq_l, xs_l)
-        if self.shared is not None and self.ep:
-            self.shared.load_rows(xq_l, xs_l)
-        self.exchange.all_gather(xq_l, xs_l, self.xq, self.xs)
-        ops.dispatch_rows(self.xq, self.xs, r.pair_pos, self.top_k, self.a_sorted, self.as_t)
-        if self.shared is not None and not self.ep:
-            self.shared.load_rows(self.xq, self.xs)
+        self.exchange.gather_dispatch(self, x_local)
 
     def experts(self, topk_weights: torch.Tensor) -> None:
         r = self.route
@@ -232,14 +332,15 @@ class MoELayer:
 
     def kernel_launches(self) -> int:
         """b2m kernels one forward launches."""
-        if self.P == 1:
-            n = 5                       # align, quant+dispatch, GEMM1, GEMM2, combine
-            if self.shared is not None:
-                n += 2                  # shared GEMM1/GEMM2 (its A comes from the same quant pass)
-        else:
-            n = 6                       # align, quant, dispatch, GEMM1, GEMM2, combine
-            if self.shared is not None:
-                n += 3 + (1 if self.ep else 0)
+        sh = self.shared is not None
+        name = self.exchange.name
+        if name == "none":
+            return 5 + (2 if sh else 0)             # align, quant+dispatch, GEMM1, GEMM2, combine (+shared GEMMs)
+        n = 6                                      # align, quant(+push), dispatch, GEMM1, GEMM2, combine(+push)
+        if name == "p2p":
+            n += 1                                 # owner-side reduce
+        if sh:
+            n += 3 + (1 if (self.ep and name == "nccl") else 0)
         return n
 
     def forward(self, x_local: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
@@ -249,18 +350,10 @@ class MoELayer:
         shared_out = None
         if self.shared is not None and not self.ep:
             shared_out = self.shared.run(self.status)
-        ids = topk_ids if self.ep else None
-        if self.P == 1 and not (self.ep and self.shared is not None):
-            return ops.combine(self.staged, self.top_k, ids, self.expert_map, shared_out, self.out_local)
-        ops.combine(self.staged, self.top_k, ids, self.expert_map, shared_out, self.partial)
-        if self.P == 1:
-            self.out_local.copy_(self.partial)
-        else:
-            self.exchange.reduce_scatter(self.partial, self.out_local)
-        if self.shared is not None and self.ep:
-            sh = self.shared.run(self.status)
-            ops.combine(self.out_local, 1, None, None, sh, self.out_local)
-        return self.out_local
+        return self.exchange.combine_scatter(self, topk_ids if self.ep else None, shared_out)
 
     def check(self) -> None:
         ops.check_status(self.status, "MoELayer")
+
+    def close(self) -> None:
+        self.exchange.close()

@@ -15,6 +15,8 @@ from .base import BuilderFn, SchemeConfigError, SchemeSpec
 REGISTRY: dict[str, tuple[SchemeSpec, BuilderFn]] = {
     b200.SPEC_D1.code: (b200.SPEC_D1, b200.build_d1),
     b200.SPEC_D2.code: (b200.SPEC_D2, b200.build_d2),
+    b200.SPEC_D3.code: (b200.SPEC_D3, b200.build_d3),
+    b200.SPEC_D4.code: (b200.SPEC_D4, b200.build_d4),
 }
 
 

@@ -10,6 +10,9 @@ returns bf16 [M/P, K] on ``ctx.device`` ordered on the caller's current stream.
 Codes:
   d1  TP, NCCL all-gather (FP8 bytes + scales) -> b2m kernels -> NCCL reduce-scatter (bf16)
   d2  EP, same exchange, local experts only (expert_map), shared expert on local tokens
+  d3  TP, fused exchange over NVLink peer memory: the quant kernel stores into every
+      rank's gather buffer, the combine kernel stores each partial into its owner's slot
+  d4  EP, fused exchange as d3
 The NCCL schemes are the unfused comparison for the fused peer-memory schemes.
 """
 from __future__ import annotations
@@ -30,6 +33,9 @@ def _spec(code: str, name: str, parallel: str, comm: str) -> SchemeSpec:
 
 SPEC_D1 = _spec("d1", "B200-TP-NCCL", "TP", "quantize -> NCCL AG(fp8+scale) -> b2m GEMM1/GEMM2 -> NCCL RS(bf16)")
 SPEC_D2 = _spec("d2", "B200-EP-NCCL", "EP", "quantize -> NCCL AG(fp8+scale) -> b2m GEMMs(local experts) -> NCCL RS -> +shared")
+SPEC_D3 = _spec("d3", "B200-TP-P2P", "TP", "quantize+push(peer memory) -> b2m GEMM1/GEMM2 -> combine+push -> owner reduce")
+SPEC_D4 = _spec("d4", "B200-EP-P2P", "EP", "quantize+push(peer memory) -> b2m GEMMs(local experts) -> combine+push -> owner reduce(+shared)")
+EXCHANGE = {"d1": "nccl", "d2": "nccl", "d3": "p2p", "d4": "p2p"}
 
 
 def require_data(data: Any) -> Any:
@@ -42,7 +48,7 @@ def build_layer(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, exchange: Any =
     """Shard views + prepared weights + MoELayer for this rank."""
     import torch
 
-    from ..layer import ExpertWeights, MoELayer, NcclExchange
+    from ..layer import ExpertWeights, MoELayer, NcclExchange, P2PExchange
     from ..weights import ep_views, tp_views
 
     bundle = require_data(data)
@@ -61,7 +67,7 @@ def build_layer(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, exchange: Any =
         sv = tp_views(*sargs, ctx.rank, ctx.world_size) if spec.parallel == "TP" else tp_views(*sargs, 0, 1)
         shared = ExpertWeights.prepare(sv["w1"], sv["w1_scale"], sv["w2"], sv["w2_scale"])
     if exchange is None and ctx.world_size > 1:
-        exchange = NcclExchange(ctx.group)
+        exchange = P2PExchange(ctx.group) if EXCHANGE.get(spec.code) == "p2p" else NcclExchange(ctx.group)
     expert_map = views.get("expert_map")
     layer = MoELayer(weights, T, s.top_k, s.E, expert_map=expert_map, shared=shared, exchange=exchange,
                      device=device)
@@ -87,7 +93,10 @@ def build_instance(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, scheme_cfg: 
         return out
 
     def close() -> None:
-        layer.check()
+        try:
+            layer.check()
+        finally:
+            layer.close()
 
     diag = {"shard_level": level, "tokens": layer.T, "rows_cap": layer.route.rows_cap,
             "experts_local": layer.w.num_experts, "inter_local": layer.w.inter}
@@ -100,3 +109,11 @@ def build_d1(cfg: Any, ctx: Any, data: Any, scheme_cfg: Any) -> SchemeInstance:
 
 def build_d2(cfg: Any, ctx: Any, data: Any, scheme_cfg: Any) -> SchemeInstance:
     return build_instance(SPEC_D2, cfg, ctx, data, scheme_cfg)
+
+
+def build_d3(cfg: Any, ctx: Any, data: Any, scheme_cfg: Any) -> SchemeInstance:
+    return build_instance(SPEC_D3, cfg, ctx, data, scheme_cfg)
+
+
+def build_d4(cfg: Any, ctx: Any, data: Any, scheme_cfg: Any) -> SchemeInstance:
+    return build_instance(SPEC_D4, cfg, ctx, data, scheme_cfg)

@@ -1,0 +1,74 @@
+"""Multi-GPU parity check, run under torchrun (one rank per GPU, NCCL).
+
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 tests/dist_gpu_check.py --scheme d3 --preset mixtral --tokens 512
+
+Every rank builds the same seeded data, runs the scheme twice (buffers reused), and
+compares its [T/P, H] output slice with the fp32 torch golden of the full layer under
+the reference worker's gates plus the calibrated max-abs bound.  Exit status 0 only
+if every rank passes; rank 0 prints one JSON line.
+"""
+import argparse
+import json
+import os
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--scheme", default="d3")
+    ap.add_argument("--preset", default="mixtral")
+    ap.add_argument("--tokens", type=int, default=512)
+    ap.add_argument("--zipf", action="store_true")
+    args = ap.parse_args()
+
+    import torch
+    import torch.distributed as dist
+
+    from oracle import golden as ogolden
+    from tests import torch_ref
+    from td_benchmark_b200 import configs, data
+    from td_benchmark_b200.context import init_context
+    from td_benchmark_b200.schemes import build_scheme
+    from td_benchmark_b200.schemes.base import SchemeCfg
+
+    ctx = init_context(backend="nccl", timeout_s=120.0)
+    over = {"M": args.tokens}
+    if args.preset == "dsv3" and not args.zipf:
+        over["imbalance_kind"] = "none"
+    cfg = configs.preset(args.preset, **over)
+    bundle = data.build_bundle(cfg, rank=ctx.rank, world_size=ctx.world_size, device=ctx.device)
+    inst = build_scheme(cfg, ctx, bundle, SchemeCfg(args.scheme, {"check_status": True}))
+    out1 = inst.run().clone()
+    out2 = inst.run()
+    torch.cuda.synchronize()
+    same = bool(torch.equal(out1, out2))
+    ck = bundle.ckpt
+    sw = None
+    if ck.shared_w1 is not None:
+        sw = (ck.shared_w1.fp8, ck.shared_w1.scale, ck.shared_w2.fp8, ck.shared_w2.scale)
+    g, calib = torch_ref.act_quant_error(bundle.hidden_full, bundle.routing.topk_ids_full,
+                                         bundle.routing.topk_weights_full, ck.w1.fp8, ck.w1.scale, ck.w2.fp8,
+                                         ck.w2.scale, sw)
+    tl = out2.shape[0]
+    ref = g[ctx.rank * tl:(ctx.rank + 1) * tl]
+    rep = ogolden.compare_outputs(out2.float().cpu().numpy(), ref.cpu().numpy(), **ogolden.GATES)
+    ok = rep["pass"] and rep["max_abs"] <= 1.5 * calib and same
+    inst.close()
+    flag = torch.tensor([1.0 if ok else 0.0], device=ctx.device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    if ctx.rank == 0:
+        print(json.dumps({"scheme": args.scheme, "preset": args.preset, "tokens": args.tokens, "world": ctx.world_size,
+                          "pass": bool(flag.item() > 0), "rank0": {k: rep[k] for k in ("cos_sim", "rel_p99", "max_abs",
+                                                                                         "scale")},
+                          "calib_max_abs": calib, "repeatable": same}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0 if flag.item() > 0 else 1
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

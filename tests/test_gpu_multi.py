@@ -1,0 +1,45 @@
+"""Multi-GPU parity of the NCCL and peer-memory schemes (skipped with fewer than 2 GPUs)."""
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _gpus() -> int:
+    try:
+        import torch
+        return torch.cuda.device_count() if torch.cuda.is_available() else 0
+    except Exception:
+        return 0
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("scheme,preset,tokens,extra", [
+    ("d1", "mixtral", 512, []), ("d3", "mixtral", 512, []),
+    ("d2", "dsv3", 512, []), ("d4", "dsv3", 512, []), ("d4", "dsv3", 1024, ["--zipf"]),
+    ("d3", "qwen3", 256, []),
+])
+def test_multi_gpu_scheme_matches_golden(scheme, preset, tokens, extra):
+    n = min(_gpus(), 4)
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={n}", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           str(ROOT / "tests" / "dist_gpu_check.py"), "--scheme", scheme, "--preset", preset, "--tokens", str(tokens),
+           *extra]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    res = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT, env=env)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    assert '"pass": true' in res.stdout
