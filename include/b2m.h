@@ -193,6 +193,20 @@ int b2m_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int
                    void* const* s_dst, int64_t row0, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
                    void* stream);
 
+/* b2m_quant_push for callers that cannot allocate device memory (a runtime that
+ * owns every device byte through its own arena, or code that may not call
+ * cudaMalloc): no counter argument; the completion counter lives in a static
+ * 256-byte device array of this library (held on every GPU that loads it, until
+ * exit).  No counterpart in the reference.  Limits: world <= 8 (B2M_ERR_ARG beyond);
+ * the scratch need is one counter whatever rows/hidden are.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) and should
+ * come before any stream capture.  Each call clears the counter on `stream` before
+ * the launch; calls share it, so calls that overlap on the GPU race and must be
+ * serialised by the caller.  Allocates nothing (no cudaMalloc/cudaFree). */
+int b2m_quant_push_noalloc(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world,
+                           void* const* q_dst, void* const* s_dst, int64_t row0, uint32_t* const* flag_dst,
+                           uint32_t epoch, void* stream);
+
 /* b2m_dispatch_rows on the gather buffer, reading source rank s's rows
  * (tokens [s*T/world, (s+1)*T/world)) only once flags[s] >= epoch (own rank first).
  * top_k <= 8. */

@@ -34,6 +34,7 @@ SIGNATURES: dict[str, list] = {
     "b2m_ipc_open": [_p, _c.POINTER(_p)],
     "b2m_ipc_close": [_p],
     "b2m_quant_push": [_p, _i64, _i64, _i64, _i32, _p, _p, _i64, _p, _c.c_uint32, _p, _p],
+    "b2m_quant_push_noalloc": [_p, _i64, _i64, _i64, _i32, _p, _p, _i64, _p, _c.c_uint32, _p],
     "b2m_dispatch_rows_wait": [_p, _p, _i64, _i64, _p, _i32, _p, _p, _i64, _p, _i32, _i32, _c.c_uint32, _p, _p],
     "b2m_combine_push": [_p, _i64, _i32, _i64, _p, _p, _p, _i32, _i32, _p, _p, _c.c_uint32, _p, _p],
     "b2m_rs_reduce": [_p, _i64, _i64, _i32, _p, _c.c_uint32, _p, _p, _p, _p],

@@ -28,6 +28,8 @@
 
 #include <string.h>
 
+#include <mutex>
+
 namespace b2m {
 namespace {
 
@@ -216,6 +218,41 @@ int grid_for(int64_t work, int num_sms, int per_sm) {
 }  // namespace
 }  // namespace b2m
 
+// ---------------------------------------------------------------- allocation-free all-gather push
+// Callers that cannot allocate device memory (a runtime that owns every byte through
+// its own arena, or code that must not call cudaMalloc at all) cannot hand
+// b2m_quant_push its completion counter.  b2m_quant_push_noalloc keeps that counter
+// in this library's own static device memory instead: 64 int32 (256 bytes) per GPU
+// that loads the library, held until the process exits; one call uses one counter
+// (independent of rows and hidden) and world is limited to 8 as for b2m_quant_push.
+// Every call shares that counter: calls that overlap on the GPU (other streams,
+// other threads) race on it, so a caller must serialise them.
+namespace b2m {
+namespace {
+constexpr int kPushScratchInts = 64;
+constexpr int kPushScratchNeeded = 1;  // one grid-completion counter per call
+static __device__ __align__(256) int32_t g_push_scratch[kPushScratchInts];
+
+// Device address of g_push_scratch on the current device, looked up once per device
+// (the host-side name is only a stand-in and must never be handed to a kernel).
+int push_scratch_ptr(int32_t** out) {
+  static std::mutex mu;
+  static int32_t* addr[64] = {nullptr};
+  int dev = 0;
+  B2M_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  if (dev < 0 || dev >= 64) return fail(B2M_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    B2M_TRY(check_cuda(cudaGetSymbolAddress(&p, g_push_scratch), "cudaGetSymbolAddress(g_push_scratch)"));
+    addr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = addr[dev];
+  return B2M_OK;
+}
+}  // namespace
+}  // namespace b2m
+
 extern "C" {
 
 int b2m_symm_alloc(int64_t bytes, void** dev_ptr) {
@@ -276,6 +313,26 @@ int b2m_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int
   quant_push_kernel<<<grid_for(groups * 16, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, rows, hidden / 128, world, q, s, row0, f, epoch, counter);
   return check_cuda(cudaGetLastError(), "quant_push launch");
+}
+
+int b2m_quant_push_noalloc(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world,
+                           void* const* q_dst, void* const* s_dst, int64_t row0, uint32_t* const* flag_dst,
+                           uint32_t epoch, void* stream) {
+  using namespace b2m;
+  static_assert(kPushScratchNeeded <= kPushScratchInts, "scratch capacity");
+  if (world < 1 || world > kMaxWorld)
+    return fail(B2M_ERR_ARG, "quant_push_noalloc: world=%d outside [1, %d]", world, kMaxWorld);
+  // The scratch need is one counter whatever rows/hidden are, so no problem size can
+  // outgrow the static array; the peer table bounds world (checked above).
+  int32_t* counter = nullptr;
+  B2M_TRY(require_sm100(nullptr));
+  B2M_TRY(push_scratch_ptr(&counter));
+  // The counter must start at zero; a previous call normally leaves it zero, but one
+  // that was aborted might not, so clear it on the stream (no allocation involved).
+  B2M_TRY(check_cuda(cudaMemsetAsync(counter, 0, sizeof(int32_t) * kPushScratchNeeded,
+                                     static_cast<cudaStream_t>(stream)),
+                     "quant_push_noalloc: clear scratch"));
+  return b2m_quant_push(x, rows, hidden, ldx, world, q_dst, s_dst, row0, flag_dst, epoch, counter, stream);
 }
 
 int b2m_dispatch_rows_wait(const void* xq, const float* xs, int64_t tokens, int64_t hidden, const int32_t* pair_pos,
