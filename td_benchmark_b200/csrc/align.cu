@@ -5,8 +5,8 @@
 // expert are emitted in ascending flat index, which makes the output unique.
 //
 // One CTA of 32 warps.  Warp w owns the contiguous pair range
-// [w*chunk, (w+1)*chunk).  Pass A: per-warp per-expert counts (warp_cnt[w][e]) from
-// __match_any_sync groups — no atomics, so the result does not depend on timing.
+// [w*chunk, (w+1)*chunk).  Pass A: per-warp per-expert counts (warp_cnt[w][e], shared
+// atomics: a count does not depend on the order of the adds).
 // Scan: padded counts -> expert segment starts; per-(warp, expert) bases are the
 // segment start plus the counts of lower warps.  Pass C: each warp walks its range
 // again in order and places every pair at base + rank inside its match group; the
@@ -21,6 +21,7 @@ namespace {
 constexpr int kAlignWarps = 32;
 constexpr int kAlignThreads = kAlignWarps * 32;
 constexpr int kMaxExperts = 1024;
+constexpr int kBatch = 8;  // ids loaded per lane before use (keeps 8 loads in flight per warp)
 
 __global__ void __launch_bounds__(kAlignThreads, 1)
     align_kernel(const int32_t* __restrict__ topk_ids, int64_t numel, int32_t num_experts, int32_t bs,
@@ -43,16 +44,18 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
   for (int i = tid; i < kAlignWarps * num_experts; i += kAlignThreads) warp_cnt[i] = 0;
   __syncthreads();
 
-  // Pass A: per-warp counts.
+  // Pass A: per-warp counts (shared-memory atomics; the count does not depend on order).
   int32_t* my_cnt = warp_cnt + warp * num_experts;
-  for (int64_t i0 = lo; i0 < hi; i0 += 32) {
-    const int64_t i = i0 + lane;
-    int32_t e = i < hi ? __ldg(topk_ids + i) : -1;
-    if (e >= num_experts) e = -1;  // out-of-range ids take no slot
-    const uint32_t grp = __match_any_sync(0xffffffffu, e);
-    const int leader = __ffs(grp) - 1;
-    if (e >= 0 && lane == leader) my_cnt[e] += __popc(grp);
-    __syncwarp();
+  for (int64_t i0 = lo; i0 < hi; i0 += 32 * kBatch) {
+    int32_t ev[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int64_t i = i0 + u * 32 + lane;
+      ev[u] = i < hi ? __ldg(topk_ids + i) : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (ev[u] >= 0 && ev[u] < num_experts) atomicAdd(&my_cnt[ev[u]], 1);
   }
   __syncthreads();
 
@@ -96,22 +99,31 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
   }
   __syncthreads();
 
-  // Pass C: ordered scatter.
-  for (int64_t i0 = lo; i0 < hi; i0 += 32) {
-    const int64_t i = i0 + lane;
-    int32_t e = i < hi ? __ldg(topk_ids + i) : -1;
-    if (e >= num_experts) e = -1;
-    const uint32_t grp = __match_any_sync(0xffffffffu, e);
-    const int leader = __ffs(grp) - 1;
-    const int rank = __popc(grp & ((1u << lane) - 1u));
-    if (e >= 0) sorted_ids[my_cnt[e] + rank] = static_cast<int32_t>(i);
-    if (pair_pos && i < hi) {
-      const bool local = e >= 0 && (expert_map == nullptr || __ldg(expert_map + e) >= 0);
-      pair_pos[i] = local ? my_cnt[e] + rank : -1;
+  // Pass C: ordered scatter (ascending pair index inside every expert segment).
+  for (int64_t i0 = lo; i0 < hi; i0 += 32 * kBatch) {
+    int32_t ev[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int64_t i = i0 + u * 32 + lane;
+      ev[u] = i < hi ? __ldg(topk_ids + i) : -1;
+      if (ev[u] >= num_experts) ev[u] = -1;  // out-of-range ids take no slot
     }
-    __syncwarp();
-    if (e >= 0 && lane == leader) my_cnt[e] += __popc(grp);
-    __syncwarp();
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int64_t i = i0 + u * 32 + lane;
+      const int32_t e = ev[u];
+      const uint32_t grp = __match_any_sync(0xffffffffu, e);
+      const int leader = __ffs(grp) - 1;
+      const int rank = __popc(grp & ((1u << lane) - 1u));
+      if (e >= 0) sorted_ids[my_cnt[e] + rank] = static_cast<int32_t>(i);
+      if (pair_pos && i < hi) {
+        const bool local = e >= 0 && (expert_map == nullptr || __ldg(expert_map + e) >= 0);
+        pair_pos[i] = local ? my_cnt[e] + rank : -1;
+      }
+      __syncwarp();
+      if (e >= 0 && lane == leader) my_cnt[e] += __popc(grp);
+      __syncwarp();
+    }
   }
 
   // Pads inside segments, block -> expert table.

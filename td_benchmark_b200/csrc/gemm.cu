@@ -7,7 +7,9 @@
 //               GEMM, the gate/up output for the down GEMM), its 128 row scales (one
 //               512-byte bulk copy of the K-block-major scale array), B (weights) by 2D
 //               tiled TMA, and the B block scales of the stage (prefetched 32 K blocks at
-//               a time across the warp's lanes).
+//               a time across the warp's lanes).  The scales go to an 8-deep ring with
+//               its own barriers, so an operand stage is recycled as soon as the MMA that
+//               read it completes.
 //   warp 1      TMEM allocator and single-thread MMA issuer: per 128-wide K block,
 //               4 x tcgen05.mma kind::f8f6f4 (M=128, N=256, K=32) into one of two
 //               TMEM accumulators (2 x 256 fp32 columns).
@@ -17,10 +19,10 @@
 //               (tcgen05.ld), multiplied by a_scale[row, kb] * b_scale[nblk, kb] (read
 //               from the stage in shared memory) and added to fp32 registers with packed
 //               f32x2 FMAs.  The double-buffered TMEM lets the tensor pipe run one K
-//               block ahead; a stage is recycled once the MMA has consumed it and the
-//               epilogue warps have read its scales.
-// Tiles are (128 sorted rows) x (256 output columns), visited M-block fastest so
-// CTAs running together share the weight tile in L2.  The tile space is walked with
+//               block ahead.
+// Tiles are (128 sorted rows) x (256 output columns), visited in bands of 16 M blocks
+// (N tile by N tile inside a band) so CTAs running together share weight tiles and
+// A rows in L2.  The tile space is walked with
 // a static stride of gridDim.x; blocks whose expert id is -1 are skipped.
 //
 // Gate/up epilogue (replaces silu_and_mul + the second quant, overlap_forward.py:554-561):
@@ -45,6 +47,8 @@ namespace {
 
 constexpr int BM = 128, BN = 256, BK = 128;
 constexpr int STAGES = 4;
+constexpr int SRING = 8;     // scale ring depth (decoupled from the operand stages)
+constexpr int GROUP_M = 16;  // tile raster: bands of GROUP_M M-blocks x all N tiles
 constexpr int A_BYTES = BM * BK;  // 16 KB
 constexpr int B_BYTES = BN * BK;  // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -63,8 +67,10 @@ struct Control {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
-  alignas(16) float as[STAGES][BM];  // A row scales of each stage
-  alignas(16) float bs[STAGES][4];   // B block scales of each stage: rows [0,128) and [128,256) of the tile
+  uint64_t sfull[SRING];
+  uint64_t sempty[SRING];
+  alignas(16) float as[SRING][BM];  // A row scales of K block kbg (slot kbg % SRING)
+  alignas(16) float bs[SRING][4];   // B block scales of that K block: tile rows [0,128) and [128,256)
   float amax[2][2][BM];              // [tile parity][column half][row]
 };
 
@@ -104,7 +110,21 @@ __device__ __forceinline__ float silu(float x) { return x * __frcp_rn(1.0f + __e
 struct TileWalk {
   int64_t num_tiles;
   int num_mb;
+  int num_nt;
 };
+
+// Tile t -> (M block, N tile): bands of GROUP_M consecutive M blocks (experts are
+// contiguous in M) walked N-tile by N-tile, so the CTAs running together share a few
+// weight tiles and a band of A rows, both L2-resident.
+__device__ __forceinline__ void tile_coords(int64_t t, const TileWalk& tw, int& mb, int& nt) {
+  const int64_t per_band = static_cast<int64_t>(GROUP_M) * tw.num_nt;
+  const int64_t band = t / per_band;
+  const int first = static_cast<int>(band * GROUP_M);
+  const int rows = tw.num_mb - first < GROUP_M ? tw.num_mb - first : GROUP_M;
+  const int64_t in_band = t - band * per_band;
+  mb = first + static_cast<int>(in_band % rows);
+  nt = static_cast<int>(in_band / rows);
+}
 
 // ---------------------------------------------------------------- warp 0: B (+A for the down GEMM)
 template <bool kGateUp>
@@ -114,10 +134,10 @@ __device__ __forceinline__ void stage_producer(const CUtensorMap* map_a, const C
   volatile int* abort = &C->abort;
   uint32_t kbg = 0;
   bool alive = true;
-  const uint32_t tx = A_BYTES + B_BYTES + BM * 4;
+  const uint32_t tx = A_BYTES + B_BYTES;
   for (int64_t tile = blockIdx.x; tile < tw.num_tiles && alive; tile += gridDim.x) {
-    const int mb = static_cast<int>(tile % tw.num_mb);
-    const int nt = static_cast<int>(tile / tw.num_mb);
+    int mb, nt;
+    tile_coords(tile, tw, mb, nt);
     const int e = __ldg(p.expert_ids + mb);
     if (e < 0) continue;
     const int blk0 = 2 * nt;
@@ -136,8 +156,12 @@ __device__ __forceinline__ void stage_producer(const CUtensorMap* map_a, const C
       const float s1 = __shfl_sync(0xffffffffu, pre1, kb & 31);
       const int s = kbg % STAGES;
       const uint32_t ph = (kbg / STAGES) & 1;
+      const int r = kbg % SRING;
+      const uint32_t rph = (kbg / SRING) & 1;
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(&C->empty[s], ph ^ 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort);
+      if (lane == 0)
+        ok = mbar_wait(&C->sempty[r], rph ^ 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort) &&
+             mbar_wait(&C->empty[s], ph ^ 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         alive = false;
@@ -145,22 +169,27 @@ __device__ __forceinline__ void stage_producer(const CUtensorMap* map_a, const C
       }
       if (lane == 0) {
         uint8_t* sa = smem + s * STAGE_BYTES;
-        C->bs[s][0] = s0;
-        C->bs[s][1] = s1;
+        C->bs[r][0] = s0;
+        C->bs[r][1] = s1;
+        mbar_arrive_expect_tx(&C->sfull[r], BM * 4);  // releases the bs stores, counts the bulk copy
+        bulk_load(C->as[r], p.a_scale + static_cast<int64_t>(kb) * p.a_scale_ld + static_cast<int64_t>(mb) * BM,
+                  BM * 4, &C->sfull[r]);
         mbar_arrive_expect_tx(&C->full[s], tx);
         tma_load_2d(sa, map_a, &C->full[s], kb * BK, mb * BM);
         tma_load_2d(sa + A_BYTES, map_b, &C->full[s], kb * BK, b_row);
-        bulk_load(C->as[s], p.a_scale + static_cast<int64_t>(kb) * p.a_scale_ld + static_cast<int64_t>(mb) * BM,
-                  BM * 4, &C->full[s]);
       }
       __syncwarp();
     }
   }
-  // Drain: the copies of the last STAGES stages must have landed before the CTA exits.
+  // Drain: the copies of the last STAGES stages (and SRING scale slots) must have
+  // landed before the CTA exits.
   if (lane == 0) {
     const uint32_t first = kbg > STAGES ? kbg - STAGES : 0;
     for (uint32_t i = first; i < kbg; ++i)
       mbar_wait(&C->full[i % STAGES], (i / STAGES) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
+    const uint32_t rfirst = kbg > SRING ? kbg - SRING : 0;
+    for (uint32_t i = rfirst; i < kbg; ++i)
+      mbar_wait(&C->sfull[i % SRING], (i / SRING) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
   }
   __syncwarp();
 }
@@ -172,7 +201,8 @@ __device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, C
   uint32_t kbg = 0;
   bool alive = true;
   for (int64_t tile = blockIdx.x; tile < tw.num_tiles && alive; tile += gridDim.x) {
-    const int mb = static_cast<int>(tile % tw.num_mb);
+    int mb, nt;
+    tile_coords(tile, tw, mb, nt);
     if (__ldg(p.expert_ids + mb) < 0) continue;
     for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
       const int s = kbg % STAGES;
@@ -224,44 +254,48 @@ __device__ __forceinline__ void epilogue_warps(const GemmParams& p, Control* C, 
 
   // Row info of the next tile is loaded one tile ahead.
   int64_t tile = blockIdx.x;
+  auto mb_of = [&](int64_t t) {
+    int m, n;
+    tile_coords(t, tw, m, n);
+    return m;
+  };
   auto next_valid = [&](int64_t t) {
-    while (t < tw.num_tiles && __ldg(p.expert_ids + static_cast<int>(t % tw.num_mb)) < 0) t += gridDim.x;
+    while (t < tw.num_tiles && __ldg(p.expert_ids + mb_of(t)) < 0) t += gridDim.x;
     return t;
   };
   tile = next_valid(tile);
-  int pair_next = (!kGateUp && tile < tw.num_tiles) ? __ldg(p.sorted_ids + (tile % tw.num_mb) * BM + r) : 0;
+  int pair_next = (!kGateUp && tile < tw.num_tiles) ? __ldg(p.sorted_ids + mb_of(tile) * BM + r) : 0;
   for (; tile < tw.num_tiles && alive;) {
-    const int mb = static_cast<int>(tile % tw.num_mb);
-    const int nt = static_cast<int>(tile / tw.num_mb);
+    int mb, nt;
+    tile_coords(tile, tw, mb, nt);
     const int64_t prow = static_cast<int64_t>(mb) * BM + r;
     const int pair = pair_next;
     const bool valid = pair < p.numel;
     float wrow = 1.0f;
     if (!kGateUp && valid && p.topk_weights) wrow = __ldg(p.topk_weights + pair);
     const int64_t tile_after = next_valid(tile + gridDim.x);
-    if (!kGateUp && tile_after < tw.num_tiles) pair_next = __ldg(p.sorted_ids + (tile_after % tw.num_mb) * BM + r);
+    if (!kGateUp && tile_after < tw.num_tiles) pair_next = __ldg(p.sorted_ids + mb_of(tile_after) * BM + r);
 
     float acc[128];
 #pragma unroll
     for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
 
     for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
-      const int s = kbg % STAGES;
+      const int rs = kbg % SRING;
       const int b = kbg & 1;
       int ok = mbar_wait(&C->tfull[b], (kbg >> 1) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE, abort);
-      // The stage's scales were published through full[s] (already complete for this kb).
-      ok = ok && mbar_wait(&C->full[s], (kbg / STAGES) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
+      ok = ok && mbar_wait(&C->sfull[rs], (kbg / SRING) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
                            abort);
       if (!__all_sync(0xffffffffu, ok)) {
         alive = false;
         break;
       }
       tc_fence_after();
-      const float sa = C->as[s][r];
-      const float s_lo = sa * C->bs[s][sidx_lo];
-      const float s_hi = sa * C->bs[s][sidx_hi];
+      const float sa = C->as[rs][r];
+      const float s_lo = sa * C->bs[rs][sidx_lo];
+      const float s_hi = sa * C->bs[rs][sidx_hi];
       __syncwarp();
-      if (lane == 0) mbar_arrive(&C->empty[s]);
+      if (lane == 0) mbar_arrive(&C->sempty[rs]);
       const uint32_t base = tmem_base + lane_off + static_cast<uint32_t>(b * BN);
       {
         float v0[32], v1[32];
@@ -359,12 +393,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0 && blockIdx.x == 0) set_status(p.status, B2M_STATUS_BAD_ROUTING);
     num_mb = 0;
   }
-  const TileWalk tw{static_cast<int64_t>(num_mb) * p.num_nt, num_mb > 0 ? num_mb : 1};
+  const TileWalk tw{static_cast<int64_t>(num_mb) * p.num_nt, num_mb > 0 ? num_mb : 1, p.num_nt};
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&C->full[s], 1);
-      mbar_init(&C->empty[s], 1 + NUM_EPI_WARPS);
+      mbar_init(&C->empty[s], 1);
+    }
+    for (int r = 0; r < SRING; ++r) {
+      mbar_init(&C->sfull[r], 1);
+      mbar_init(&C->sempty[r], NUM_EPI_WARPS);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&C->tfull[b], 1);
