@@ -104,7 +104,7 @@ struct GemmParams {
 
 // silu(x) = x * sigmoid(x).  The gate/up intermediate is requantised to e4m3 right
 // after, so the fast exponential and reciprocal are far inside its tolerance.
-__device__ __forceinline__ float silu(float x) { return x * __frcp_rn(1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // Shared tile walk of every role: returns false when the tile is skipped (expert -1).
 struct TileWalk {

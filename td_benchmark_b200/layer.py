@@ -194,6 +194,9 @@ class P2PExchange:
         self.rank = dist.get_rank(group)
         self.epoch = 0
         self.ws = None
+        # Diagnostic only (bench's exposed-communication split): run the same kernels on
+        # local data with every peer flag treated as already set and nothing sent.
+        self.compute_only = False
 
     def setup(self, layer: "MoELayer") -> None:
         from .symm import SymmetricWorkspace, ptr_array
@@ -220,6 +223,8 @@ class P2PExchange:
     def gather_dispatch(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
         from . import _lib
 
+        if self.compute_only:
+            return self._gather_dispatch_local(layer, x_local)
         self.epoch += 1
         st = ops._stream(layer.device)
         Tl, H = layer.T_local, layer.H
@@ -238,9 +243,30 @@ class P2PExchange:
                       sh.route.pair_pos.data_ptr(), 1, sh.a.data_ptr(), sh.as_t.data_ptr(), sh.route.rows_cap,
                       self.ag_flags, self.world_size, self.rank, self.epoch, layer.status.data_ptr(), st)
 
+    def _gather_dispatch_local(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
+        r0 = self.rank * layer.T_local
+        ops.quant_g128(x_local, layer.xq[r0:r0 + layer.T_local], layer.xs[r0:r0 + layer.T_local])
+        if layer.shared is not None and layer.ep:
+            layer.shared.load_rows(layer.xq[r0:r0 + layer.T_local], layer.xs[r0:r0 + layer.T_local])
+        ops.dispatch_rows(layer.xq, layer.xs, layer.route.pair_pos, layer.top_k, layer.a_sorted, layer.as_t)
+        if layer.shared is not None and not layer.ep:
+            layer.shared.load_rows(layer.xq, layer.xs)
+
+    def _combine_scatter_local(self, layer: "MoELayer", ids, shared_out) -> torch.Tensor:
+        from . import _lib
+
+        st = ops._stream(layer.device)
+        ops.combine(layer.staged, layer.top_k, ids, layer.expert_map, shared_out, self.slots)
+        add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
+        _lib.call("b2m_rs_reduce", self.slots.data_ptr(), layer.T_local, layer.H, self.world_size, self.rs_flags, 0,
+                  None if add is None else add.data_ptr(), layer.out_local.data_ptr(), layer.status.data_ptr(), st)
+        return layer.out_local
+
     def combine_scatter(self, layer: "MoELayer", ids, shared_out) -> torch.Tensor:
         from . import _lib
 
+        if self.compute_only:
+            return self._combine_scatter_local(layer, ids, shared_out)
         st = ops._stream(layer.device)
         _lib.call("b2m_combine_push", layer.staged.data_ptr(), layer.T, layer.top_k, layer.H,
                   None if ids is None else ids.data_ptr(),
