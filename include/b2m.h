@@ -101,10 +101,14 @@ int b2m_dispatch_rows(const void* xq, const float* xs, int64_t tokens, int64_t h
  * numel + E*(block_size-1) (or numel*block_size when numel < E) and
  * expert_ids_cap >= cdiv(sorted_cap, block_size).  num_experts <= 1024.
  * pair_pos (nullable, int32 [numel]) additionally receives the inverse map: the
- * sorted position of every pair, or -1 when its expert is not local. */
+ * sorted position of every pair, or -1 when its expert is not local.
+ * block_pairs (nullable, int32 [1 + 2*expert_ids_cap]) receives the work list of the
+ * paired-CTA GEMMs: [0] = number of pairs P, then P entries (first block, second
+ * block or -1) pairing consecutive blocks inside every local expert's segment. */
 int b2m_align(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int32_t block_size,
               const int32_t* expert_map, int32_t* sorted_token_ids, int64_t sorted_cap, int32_t* expert_ids,
-              int64_t expert_ids_cap, int32_t* num_tokens_post_padded, int32_t* pair_pos, void* stream);
+              int64_t expert_ids_cap, int32_t* num_tokens_post_padded, int32_t* pair_pos, int32_t* block_pairs,
+              void* stream);
 
 /* ---------------------------------------------------------------------------
  * Gate/up weight layout for K3.  The reference stores w1 as [E, 2I, H] with all
@@ -134,11 +138,14 @@ int b2m_w1_interleave(const void* w1, const float* w1_scale, int32_t num_experts
  * w1: interleaved e4m3 [E, 2I, hidden]; w1_scale: interleaved fp32 [E, 2I/128, hidden/128];
  * out_q: e4m3 [rows_cap, I]; out_scale_t: fp32 [I/128, rows_cap].
  * hidden % 128 == 0, I % 128 == 0, rows_cap % 128 == 0, expert_ids holds
- * rows_cap/128 entries. */
+ * rows_cap/128 entries.
+ * block_pairs (nullable): the pair list of b2m_align.  When given, the GEMM runs on
+ * CTA pairs (cta_group::2, M = 256 over two consecutive blocks of one expert, half
+ * of each B tile staged per CTA); otherwise one CTA per 128-row block. */
 int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden, const void* w1,
               const float* w1_scale, int32_t num_experts, int32_t inter, const int32_t* expert_ids,
-              const int32_t* num_tokens_post_padded, void* out_q, float* out_scale_t, int32_t* dev_status,
-              void* stream);
+              const int32_t* num_tokens_post_padded, const int32_t* block_pairs, void* out_q, float* out_scale_t,
+              int32_t* dev_status, void* stream);
 
 /* ---------------------------------------------------------------------------
  * K4  down grouped GEMM with the routed top-k weight in the epilogue.
@@ -150,11 +157,11 @@ int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, in
  * w(pair) = topk_weights[pair] (flat [T*k] fp32), or 1 when topk_weights is NULL.
  * a_fp8 / a_scale_t: K3's out_q / out_scale_t; w2: e4m3 [E, hidden, I];
  * w2_scale: fp32 [E, ceil(hidden/128), I/128]; out: bf16 [numel, hidden] indexed by pair.
- * hidden % 128 == 0, I % 128 == 0. */
+ * hidden % 128 == 0, I % 128 == 0.  block_pairs as for b2m_gemm1. */
 int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int32_t inter, const void* w2,
               const float* w2_scale, int32_t num_experts, int64_t hidden, const int32_t* sorted_token_ids,
-              const int32_t* expert_ids, const int32_t* num_tokens_post_padded, int64_t numel,
-              const float* topk_weights, void* out_bf16, int32_t* dev_status, void* stream);
+              const int32_t* expert_ids, const int32_t* num_tokens_post_padded, const int32_t* block_pairs,
+              int64_t numel, const float* topk_weights, void* out_bf16, int32_t* dev_status, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Top-k combine (+ shared expert add).

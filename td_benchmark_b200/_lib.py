@@ -23,10 +23,10 @@ SIGNATURES: dict[str, list] = {
     "b2m_quant_g128_t": [_p, _i64, _i64, _i64, _p, _i64, _p, _i64, _p],
     "b2m_quant_dispatch": [_p, _i64, _i64, _i64, _p, _i32, _p, _p, _i64, _p, _p, _i64, _p],
     "b2m_dispatch_rows": [_p, _p, _i64, _i64, _p, _i32, _p, _p, _i64, _p],
-    "b2m_align": [_p, _i64, _i32, _i32, _p, _p, _i64, _p, _i64, _p, _p, _p],
+    "b2m_align": [_p, _i64, _i32, _i32, _p, _p, _i64, _p, _i64, _p, _p, _p, _p],
     "b2m_w1_interleave": [_p, _p, _i32, _i32, _i64, _p, _p, _p],
-    "b2m_gemm1": [_p, _p, _i64, _i64, _p, _p, _i32, _i32, _p, _p, _p, _p, _p, _p],
-    "b2m_gemm2": [_p, _p, _i64, _i32, _p, _p, _i32, _i64, _p, _p, _p, _i64, _p, _p, _p, _p],
+    "b2m_gemm1": [_p, _p, _i64, _i64, _p, _p, _i32, _i32, _p, _p, _p, _p, _p, _p, _p],
+    "b2m_gemm2": [_p, _p, _i64, _i32, _p, _p, _i32, _i64, _p, _p, _p, _p, _i64, _p, _p, _p, _p],
     "b2m_combine": [_p, _i64, _i32, _i64, _p, _p, _p, _p, _i64, _p],
     "b2m_symm_alloc": [_i64, _c.POINTER(_p)],
     "b2m_symm_free": [_p],

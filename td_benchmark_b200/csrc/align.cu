@@ -11,7 +11,8 @@
 // segment start plus the counts of lower warps.  Pass C: each warp walks its range
 // again in order and places every pair at base + rank inside its match group; the
 // optional inverse map pair_pos[pair] = sorted position (-1 for a non-local expert)
-// drives the row dispatch into the sorted operand layout of the gate/up GEMM.
+// drives the row dispatch into the sorted operand layout of the gate/up GEMM, and the
+// optional block-pair list feeds the paired-CTA GEMMs.
 #include "b2m_common.cuh"
 #include "b2m_host.h"
 
@@ -27,12 +28,14 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
     align_kernel(const int32_t* __restrict__ topk_ids, int64_t numel, int32_t num_experts, int32_t bs,
                  const int32_t* __restrict__ expert_map, int32_t* __restrict__ sorted_ids, int64_t sorted_cap,
                  int32_t* __restrict__ expert_ids, int64_t expert_ids_cap, int32_t* __restrict__ ntpp_out,
-                 int32_t* __restrict__ pair_pos) {
+                 int32_t* __restrict__ pair_pos, int32_t* __restrict__ block_pairs) {
   extern __shared__ int32_t sm[];
   int32_t* warp_cnt = sm;                                  // [32][E] counts, then bases
   int32_t* counts = warp_cnt + kAlignWarps * num_experts;  // [E]
   int32_t* starts = counts + num_experts;                  // [E]
+  int32_t* pstart = starts + num_experts;                  // [E] first pair index of each expert
   __shared__ int32_t s_total;
+  __shared__ int32_t s_pairs;
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -84,6 +87,26 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
       carry += __shfl_sync(0xffffffffu, incl, 31);
     }
     if (lane == 0) s_total = carry;
+    if (block_pairs) {  // pairs of consecutive blocks inside each local expert's segment
+      int32_t pc = 0;
+      for (int e0 = 0; e0 < num_experts; e0 += 32) {
+        const int e = e0 + lane;
+        int32_t np = 0;
+        if (e < num_experts && (expert_map == nullptr || __ldg(expert_map + e) >= 0)) {
+          const int32_t nb = (counts[e] + bs - 1) / bs;
+          np = (nb + 1) / 2;
+        }
+        int32_t incl = np;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int32_t v = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += v;
+        }
+        if (e < num_experts) pstart[e] = pc + incl - np;
+        pc += __shfl_sync(0xffffffffu, incl, 31);
+      }
+      if (lane == 0) s_pairs = pc;
+    }
   }
   __syncthreads();
   const int32_t total = s_total;
@@ -135,7 +158,16 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
     for (int32_t s = st + c; s < st + p; ++s) sorted_ids[s] = pad_id;
     const int32_t mapped = expert_map ? __ldg(expert_map + e) : e;
     for (int32_t b = st / bs; b < (st + p) / bs; ++b) expert_ids[b] = mapped;
+    if (block_pairs && mapped >= 0) {
+      const int32_t nb = p / bs;
+      for (int32_t j = 0; 2 * j < nb; ++j) {
+        const int32_t first = st / bs + 2 * j;
+        block_pairs[1 + 2 * (pstart[e] + j)] = first;
+        block_pairs[2 + 2 * (pstart[e] + j)] = 2 * j + 1 < nb ? first + 1 : -1;
+      }
+    }
   }
+  if (block_pairs && tid == 0) block_pairs[0] = s_pairs;
   // Tails.
   for (int64_t s = total + tid; s < sorted_cap; s += kAlignThreads) sorted_ids[s] = pad_id;
   for (int64_t b = total / bs + tid; b < expert_ids_cap; b += kAlignThreads) expert_ids[b] = -1;
@@ -148,7 +180,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
 extern "C" int b2m_align(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int32_t block_size,
                          const int32_t* expert_map, int32_t* sorted_token_ids, int64_t sorted_cap,
                          int32_t* expert_ids, int64_t expert_ids_cap, int32_t* num_tokens_post_padded,
-                         int32_t* pair_pos, void* stream) {
+                         int32_t* pair_pos, int32_t* block_pairs, void* stream) {
   using namespace b2m;
   B2M_TRY(require_sm100(nullptr));
   if (num_experts <= 0 || num_experts > kMaxExperts)
@@ -166,13 +198,13 @@ extern "C" int b2m_align(const int32_t* topk_ids, int64_t numel, int32_t num_exp
   if ((sorted_cap > 0 && !sorted_token_ids) || (expert_ids_cap > 0 && !expert_ids) || !num_tokens_post_padded ||
       (numel > 0 && !topk_ids))
     return fail(B2M_ERR_ARG, "align: null pointer");
-  const size_t smem = (size_t(kAlignWarps) + 2) * num_experts * sizeof(int32_t);
+  const size_t smem = (size_t(kAlignWarps) + 3) * num_experts * sizeof(int32_t);
   if (smem > 48 * 1024)
     B2M_TRY(check_cuda(
         cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
         "align: cudaFuncSetAttribute"));
   align_kernel<<<1, kAlignThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       topk_ids, numel, num_experts, block_size, expert_map, sorted_token_ids, sorted_cap, expert_ids,
-      expert_ids_cap, num_tokens_post_padded, pair_pos);
+      expert_ids_cap, num_tokens_post_padded, pair_pos, block_pairs);
   return check_cuda(cudaGetLastError(), "align launch");
 }

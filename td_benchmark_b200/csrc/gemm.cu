@@ -232,6 +232,68 @@ __device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, C
   }
 }
 
+// End of a tile for one epilogue thread (row r of the tile, column half h), acc holding
+// its 128 promoted fp32 columns.  Gate/up: h = silu(gate) * up, 1x128 requant across the
+// row's two column halves (partial amax exchanged through shared memory), codes + scale
+// stored at sorted row prow.  Down: routed weight, bf16, stored at the pair's row.
+// Returns false when the amax exchange timed out.
+template <bool kGateUp>
+__device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)[2][BM], uint64_t* amax_bar,
+                                           float (&acc)[128], int64_t prow, int nt, int h, int r, int pair,
+                                           float wrow, bool valid, uint32_t tiles_done, int lane,
+                                           volatile int* abort) {
+  if (kGateUp) {
+    // h = silu(gate) * up, then 1x128 quant across both column halves of the row.
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const float v = silu(acc[i]) * acc[64 + i];
+      acc[i] = v;
+      amax = fmaxf(amax, fabsf(v));
+    }
+    const int par = tiles_done & 1;
+    amax_x[par][h][r] = amax;
+    mbar_arrive(&amax_bar[par]);
+    int ok = mbar_wait(&amax_bar[par], (tiles_done >> 1) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
+                       abort);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    amax = fmaxf(amax_x[par][0][r], amax_x[par][1][r]);
+    const float scale = fmaxf(amax / 448.0f, 1e-12f);
+    const float inv = 1.0f / scale;  // one IEEE division per row; codes use x * (1/scale)
+    uint8_t* dst = p.out_q + prow * p.inter + nt * 128 + 64 * h;
+#pragma unroll
+    for (int i = 0; i < 64; i += 16) {
+      uint4 w;
+      w.x = pack4_e4m3(clamp448(acc[i + 0] * inv), clamp448(acc[i + 1] * inv), clamp448(acc[i + 2] * inv),
+                       clamp448(acc[i + 3] * inv));
+      w.y = pack4_e4m3(clamp448(acc[i + 4] * inv), clamp448(acc[i + 5] * inv), clamp448(acc[i + 6] * inv),
+                       clamp448(acc[i + 7] * inv));
+      w.z = pack4_e4m3(clamp448(acc[i + 8] * inv), clamp448(acc[i + 9] * inv), clamp448(acc[i + 10] * inv),
+                       clamp448(acc[i + 11] * inv));
+      w.w = pack4_e4m3(clamp448(acc[i + 12] * inv), clamp448(acc[i + 13] * inv), clamp448(acc[i + 14] * inv),
+                       clamp448(acc[i + 15] * inv));
+      *reinterpret_cast<uint4*>(dst + i) = w;
+    }
+    if (h == 0) p.out_scale_t[static_cast<int64_t>(nt) * p.rows_cap + prow] = scale;
+  } else {
+    const bool cols_valid = 2 * nt + h < p.n_blocks;
+    if (valid && cols_valid) {
+      __nv_bfloat16* dst = p.out_bf16 + static_cast<int64_t>(pair) * p.hidden + nt * BN + 128 * h;
+#pragma unroll
+      for (int i = 0; i < 128; i += 8) {
+        uint32_t u[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const __nv_bfloat162 v = __floats2bfloat162_rn(acc[i + 2 * j] * wrow, acc[i + 2 * j + 1] * wrow);
+          u[j] = *reinterpret_cast<const uint32_t*>(&v);
+        }
+        *reinterpret_cast<uint4*>(dst + i) = make_uint4(u[0], u[1], u[2], u[3]);
+      }
+    }
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- warps 4-11: promotion + epilogue
 template <bool kGateUp>
 __device__ __forceinline__ void epilogue_warps(const GemmParams& p, Control* C, TileWalk tw, uint32_t tmem_base,
@@ -323,55 +385,9 @@ __device__ __forceinline__ void epilogue_warps(const GemmParams& p, Control* C, 
     }
     if (!alive) break;
 
-    if (kGateUp) {
-      // h = silu(gate) * up, then 1x128 quant across both column halves of the row.
-      float amax = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float v = silu(acc[i]) * acc[64 + i];
-        acc[i] = v;
-        amax = fmaxf(amax, fabsf(v));
-      }
-      const int par = tiles_done & 1;
-      C->amax[par][h][r] = amax;
-      mbar_arrive(&C->amax_bar[par]);
-      int ok = mbar_wait(&C->amax_bar[par], (tiles_done >> 1) & 1, p.timeout_ns, p.status,
-                         B2M_STATUS_TIMEOUT_EPILOGUE, abort);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      amax = fmaxf(C->amax[par][0][r], C->amax[par][1][r]);
-      const float scale = fmaxf(amax / 448.0f, 1e-12f);
-      const float inv = 1.0f / scale;  // one IEEE division per row; codes use x * (1/scale)
-      uint8_t* dst = p.out_q + prow * p.inter + nt * 128 + 64 * h;
-#pragma unroll
-      for (int i = 0; i < 64; i += 16) {
-        uint4 w;
-        w.x = pack4_e4m3(clamp448(acc[i + 0] * inv), clamp448(acc[i + 1] * inv), clamp448(acc[i + 2] * inv),
-                         clamp448(acc[i + 3] * inv));
-        w.y = pack4_e4m3(clamp448(acc[i + 4] * inv), clamp448(acc[i + 5] * inv), clamp448(acc[i + 6] * inv),
-                         clamp448(acc[i + 7] * inv));
-        w.z = pack4_e4m3(clamp448(acc[i + 8] * inv), clamp448(acc[i + 9] * inv), clamp448(acc[i + 10] * inv),
-                         clamp448(acc[i + 11] * inv));
-        w.w = pack4_e4m3(clamp448(acc[i + 12] * inv), clamp448(acc[i + 13] * inv), clamp448(acc[i + 14] * inv),
-                         clamp448(acc[i + 15] * inv));
-        *reinterpret_cast<uint4*>(dst + i) = w;
-      }
-      if (h == 0) p.out_scale_t[static_cast<int64_t>(nt) * p.rows_cap + prow] = scale;
-    } else {
-      const bool cols_valid = 2 * nt + h < p.n_blocks;
-      if (valid && cols_valid) {
-        __nv_bfloat16* dst = p.out_bf16 + static_cast<int64_t>(pair) * p.hidden + nt * BN + 128 * h;
-#pragma unroll
-        for (int i = 0; i < 128; i += 8) {
-          uint32_t u[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const __nv_bfloat162 v = __floats2bfloat162_rn(acc[i + 2 * j] * wrow, acc[i + 2 * j + 1] * wrow);
-            u[j] = *reinterpret_cast<const uint32_t*>(&v);
-          }
-          *reinterpret_cast<uint4*>(dst + i) = make_uint4(u[0], u[1], u[2], u[3]);
-        }
-      }
-    }
+    if (!finish_tile<kGateUp>(p, C->amax, C->amax_bar, acc, prow, nt, h, r, pair, wrow, valid, tiles_done, lane,
+                              abort))
+      break;
     ++tiles_done;
     tile = tile_after;
   }
@@ -444,6 +460,328 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ================================================================ paired-CTA variant
+// Cluster of two CTAs on one work item = a pair of consecutive 128-row blocks of the same
+// expert (from the alignment's block-pair list) x one 256-column N tile.  The leader
+// issues tcgen05.mma.cta_group::2 (M=256, N=256, K=32): A rows [0,128) come from the
+// leader's shared memory and [128,256) from the peer's; the 256 B rows are split the
+// same way, so each CTA stages 32 KB per K block (6 stages instead of 4 x 48 KB) and the
+// accumulator rows of each CTA land in its own TMEM.  Each CTA promotes and stores its
+// own 128 rows exactly as the single-CTA kernel does.  A trailing odd block runs with a
+// partner that repeats its rows and skips its stores.  All TMA loads are plain (no
+// multicast); the only cluster-wide operations are the MMA commits and barrier arrives.
+constexpr int PSTAGES = 6;
+constexpr int BH = BN / 2;  // B rows staged per CTA
+constexpr int PA_BYTES = BM * BK;
+constexpr int PB_BYTES = BH * BK;
+constexpr int PSTAGE_BYTES = PA_BYTES + PB_BYTES;
+constexpr int GROUP_P = 8;  // raster band: GROUP_P pairs x all N tiles
+constexpr uint32_t IDESC_PAIR = idesc_e4m3_f32(2 * BM, BN);
+
+struct PairControl {
+  uint64_t full[PSTAGES];   // leader: both CTAs' operand bytes of a stage
+  uint64_t empty[PSTAGES];  // each CTA: its stage was consumed by the pair MMA
+  uint64_t tfull[2];        // each CTA: accumulator buffer ready
+  uint64_t tempty[2];       // leader: both CTAs' epilogues released the buffer (16 warp arrivals)
+  uint64_t amax_bar[2];
+  uint64_t mma_done;
+  uint64_t sfull[SRING];
+  uint64_t sempty[SRING];
+  uint32_t tmem_base;
+  int abort;
+  alignas(16) float as[SRING][BM];
+  alignas(16) float bs[SRING][4];
+  float amax[2][2][BM];
+};
+constexpr size_t PSMEM_BYTES = size_t(PSTAGES) * PSTAGE_BYTES + sizeof(PairControl) + 1024;
+static_assert(PSMEM_BYTES <= 227 * 1024, "shared memory budget (pair)");
+
+struct PairWalk {
+  const int32_t* pairs;  // [0] = count, then (first, second or -1)
+  int num_pairs;
+  int num_nt;
+  int64_t num_items;
+};
+
+struct PairItem {
+  int b0, b1, nt;
+};
+
+__device__ __forceinline__ PairItem pair_item(int64_t w, const PairWalk& pw) {
+  const int64_t per_band = static_cast<int64_t>(GROUP_P) * pw.num_nt;
+  const int64_t band = w / per_band;
+  const int first = static_cast<int>(band * GROUP_P);
+  const int rows = pw.num_pairs - first < GROUP_P ? pw.num_pairs - first : GROUP_P;
+  const int64_t in_band = w - band * per_band;
+  const int pi = first + static_cast<int>(in_band % rows);
+  PairItem it;
+  it.nt = static_cast<int>(in_band / rows);
+  it.b0 = __ldg(pw.pairs + 1 + 2 * pi);
+  it.b1 = __ldg(pw.pairs + 2 + 2 * pi);
+  return it;
+}
+
+template <bool kGateUp>
+__device__ __forceinline__ void pair_producer(const CUtensorMap* map_a, const CUtensorMap* map_b, const GemmParams& p,
+                                              uint8_t* smem, PairControl* C, const PairWalk& pw, uint32_t cr,
+                                              int lane) {
+  volatile int* abort = &C->abort;
+  uint32_t kbg = 0;
+  bool alive = true;
+  const int64_t cluster = blockIdx.x >> 1;
+  const int64_t nclusters = gridDim.x >> 1;
+  for (int64_t w = cluster; w < pw.num_items && alive; w += nclusters) {
+    const PairItem it = pair_item(w, pw);
+    const int mb = (cr == 0 || it.b1 < 0) ? it.b0 : it.b1;
+    const int e = __ldg(p.expert_ids + it.b0);
+    const int blk1 = 2 * it.nt + 1 < p.n_blocks ? 2 * it.nt + 1 : 2 * it.nt;
+    const float* bs0 = p.b_scale + (static_cast<int64_t>(e) * p.n_blocks + 2 * it.nt) * p.num_kb;
+    const float* bs1 = p.b_scale + (static_cast<int64_t>(e) * p.n_blocks + blk1) * p.num_kb;
+    const int b_row = e * p.n_rows + it.nt * BN + static_cast<int>(cr) * BH;
+    float pre0 = 0.0f, pre1 = 0.0f;
+    for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
+      if ((kb & 31) == 0) {
+        const int k = kb + lane;
+        pre0 = k < p.num_kb ? __ldg(bs0 + k) : 0.0f;
+        pre1 = k < p.num_kb ? __ldg(bs1 + k) : 0.0f;
+      }
+      const float s0 = __shfl_sync(0xffffffffu, pre0, kb & 31);
+      const float s1 = __shfl_sync(0xffffffffu, pre1, kb & 31);
+      const int s = kbg % PSTAGES;
+      const uint32_t ph = (kbg / PSTAGES) & 1;
+      const int r = kbg % SRING;
+      const uint32_t rph = (kbg / SRING) & 1;
+      int ok = 1;
+      if (lane == 0)
+        ok = mbar_wait(&C->sempty[r], rph ^ 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort) &&
+             mbar_wait(&C->empty[s], ph ^ 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        alive = false;
+        break;
+      }
+      if (lane == 0) {
+        uint8_t* sa = smem + s * PSTAGE_BYTES;
+        C->bs[r][0] = s0;
+        C->bs[r][1] = s1;
+        mbar_arrive_expect_tx(&C->sfull[r], BM * 4);
+        bulk_load(C->as[r], p.a_scale + static_cast<int64_t>(kb) * p.a_scale_ld + static_cast<int64_t>(mb) * BM,
+                  BM * 4, &C->sfull[r]);
+        const uint32_t full_leader = mapa_shared(smem_u32(&C->full[s]), 0);
+        if (cr == 0) mbar_arrive_expect_tx(&C->full[s], 2 * PSTAGE_BYTES);  // both CTAs' operand bytes
+        tma_load_2d_pair(sa, map_a, full_leader, kb * BK, mb * BM);
+        tma_load_2d_pair(sa + PA_BYTES, map_b, full_leader, kb * BK, b_row);
+      }
+      __syncwarp();
+    }
+  }
+  // Drain: the leader's full barriers count both CTAs' bytes; the scale ring is local.
+  if (lane == 0) {
+    if (cr == 0) {
+      const uint32_t first = kbg > PSTAGES ? kbg - PSTAGES : 0;
+      for (uint32_t i = first; i < kbg; ++i)
+        mbar_wait(&C->full[i % PSTAGES], (i / PSTAGES) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN,
+                  nullptr);
+    }
+    const uint32_t rfirst = kbg > SRING ? kbg - SRING : 0;
+    for (uint32_t i = rfirst; i < kbg; ++i)
+      mbar_wait(&C->sfull[i % SRING], (i / SRING) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ void pair_mma_thread(const GemmParams& p, uint8_t* smem, PairControl* C,
+                                                const PairWalk& pw, uint32_t tmem_base) {
+  volatile int* abort = &C->abort;
+  uint32_t kbg = 0;
+  bool alive = true;
+  const int64_t cluster = blockIdx.x >> 1;
+  const int64_t nclusters = gridDim.x >> 1;
+  for (int64_t w = cluster; w < pw.num_items && alive; w += nclusters) {
+    for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
+      const int s = kbg % PSTAGES;
+      const uint32_t ph = (kbg / PSTAGES) & 1;
+      const int b = kbg & 1;
+      const uint32_t tph = (kbg >> 1) & 1;
+      if (!mbar_wait(&C->tempty[b], tph ^ 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_MMA, abort) ||
+          !mbar_wait(&C->full[s], ph, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_MMA, abort)) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const uint64_t adesc = smem_desc_sw128(smem_u32(smem + s * PSTAGE_BYTES));
+      const uint64_t bdesc = smem_desc_sw128(smem_u32(smem + s * PSTAGE_BYTES + PA_BYTES));
+      const uint32_t d = tmem_base + static_cast<uint32_t>(b * BN);
+#pragma unroll
+      for (int k = 0; k < BK / 32; ++k) mma_e4m3_pair(d, adesc + 2 * k, bdesc + 2 * k, IDESC_PAIR, k > 0 ? 1u : 0u);
+      mma_commit_pair(&C->empty[s], 0x3);
+      mma_commit_pair(&C->tfull[b], 0x3);
+    }
+  }
+  if (kbg > 0) {
+    mma_commit_pair(&C->mma_done, 0x1);
+    mbar_wait(&C->mma_done, 0, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
+  }
+}
+
+template <bool kGateUp>
+__device__ __forceinline__ void pair_epilogue(const GemmParams& p, PairControl* C, const PairWalk& pw,
+                                              uint32_t tmem_base, uint32_t cr, int warp, int lane) {
+  volatile int* abort = &C->abort;
+  const int q = warp & 3;
+  const int h = (warp - 4) >> 2;
+  const int r = q * 32 + lane;
+  const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+  const uint32_t tempty_leader0 = mapa_shared(smem_u32(&C->tempty[0]), 0);
+  const uint32_t tempty_leader1 = mapa_shared(smem_u32(&C->tempty[1]), 0);
+  uint32_t kbg = 0, tiles_done = 0;
+  bool alive = true;
+  const uint32_t c0 = kGateUp ? 64 * h : 128 * h;
+  const uint32_t c1 = c0 + 32;
+  const uint32_t c2 = kGateUp ? 128 + 64 * h : c0 + 64;
+  const uint32_t c3 = c2 + 32;
+  const int sidx_lo = kGateUp ? 0 : h;
+  const int sidx_hi = kGateUp ? 1 : h;
+  const int64_t cluster = blockIdx.x >> 1;
+  const int64_t nclusters = gridDim.x >> 1;
+  for (int64_t w = cluster; w < pw.num_items && alive; w += nclusters) {
+    const PairItem it = pair_item(w, pw);
+    const bool mine = cr == 0 || it.b1 >= 0;  // a repeated partner block stores nothing
+    const int mb = (cr == 0 || it.b1 < 0) ? it.b0 : it.b1;
+    const int64_t prow = static_cast<int64_t>(mb) * BM + r;
+    int pair = 0;
+    float wrow = 1.0f;
+    bool valid = false;
+    if (!kGateUp) {
+      pair = __ldg(p.sorted_ids + prow);
+      valid = pair < p.numel;
+      if (valid && p.topk_weights) wrow = __ldg(p.topk_weights + pair);
+    }
+    float acc[128];
+#pragma unroll
+    for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+    for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
+      const int rs = kbg % SRING;
+      const int b = kbg & 1;
+      int ok = mbar_wait(&C->tfull[b], (kbg >> 1) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE, abort);
+      ok = ok && mbar_wait(&C->sfull[rs], (kbg / SRING) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
+                           abort);
+      if (!__all_sync(0xffffffffu, ok)) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const float sa = C->as[rs][r];
+      const float s_lo = sa * C->bs[rs][sidx_lo];
+      const float s_hi = sa * C->bs[rs][sidx_hi];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&C->sempty[rs]);
+      const uint32_t base = tmem_base + lane_off + static_cast<uint32_t>(b * BN);
+      {
+        float v0[32], v1[32];
+        tmem_ld32(base + c0, v0);
+        tmem_ld32(base + c1, v1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) fma2(acc[i], acc[i + 1], v0[i], v0[i + 1], s_lo);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) fma2(acc[32 + i], acc[33 + i], v1[i], v1[i + 1], s_lo);
+      }
+      {
+        float v2[32], v3[32];
+        tmem_ld32(base + c2, v2);
+        tmem_ld32(base + c3, v3);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        // The loads of this buffer have returned (wait::ld), so the leader may overwrite it:
+        // a relaxed arrive suffices and avoids a cluster-scope fence per K block.
+        if (lane == 0) mbar_arrive_cluster_relaxed(b ? tempty_leader1 : tempty_leader0);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) fma2(acc[64 + i], acc[65 + i], v2[i], v2[i + 1], s_hi);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) fma2(acc[96 + i], acc[97 + i], v3[i], v3[i + 1], s_hi);
+      }
+    }
+    if (!alive) break;
+    if (mine) {
+      if (!finish_tile<kGateUp>(p, C->amax, C->amax_bar, acc, prow, it.nt, h, r, pair, wrow, valid, tiles_done,
+                                lane, abort))
+        break;
+      ++tiles_done;
+    }
+  }
+}
+
+template <bool kGateUp>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    moe_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                         const __grid_constant__ GemmParams p, const int32_t* __restrict__ block_pairs) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PairControl* C = reinterpret_cast<PairControl*>(smem + PSTAGES * PSTAGE_BYTES);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cr = cluster_ctarank();
+
+  const int32_t ntpp = __ldg(p.ntpp);
+  int num_pairs = __ldg(block_pairs);
+  if (ntpp < 0 || ntpp % BM != 0 || ntpp / BM > p.max_blocks || num_pairs < 0 || num_pairs > p.max_blocks) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) set_status(p.status, B2M_STATUS_BAD_ROUTING);
+    num_pairs = 0;
+  }
+  const PairWalk pw{block_pairs, num_pairs, p.num_nt, static_cast<int64_t>(num_pairs) * p.num_nt};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PSTAGES; ++s) {
+      mbar_init(&C->full[s], 1);
+      mbar_init(&C->empty[s], 1);
+    }
+    for (int r = 0; r < SRING; ++r) {
+      mbar_init(&C->sfull[r], 1);
+      mbar_init(&C->sempty[r], NUM_EPI_WARPS);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&C->tfull[b], 1);
+      mbar_init(&C->tempty[b], 2 * NUM_EPI_WARPS);
+      mbar_init(&C->amax_bar[b], NUM_EPI_THREADS);
+    }
+    mbar_init(&C->mma_done, 1);
+    C->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) tmem_alloc_pair(&C->tmem_base, TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or TMA signal
+  tc_fence_after();
+  const uint32_t tmem_base = C->tmem_base;
+
+  if (warp < 4) {
+    reg_dealloc<56>();
+    if (warp == 0) {
+      pair_producer<kGateUp>(&map_a, &map_b, p, smem, C, pw, cr, lane);
+    } else if (warp == 1) {
+      if (lane == 0 && cr == 0) pair_mma_thread(p, smem, C, pw, tmem_base);
+      __syncwarp();
+    }
+  } else {
+    reg_alloc<224>();
+    pair_epilogue<kGateUp>(p, C, pw, tmem_base, cr, warp, lane);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs and the peer's epilogue are done with both CTAs' memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 int encode_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
                   uint32_t box_inner, uint32_t box_outer) {
@@ -488,13 +826,36 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& 
   return check_cuda(cudaGetLastError(), kGateUp ? "gemm1 launch" : "gemm2 launch");
 }
 
+template <bool kGateUp>
+int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, const int32_t* block_pairs,
+                     int num_sms, cudaStream_t s) {
+  static int attr_done[64] = {0};
+  int dev = 0;
+  B2M_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    B2M_TRY(check_cuda(cudaFuncSetAttribute(moe_gemm_pair_kernel<kGateUp>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(PSMEM_BYTES)),
+                       "gemm pair: cudaFuncSetAttribute"));
+    attr_done[dev] = 1;
+  }
+  int64_t upper = static_cast<int64_t>(p.max_blocks) * p.num_nt;  // pairs <= blocks
+  int64_t clusters = num_sms / 2;
+  if (upper < clusters) clusters = upper;
+  if (clusters < 1) clusters = 1;
+  moe_gemm_pair_kernel<kGateUp><<<static_cast<int>(2 * clusters), NUM_THREADS, PSMEM_BYTES, s>>>(ma, mb, p,
+                                                                                                block_pairs);
+  return check_cuda(cudaGetLastError(), kGateUp ? "gemm1 pair launch" : "gemm2 pair launch");
+}
+
 }  // namespace
 }  // namespace b2m
 
 extern "C" int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden,
                          const void* w1, const float* w1_scale, int32_t num_experts, int32_t inter,
-                         const int32_t* expert_ids, const int32_t* num_tokens_post_padded, void* out_q,
-                         float* out_scale_t, int32_t* dev_status, void* stream) {
+                         const int32_t* expert_ids, const int32_t* num_tokens_post_padded,
+                         const int32_t* block_pairs, void* out_q, float* out_scale_t, int32_t* dev_status,
+                         void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
@@ -510,7 +871,8 @@ extern "C" int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t r
   if (rows_cap / BM > INT32_MAX) return fail(B2M_ERR_ARG, "gemm1: sizes overflow int32 indices");
   CUtensorMap ma, mb;
   B2M_TRY(encode_map_2d(&ma, a_sorted, hidden, rows_cap, hidden, BK, BM));
-  B2M_TRY(encode_map_2d(&mb, w1, hidden, static_cast<uint64_t>(num_experts) * 2 * inter, hidden, BK, BN));
+  B2M_TRY(encode_map_2d(&mb, w1, hidden, static_cast<uint64_t>(num_experts) * 2 * inter, hidden, BK,
+                        block_pairs ? BH : BN));
   GemmParams p{};
   p.expert_ids = expert_ids;
   p.ntpp = num_tokens_post_padded;
@@ -529,13 +891,15 @@ extern "C" int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t r
   p.hidden = hidden;
   p.status = dev_status;
   p.timeout_ns = timeout_ns();
+  if (block_pairs) return launch_gemm_pair<true>(ma, mb, p, block_pairs, num_sms, static_cast<cudaStream_t>(stream));
   return launch_gemm<true>(ma, mb, p, num_sms, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int32_t inter, const void* w2,
                          const float* w2_scale, int32_t num_experts, int64_t hidden, const int32_t* sorted_token_ids,
-                         const int32_t* expert_ids, const int32_t* num_tokens_post_padded, int64_t numel,
-                         const float* topk_weights, void* out_bf16, int32_t* dev_status, void* stream) {
+                         const int32_t* expert_ids, const int32_t* num_tokens_post_padded,
+                         const int32_t* block_pairs, int64_t numel, const float* topk_weights, void* out_bf16,
+                         int32_t* dev_status, void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
@@ -551,7 +915,8 @@ extern "C" int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows
   if (rows_cap / BM > INT32_MAX || numel >= INT32_MAX) return fail(B2M_ERR_ARG, "gemm2: sizes overflow int32");
   CUtensorMap ma, mb;
   B2M_TRY(encode_map_2d(&ma, a_fp8, inter, rows_cap, inter, BK, BM));
-  B2M_TRY(encode_map_2d(&mb, w2, inter, static_cast<uint64_t>(num_experts) * hidden, inter, BK, BN));
+  B2M_TRY(encode_map_2d(&mb, w2, inter, static_cast<uint64_t>(num_experts) * hidden, inter, BK,
+                        block_pairs ? BH : BN));
   GemmParams p{};
   p.sorted_ids = sorted_token_ids;
   p.expert_ids = expert_ids;
@@ -572,5 +937,7 @@ extern "C" int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows
   p.hidden = hidden;
   p.status = dev_status;
   p.timeout_ns = timeout_ns();
+  if (block_pairs)
+    return launch_gemm_pair<false>(ma, mb, p, block_pairs, num_sms, static_cast<cudaStream_t>(stream));
   return launch_gemm<false>(ma, mb, p, num_sms, static_cast<cudaStream_t>(stream));
 }

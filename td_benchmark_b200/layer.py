@@ -25,6 +25,11 @@ import torch
 from . import ops
 
 BM = 128
+# GEMMs on CTA pairs (cta_group::2, two 128-row blocks of one expert per work item).
+# Off by default: with per-128-K promotion the TMEM hand-off per K block limits both
+# variants alike, and the paired one loses the odd trailing block of every expert
+# (measured on B200: equal on the Mixtral shape, slower on DeepSeek-V3).
+PAIRED_GEMM = False
 
 
 @dataclass
@@ -67,6 +72,10 @@ class _Routing:
         self.expert_ids = torch.empty(self.nblk, dtype=torch.int32, device=device)
         self.ntpp = torch.empty(1, dtype=torch.int32, device=device)
         self.pair_pos = torch.empty(numel, dtype=torch.int32, device=device)
+        self.block_pairs = torch.empty(1 + 2 * self.nblk, dtype=torch.int32, device=device)
+
+    def pairs(self, paired: bool) -> torch.Tensor | None:
+        return self.block_pairs if paired else None
 
 
 class SharedExpert:
@@ -91,6 +100,14 @@ class SharedExpert:
         self.route.expert_ids.copy_(eids)
         self.route.ntpp.fill_(nb * BM)
         self.route.pair_pos.copy_(torch.arange(rows, dtype=torch.int32))
+        bp = torch.full((1 + 2 * self.route.nblk,), -1, dtype=torch.int32)
+        npairs = (nb + 1) // 2
+        bp[0] = npairs
+        for i in range(npairs):
+            bp[1 + 2 * i] = 2 * i
+            bp[2 + 2 * i] = 2 * i + 1 if 2 * i + 1 < nb else -1
+        self.route.block_pairs.copy_(bp)
+        self.paired = PAIRED_GEMM and nb >= 2
         H = weights.hidden
         self.a = torch.empty((self.route.rows_cap, H), dtype=ops.FP8, device=device)
         self.as_t = torch.empty((H // 128, self.route.rows_cap), dtype=torch.float32, device=device)
@@ -104,10 +121,11 @@ class SharedExpert:
 
     def run(self, status: torch.Tensor | None) -> torch.Tensor:
         r = self.route
+        bp = r.pairs(self.paired)
         ops.gemm1(self.a, self.as_t, self.w.w1i, self.w.w1i_scale, r.expert_ids, r.ntpp, self.inter_q, self.inter_st,
-                  status)
+                  status, block_pairs=bp)
         ops.gemm2(self.inter_q, self.inter_st, self.w.w2, self.w.w2_scale, r.sorted_ids, r.expert_ids, r.ntpp,
-                  r.numel, None, self.out, status)
+                  r.numel, None, self.out, status, block_pairs=bp)
         return self.out
 
 
@@ -325,6 +343,9 @@ class MoELayer:
         self.out_local = torch.empty((self.T_local, H), dtype=torch.bfloat16, device=dev)
         self.status = ops.new_status(dev)
         self.events: list | None = None   # set to [] to record (name, cuda.Event) around the GEMMs
+        # CTA pairs need two blocks of one expert; with under 2 blocks per expert on
+        # average (decode shapes) a pair would mostly run with an idle partner.
+        self.paired = PAIRED_GEMM and self.numel >= 2 * BM * global_num_experts
         self.shared = None
         self.shared_local = None
         if shared is not None:
@@ -343,17 +364,18 @@ class MoELayer:
         """Alignment, then quantisation + (all-gather) + row dispatch into expert order."""
         r = self.route
         ops.moe_align_block_size(topk_ids, BM, self.E, self.expert_map, out=(r.sorted_ids, r.expert_ids, r.ntpp),
-                                 pair_pos=r.pair_pos)
+                                 pair_pos=r.pair_pos, block_pairs=r.pairs(self.paired))
         self.exchange.gather_dispatch(self, x_local)
 
     def experts(self, topk_weights: torch.Tensor) -> None:
         r = self.route
         self._event("gemm1_start")
+        bp = r.pairs(self.paired)
         ops.gemm1(self.a_sorted, self.as_t, self.w.w1i, self.w.w1i_scale, r.expert_ids, r.ntpp, self.inter_q,
-                  self.inter_st, self.status)
+                  self.inter_st, self.status, block_pairs=bp)
         self._event("gemm1_end")
         ops.gemm2(self.inter_q, self.inter_st, self.w.w2, self.w.w2_scale, r.sorted_ids, r.expert_ids, r.ntpp,
-                  self.numel, topk_weights.reshape(-1), self.staged, self.status)
+                  self.numel, topk_weights.reshape(-1), self.staged, self.status, block_pairs=bp)
         self._event("gemm2_end")
 
     def kernel_launches(self) -> int:

@@ -124,11 +124,12 @@ def align_sizes(numel: int, num_experts: int, block_size: int) -> tuple[int, int
 def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int,
                          expert_map: torch.Tensor | None = None,
                          out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None,
-                         pair_pos: torch.Tensor | None = None
+                         pair_pos: torch.Tensor | None = None, block_pairs: torch.Tensor | None = None
                          ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Same signature and outputs as vLLM's ``moe_align_block_size`` (without the padding flags).
 
-    ``pair_pos`` (int32 [numel], optional) also receives each pair's sorted position (-1: non-local)."""
+    ``pair_pos`` (int32 [numel], optional) also receives each pair's sorted position (-1: non-local);
+    ``block_pairs`` (int32 [1 + 2*nblk], optional) the block-pair work list of the paired-CTA GEMMs."""
     _cuda(topk_ids, "topk_ids")
     _need(topk_ids.dtype == torch.int32 and topk_ids.is_contiguous(), "topk_ids must be contiguous int32")
     numel = topk_ids.numel()
@@ -143,9 +144,12 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: i
         _need(expert_map.dtype == torch.int32 and expert_map.numel() >= num_experts, "expert_map must be int32 [E]")
     if pair_pos is not None:
         _need(pair_pos.dtype == torch.int32 and pair_pos.numel() == numel, "pair_pos must be int32 [numel]")
+    if block_pairs is not None:
+        _need(block_pairs.dtype == torch.int32 and block_pairs.numel() >= 1 + 2 * expert_ids.numel(),
+              "block_pairs must be int32 [1 + 2*len(expert_ids)]")
     _lib.call("b2m_align", topk_ids.data_ptr(), numel, num_experts, block_size, _ptr(expert_map),
               sorted_ids.data_ptr(), sorted_ids.numel(), expert_ids.data_ptr(), expert_ids.numel(),
-              ntpp.data_ptr(), _ptr(pair_pos), _stream(topk_ids.device))
+              ntpp.data_ptr(), _ptr(pair_pos), _ptr(block_pairs), _stream(topk_ids.device))
     return sorted_ids, expert_ids, ntpp
 
 
@@ -165,8 +169,8 @@ def w1_interleave(w1: torch.Tensor, w1_scale: torch.Tensor) -> tuple[torch.Tenso
 
 def gemm1(a_sorted: torch.Tensor, a_scale_t: torch.Tensor, w1i: torch.Tensor, w1i_scale: torch.Tensor,
           expert_ids: torch.Tensor, ntpp: torch.Tensor, out_q: torch.Tensor | None = None,
-          out_scale_t: torch.Tensor | None = None, status: torch.Tensor | None = None
-          ) -> tuple[torch.Tensor, torch.Tensor]:
+          out_scale_t: torch.Tensor | None = None, status: torch.Tensor | None = None,
+          block_pairs: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Gate/up grouped GEMM + SiLU*mul + 1x128 requant on expert-sorted A.
 
     a_sorted e4m3 [rows_cap, H], a_scale_t fp32 [H/128, rows_cap] -> (q [rows_cap, I], scale_t [I/128, rows_cap])."""
@@ -183,15 +187,15 @@ def gemm1(a_sorted: torch.Tensor, a_scale_t: torch.Tensor, w1i: torch.Tensor, w1
     if out_scale_t is None:
         out_scale_t = torch.empty((inter // 128, rows_cap), dtype=torch.float32, device=a_sorted.device)
     _lib.call("b2m_gemm1", a_sorted.data_ptr(), a_scale_t.data_ptr(), rows_cap, hidden, w1i.data_ptr(),
-              w1i_scale.data_ptr(), e, inter, expert_ids.data_ptr(), ntpp.data_ptr(), out_q.data_ptr(),
-              out_scale_t.data_ptr(), _ptr(status), _stream(a_sorted.device))
+              w1i_scale.data_ptr(), e, inter, expert_ids.data_ptr(), ntpp.data_ptr(), _ptr(block_pairs),
+              out_q.data_ptr(), out_scale_t.data_ptr(), _ptr(status), _stream(a_sorted.device))
     return out_q, out_scale_t
 
 
 def gemm2(a_q: torch.Tensor, a_scale_t: torch.Tensor, w2: torch.Tensor, w2_scale: torch.Tensor,
           sorted_ids: torch.Tensor, expert_ids: torch.Tensor, ntpp: torch.Tensor, numel: int,
           topk_weights: torch.Tensor | None, out: torch.Tensor | None = None,
-          status: torch.Tensor | None = None) -> torch.Tensor:
+          status: torch.Tensor | None = None, block_pairs: torch.Tensor | None = None) -> torch.Tensor:
     """Down grouped GEMM, routed weight in the epilogue.  Returns bf16 [numel, H] indexed by flat pair."""
     _cuda(a_q, "a_q")
     rows_cap, inter = a_q.shape
@@ -204,8 +208,8 @@ def gemm2(a_q: torch.Tensor, a_scale_t: torch.Tensor, w2: torch.Tensor, w2_scale
     if out is None:
         out = torch.empty((numel, hidden), dtype=torch.bfloat16, device=a_q.device)
     _lib.call("b2m_gemm2", a_q.data_ptr(), a_scale_t.data_ptr(), rows_cap, inter, w2.data_ptr(), w2_scale.data_ptr(),
-              e, hidden, sorted_ids.data_ptr(), expert_ids.data_ptr(), ntpp.data_ptr(), numel, _ptr(topk_weights),
-              out.data_ptr(), _ptr(status), _stream(a_q.device))
+              e, hidden, sorted_ids.data_ptr(), expert_ids.data_ptr(), ntpp.data_ptr(), _ptr(block_pairs), numel,
+              _ptr(topk_weights), out.data_ptr(), _ptr(status), _stream(a_q.device))
     return out
 
 

@@ -95,6 +95,34 @@ def test_align_expert_map():
     assert np.array_equal(pp.cpu().numpy(), _inverse(sr, ids.numel(), er))
 
 
+def test_align_block_pairs():
+    E = 16
+    ids = _ids(1000, 4, E, 3, zipf=True)
+    emap = torch.full((E,), -1, dtype=torch.int32)
+    emap[4:12] = torch.arange(8, dtype=torch.int32)
+    for m in (None, emap):
+        nblk = ops.align_sizes(ids.numel(), E, 128)[1]
+        bp = torch.full((1 + 2 * nblk,), -7, dtype=torch.int32, device=DEV)
+        s, e, n = ops.moe_align_block_size(ids.to(DEV), 128, E, None if m is None else m.to(DEV), block_pairs=bp)
+        er = e.cpu().numpy()
+        bpn = bp.cpu().numpy()
+        got = [(bpn[1 + 2 * i], bpn[2 + 2 * i]) for i in range(bpn[0])]
+        exp = []
+        nb = int(n.item()) // 128
+        b = 0
+        while b < nb:
+            if er[b] < 0:
+                b += 1
+                continue
+            if b + 1 < nb and er[b + 1] == er[b]:
+                exp.append((b, b + 1))
+                b += 2
+            else:
+                exp.append((b, -1))
+                b += 1
+        assert got == exp
+
+
 def test_align_rejects_small_buffers():
     from td_benchmark_b200._lib import B2MError
     ids = _ids(64, 2, 8, 1).to(DEV)
@@ -181,22 +209,25 @@ def _deq_w(q, s):
     return qn * sn
 
 
+@pytest.mark.parametrize("paired", [True, False], ids=["pair", "single"])
 @pytest.mark.parametrize("T,H,I,E,k,zipf", [(200, 512, 256, 4, 2, False), (64, 256, 512, 8, 2, False),
-                                            (300, 1024, 384, 16, 4, True), (5, 256, 128, 8, 2, False)])
-def test_gemm1_gemm2_against_float64(T, H, I, E, k, zipf):
+                                            (300, 1024, 384, 16, 4, True), (5, 256, 128, 8, 2, False),
+                                            (700, 256, 256, 3, 2, False)])
+def test_gemm1_gemm2_against_float64(T, H, I, E, k, zipf, paired):
     x, w1q, w1s, w2q, w2s, ids, wts = _gemm_problem(T, H, I, E, k, T + H, zipf)
     xq, xs = ops.quant_g128(x.to(DEV))
     w1i, w1is = ops.w1_interleave(w1q.to(DEV), w1s.to(DEV))
     pp = torch.empty(T * k, dtype=torch.int32, device=DEV)
-    sorted_ids, eids, ntpp = ops.moe_align_block_size(ids.to(DEV), 128, E, pair_pos=pp)
+    bp = torch.empty(1 + 2 * ops.align_sizes(T * k, E, 128)[1], dtype=torch.int32, device=DEV) if paired else None
+    sorted_ids, eids, ntpp = ops.moe_align_block_size(ids.to(DEV), 128, E, pair_pos=pp, block_pairs=bp)
     rows_cap = eids.numel() * 128
     a_sorted = torch.empty((rows_cap, H), dtype=torch.float8_e4m3fn, device=DEV)
     a_st = torch.empty((H // 128, rows_cap), dtype=torch.float32, device=DEV)
     ops.dispatch_rows(xq, xs, pp, k, a_sorted, a_st)
     status = ops.new_status(DEV)
-    hq, hst = ops.gemm1(a_sorted, a_st, w1i, w1is, eids, ntpp, status=status)
+    hq, hst = ops.gemm1(a_sorted, a_st, w1i, w1is, eids, ntpp, status=status, block_pairs=bp)
     staged = ops.gemm2(hq, hst, w2q.to(DEV), w2s.to(DEV), sorted_ids, eids, ntpp, T * k, wts.reshape(-1).to(DEV),
-                       status=status)
+                       status=status, block_pairs=bp)
     torch.cuda.synchronize()
     ops.check_status(status)
     n = int(ntpp.item())
@@ -228,22 +259,24 @@ def test_gemm1_gemm2_against_float64(T, H, I, E, k, zipf):
     np.testing.assert_allclose(got, y, rtol=2 ** -7, atol=1e-3 * np.abs(y).max())
 
 
-def test_gemm_skips_non_local_experts():
+@pytest.mark.parametrize("paired", [True, False], ids=["pair", "single"])
+def test_gemm_skips_non_local_experts(paired):
     T, H, I, E, k = 128, 256, 128, 8, 2
     x, w1q, w1s, w2q, w2s, ids, wts = _gemm_problem(T, H, I, E, k, 77)
     emap = torch.full((E,), -1, dtype=torch.int32)
     emap[2:4] = torch.tensor([0, 1], dtype=torch.int32)
     w1i, w1is = ops.w1_interleave(w1q[2:4].contiguous().to(DEV), w1s[2:4].contiguous().to(DEV))
     pp = torch.empty(T * k, dtype=torch.int32, device=DEV)
-    sorted_ids, eids, ntpp = ops.moe_align_block_size(ids.to(DEV), 128, E, emap.to(DEV), pair_pos=pp)
+    bp = torch.empty(1 + 2 * ops.align_sizes(T * k, E, 128)[1], dtype=torch.int32, device=DEV) if paired else None
+    sorted_ids, eids, ntpp = ops.moe_align_block_size(ids.to(DEV), 128, E, emap.to(DEV), pair_pos=pp, block_pairs=bp)
     rows_cap = eids.numel() * 128
     a_sorted = torch.empty((rows_cap, H), dtype=torch.float8_e4m3fn, device=DEV)
     a_st = torch.empty((H // 128, rows_cap), dtype=torch.float32, device=DEV)
     ops.quant_dispatch(x.to(DEV), pp, k, a_sorted, a_st)
     staged = torch.full((T * k, H), float("nan"), dtype=torch.bfloat16, device=DEV)
-    hq, hst = ops.gemm1(a_sorted, a_st, w1i, w1is, eids, ntpp)
+    hq, hst = ops.gemm1(a_sorted, a_st, w1i, w1is, eids, ntpp, block_pairs=bp)
     ops.gemm2(hq, hst, w2q[2:4].contiguous().to(DEV), w2s[2:4].contiguous().to(DEV), sorted_ids, eids, ntpp, T * k,
-              wts.reshape(-1).to(DEV), out=staged)
+              wts.reshape(-1).to(DEV), out=staged, block_pairs=bp)
     out = ops.combine(staged, k, ids.to(DEV), emap.to(DEV))
     torch.cuda.synchronize()
     local = ((ids == 2) | (ids == 3)).reshape(-1)
