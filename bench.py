@@ -28,7 +28,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -60,52 +59,91 @@ def _peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event-reason sampling during the timed region.
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
+    A thread reads this GPU's NVML counters (read-only queries; nothing is set) every
+    `period` seconds; NVML is initialised and the device handle resolved (by UUID, so
+    CUDA and NVML orderings cannot be confused) before the region starts, and one
+    sample is taken synchronously at entry and at exit so that even a region of a few
+    milliseconds has samples.  Records the SM clock, its maximum and the reasons
+    hw_slowdown / hw_thermal_slowdown / sw_thermal_slowdown / sw_power_cap.
+    """
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap", 0x4))
+
+    def __init__(self, device, period: float = 0.002):
+        import threading
+        self.period = period
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.error = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.nv = None
+        try:
+            import pynvml as nv
+            import torch
+            nv.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.h = nv.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+            self._reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.masks = [(n, int(getattr(nv, attr, bit))) for n, attr, bit in self.REASONS]
+            self.nv = nv
+        except Exception as e:  # no NVML: the line says so
+            self.error = f"{type(e).__name__}: {e}"
+
+    def _sample(self) -> None:
+        self.samples.append((float(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)),
+                             int(self._reasons(self.h))))
+
+    def _loop(self) -> None:
+        while not self._stop.wait(self.period):
+            try:
+                self._sample()
+            except Exception as e:
+                self.error = f"{type(e).__name__}: {e}"
+                return
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+        import threading
+        if self.nv is not None:
+            self._sample()
+            self._thread = threading.Thread(target=self._loop, daemon=True)
+            self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        if self._thread is not None:
+            self._sample()
+            self._stop.set()
+            self._thread.join()
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = [c for c, _ in self.samples]
+        reasons = sorted({n for _, r in self.samples for n, m in self.masks if r & m}) if self.nv else []
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+               "samples": len(sm), "source": "NVML"}
+        if self.error:
+            out["error"] = self.error
+        return out
+
+    @staticmethod
+    def merge(parts: list[dict]) -> dict:
+        """All ranks' summaries: median of the per-rank medians, lowest rank median, union of reasons."""
+        med = [p["sm_mhz"] for p in parts if p.get("sm_mhz") is not None]
+        out = {"sm_mhz": statistics.median(med) if med else None,
+               "sm_mhz_min_rank": min(med) if med else None,
+               "sm_max_mhz": max((p["sm_max_mhz"] for p in parts if p.get("sm_max_mhz")), default=None),
+               "reasons": sorted({r for p in parts for r in p.get("reasons", [])}),
+               "samples": sum(p.get("samples", 0) for p in parts), "ranks": len(parts), "source": "NVML"}
+        errs = [p["error"] for p in parts if p.get("error")]
+        if errs:
+            out["error"] = errs[0]
+        return out
 
 
 def gemm1_flops(topk_ids, expert_map, inter_local: int, hidden: int) -> float:
@@ -210,6 +248,38 @@ def run_reference(args) -> int:
     return 0
 
 
+def _stages(starts, ends, evs) -> dict:
+    """Median duration (us) of each stage of a step, keyed by the event that closes it.
+
+    Every step records the same sequence of named events, so the list splits evenly."""
+    n = len(evs) // max(1, len(starts))
+    acc: dict[str, list[float]] = {}
+    for i, (a, b) in enumerate(zip(starts, ends)):
+        seq = evs[i * n:(i + 1) * n] + [("step_end", b)]
+        prev = a
+        for name, ev in seq:
+            acc.setdefault(name, []).append(prev.elapsed_time(ev) * 1e3)
+            prev = ev
+    return {k: statistics.median(v) for k, v in acc.items()}
+
+
+def _max_over_ranks(d: dict, world: int, dev) -> dict:
+    import torch
+    import torch.distributed as dist
+    if world == 1 or not d:
+        return d
+    v = torch.tensor(list(d.values()), dtype=torch.float64, device=dev)
+    dist.all_reduce(v, op=dist.ReduceOp.MAX)
+    return dict(zip(d.keys(), v.tolist()))
+
+
+def _before_gemm1(starts, evs) -> float:
+    """Mean time (ms) from each step's start to its gate/up GEMM launch point."""
+    g = [ev for name, ev in evs if name == "gemm1_start"]
+    t = [a.elapsed_time(b) for a, b in zip(starts, g)]
+    return sum(t) / max(1, len(t))
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -220,6 +290,10 @@ def main() -> int:
     ap.add_argument("--impl", default="b2m", choices=["b2m", "reference"])
     ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"],
                     help="exchange of the multi-GPU layer: fused peer memory (default) or NCCL")
+    ap.add_argument("--rs-mode", default="sm", choices=["sm", "ce"],
+                    help="fused reduce-scatter: SM stores into the owners' slots (default) or copy-engine push")
+    ap.add_argument("--chunks", type=int, default=4, help="down-GEMM column chunks of the copy-engine push")
+    ap.add_argument("--ce-streams", type=int, default=2, help="side streams carrying the copy-engine push")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -244,7 +318,11 @@ def main() -> int:
     code = SCHEME[(cfg.parallel, args.comm)]
     spec = REGISTRY[code][0]
     bundle = data.build_bundle(cfg, rank=rank, world_size=world, device=dev)
-    layer, level = build_layer(spec, cfg, ctx, bundle)
+    exchange = None
+    if world > 1 and args.comm == "p2p":
+        from td_benchmark_b200.layer import P2PExchange
+        exchange = P2PExchange(ctx.group, chunks=args.chunks, rs_mode=args.rs_mode, ce_streams=args.ce_streams)
+    layer, level = build_layer(spec, cfg, ctx, bundle, exchange=exchange)
     T = layer.T
     x = bundle.hidden_local.contiguous()
     ids = bundle.routing.topk_ids_full.contiguous()
@@ -255,37 +333,56 @@ def main() -> int:
         if world > 1:
             dist.barrier()
 
-    # ---- device-timed steps (inputs resident)
-    for _ in range(args.warmup):
-        layer.forward(x, ids, wts)
-    torch.cuda.synchronize()
-    layer.check()
-    barrier()
-    torch.cuda.synchronize()
+    # ---- device-timed steps (inputs resident).  Warm-up steps run exactly what a timed
+    # step runs (flush included) so that no first launch or lazy module load lands in
+    # the timed region; the clock sampler is up before the barrier that opens it.
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     layer.events = []
-    with ClockSampler(dev.index) as clk:
+    for _ in range(args.warmup):
+        flush.zero_()
+        layer.forward(x, ids, wts)
+    torch.cuda.synchronize()
+    layer.check()
+    layer.events = []
+    clk = ClockSampler(dev)
+    host_s = 0.0
+    with clk:
+        barrier()
+        torch.cuda.synchronize()
         for i in range(args.steps):
             flush.zero_()
             starts[i].record()
+            h0 = time.perf_counter()
             layer.forward(x, ids, wts)
+            host_s += time.perf_counter() - h0
             ends[i].record()
         torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     layer.check()
     local = torch.tensor([s.elapsed_time(e) for s, e in zip(starts, ends)], dtype=torch.float64, device=dev)
-    g1 = []
     evs = layer.events
+    pre_g1 = _before_gemm1(starts, evs)
+    stages = _max_over_ranks(_stages(starts, ends, evs), world, dev)
+    g1 = []
     layer.events = None
-    for i in range(0, len(evs), 3):
-        (_, a), (_, b) = evs[i], evs[i + 1]
-        g1.append(a.elapsed_time(b))
+    start = None
+    for name, ev in evs:
+        if name == "gemm1_start":
+            start = ev
+        elif name == "gemm1_end" and start is not None:
+            g1.append(start.elapsed_time(ev))
+            start = None
     if world > 1:
         dist.all_reduce(local, op=dist.ReduceOp.MAX)
     per_step = local.cpu().tolist()
     ms = sum(per_step) / len(per_step)
+    clocks = clk.summary()
+    if world > 1:
+        parts = [None] * world
+        dist.all_gather_object(parts, clocks)
+        clocks = ClockSampler.merge(parts)
 
     # ---- exposed communication (fused exchange, N > 1): the same kernels on local data
     # with every peer flag already satisfied and nothing sent; exposed = fused - that.
@@ -293,18 +390,26 @@ def main() -> int:
     if world > 1 and getattr(layer.exchange, "name", "") == "p2p":
         layer.exchange.compute_only = True
         for _ in range(args.warmup):
+            flush.zero_()
             layer.forward(x, ids, wts)
         torch.cuda.synchronize()
         barrier()
         c_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         c_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        layer.events = []
         for i in range(args.steps):
             flush.zero_()
             c_s[i].record()
             layer.forward(x, ids, wts)
             c_e[i].record()
         torch.cuda.synchronize()
+        c_pre_g1 = _before_gemm1(c_s, layer.events)
+        c_stages = _max_over_ranks(_stages(c_s, c_e, layer.events), world, dev)
+        layer.events = None
         layer.exchange.compute_only = False
+        pre = torch.tensor([pre_g1, c_pre_g1], dtype=torch.float64, device=dev)
+        dist.all_reduce(pre, op=dist.ReduceOp.MAX)
+        pre_f, pre_c = (float(v) * 1e3 for v in pre.tolist())
         c_local = torch.tensor([a.elapsed_time(b) for a, b in zip(c_s, c_e)], dtype=torch.float64, device=dev)
         dist.all_reduce(c_local, op=dist.ReduceOp.MAX)
         c_ms = float(c_local.mean().item())
@@ -312,6 +417,9 @@ def main() -> int:
         ag_bytes = (world - 1) * layer.T_local * (H_ + 4 * H_ // 128)
         rs_bytes = (world - 1) * layer.T_local * H_ * 2
         comm = {"compute_only_us": c_ms * 1e3, "fused_us": ms * 1e3, "exposed_comm_us": (ms - c_ms) * 1e3,
+                "exposed_all_gather_us": pre_f - pre_c, "exposed_reduce_scatter_us": (ms - c_ms) * 1e3 - (pre_f - pre_c),
+                "stages_us_max_over_ranks": {"fused": {k: round(v, 1) for k, v in stages.items()},
+                                             "compute_only": {k: round(v, 1) for k, v in c_stages.items()}},
                 "nvlink_bytes_per_rank": {"all_gather_in": ag_bytes, "reduce_scatter_out": rs_bytes},
                 "how": "same kernels with peer flags pre-satisfied and local data (no traffic); per-step max over ranks"}
         barrier()
@@ -334,9 +442,11 @@ def main() -> int:
         out_h.copy_(out, non_blocking=True)
 
     for _ in range(args.warmup):
+        flush.zero_()
         e2e_step()
     torch.cuda.synchronize()
     barrier()
+    torch.cuda.synchronize()
     e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     for i in range(args.steps):
@@ -380,11 +490,16 @@ def main() -> int:
         line = {
             "metric": "moe_layer_tokens_per_s", "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3,
+            "ms_per_step_min": min(per_step), "ms_per_step_median": statistics.median(per_step),
+            "host_enqueue_us_per_step": host_s / args.steps * 1e6,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp8-e4m3 (fp32 accum)",
             "data": "synthetic (seeded, BASELINE value distributions)",
             "config": {"workload": label, "tokens": T, "hidden": s.K, "intermediate": s.intermediate,
                        "experts": s.E, "top_k": s.top_k, "parallelism": f"{spec.parallel.lower()}{world}",
                        "scheme": code, "shard_level": level, "routing": cfg.routing.imbalance_kind,
+                       "exchange": (f"p2p rs={args.rs_mode} chunks={len(layer.exchange.chunk_cols)}"
+                                    if getattr(layer.exchange, "name", "") == "p2p" else
+                                    getattr(layer.exchange, "name", "none")),
                        "l2": "weights > L2 and 256 MB L2 flush between timed steps"},
             "e2e": {"value": T / (e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e_ms},
@@ -394,7 +509,7 @@ def main() -> int:
                          "peak_source": peak_src, "traffic": traffic, "gemm1_ms": g1_ms,
                          "layer_tflops": lf / (ms * 1e-3) / 1e12,
                          "layer_frac_of_fp8_peak": lf / (ms * 1e-3) / 1e12 / fp8_peak},
-            "clocks": clk.summary(),
+            "clocks": clocks,
             "comm": comm,
             "cpu_baseline": cpu,
         }

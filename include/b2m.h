@@ -157,11 +157,17 @@ int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, in
  * w(pair) = topk_weights[pair] (flat [T*k] fp32), or 1 when topk_weights is NULL.
  * a_fp8 / a_scale_t: K3's out_q / out_scale_t; w2: e4m3 [E, hidden, I];
  * w2_scale: fp32 [E, ceil(hidden/128), I/128]; out: bf16 [numel, hidden] indexed by pair.
- * hidden % 128 == 0, I % 128 == 0.  block_pairs as for b2m_gemm1. */
+ * hidden % 128 == 0, I % 128 == 0.  block_pairs as for b2m_gemm1.
+ * Only output columns [col_begin, col_end) are computed (col_begin a multiple of 256,
+ * col_end a multiple of 256 or hidden; col_end <= 0 means hidden): the reduce-scatter
+ * of one column chunk can then overlap the GEMM of the next, as the reference's N-split
+ * chunks do (overlap_forward.py:564-608).  max_ctas > 0 caps the persistent grid so
+ * that SMs stay free for a concurrently running exchange kernel. */
 int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int32_t inter, const void* w2,
               const float* w2_scale, int32_t num_experts, int64_t hidden, const int32_t* sorted_token_ids,
               const int32_t* expert_ids, const int32_t* num_tokens_post_padded, const int32_t* block_pairs,
-              int64_t numel, const float* topk_weights, void* out_bf16, int32_t* dev_status, void* stream);
+              int64_t numel, const float* topk_weights, void* out_bf16, int64_t col_begin, int64_t col_end,
+              int32_t max_ctas, int32_t* dev_status, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Top-k combine (+ shared expert add).
@@ -189,6 +195,14 @@ int b2m_symm_free(void* dev_ptr);
 int b2m_ipc_handle(void* dev_ptr, void* handle_out);
 int b2m_ipc_open(const void* handle, void** peer_ptr);
 int b2m_ipc_close(void* peer_ptr);
+
+/* Copy-engine transfers between own and peer (IPC-mapped) device memory or pinned host
+ * memory, enqueued on `stream`: one cudaMemcpyAsync / cudaMemcpy2DAsync each (pitches
+ * and width in bytes).  Used to push a rank's all-gather rows and reduce-scatter blocks
+ * and their epoch flags without occupying SMs. */
+int b2m_copy_async(void* dst, const void* src, int64_t bytes, void* stream);
+int b2m_copy2d_async(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+                     void* stream);
 
 /* All-gather push: quantise x [rows, hidden] (rule of K1) and store codes / scales
  * into rows [row0, row0+rows) of every rank's gather buffers q_dst[r] (e4m3
@@ -221,19 +235,28 @@ int b2m_dispatch_rows_wait(const void* xq, const float* xs, int64_t tokens, int6
                            int32_t top_k, void* a_sorted, float* a_scale_t, int64_t rows_cap, const uint32_t* flags,
                            int32_t world, int32_t rank, uint32_t epoch, int32_t* dev_status, void* stream);
 
-/* Reduce-scatter push: the combine of b2m_combine over all T tokens; token t's bf16
- * partial row goes to owner q = t / (T/world), row rank*(T/world) + t - q*(T/world)
- * of slot_dst[q] (bf16 [world*T/world, hidden] on rank q); then *flag_dst[q] = epoch. */
-int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, const int32_t* topk_ids,
-                     const int32_t* expert_map, const void* shared, int32_t world, int32_t rank,
-                     void* const* slot_dst, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
-                     void* stream);
+/* Reduce-scatter push: the combine of b2m_combine over all T tokens for output columns
+ * [col_begin, col_end) (8-aligned; col_end <= 0 means hidden); token t's bf16 partial
+ * goes to owner q = t / (T/world), row rank*(T/world) + t - q*(T/world) of slot_dst[q]
+ * (bf16 [world*T/world, hidden] on rank q); then *flag_dst[q] = epoch.  max_ctas > 0
+ * caps the grid (the push shares the GPU with the next chunk's down GEMM).  With
+ * counter == NULL nothing is published (flag_dst may be NULL): the partials are only
+ * stored, e.g. into a local staging buffer that copy engines push afterwards. */
+int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, int64_t col_begin,
+                     int64_t col_end, const int32_t* topk_ids, const int32_t* expert_map, const void* shared,
+                     int32_t world, int32_t rank, void* const* slot_dst, uint32_t* const* flag_dst, uint32_t epoch,
+                     int32_t* counter, int32_t max_ctas, void* stream);
 
-/* Owner side of the reduce-scatter: once flags[0..world) >= epoch,
- * out[t, :] = bf16( sum_{r=0..world-1} slots[r*rows + t, :] + add[t, :] )  (fp32, rank order).
- * add (bf16 [rows, hidden]) may be NULL. */
-int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world, const uint32_t* flags,
-                  uint32_t epoch, const void* add, void* out, int32_t* dev_status, void* stream);
+/* One thread publishes epoch to every flag_dst[r] (system-scope release after a
+ * system fence), ordered after all earlier work on `stream`. */
+int b2m_signal(uint32_t* const* flag_dst, int32_t world, uint32_t epoch, void* stream);
+
+/* Owner side of the reduce-scatter: once the nchunks*world flags (chunk-major) are all
+ * >= epoch, out[t, :] = bf16( sum_{r=0..world-1} slots[r*rows + t, :] + add[t, :] )
+ * (fp32, rank order).  add (bf16 [rows, hidden]) may be NULL. */
+int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world, int32_t nchunks,
+                  const uint32_t* flags, uint32_t epoch, const void* add, void* out, int32_t* dev_status,
+                  void* stream);
 
 #ifdef __cplusplus
 }

@@ -26,8 +26,10 @@ SIGNATURES: dict[str, list] = {
     "b2m_align": [_p, _i64, _i32, _i32, _p, _p, _i64, _p, _i64, _p, _p, _p, _p],
     "b2m_w1_interleave": [_p, _p, _i32, _i32, _i64, _p, _p, _p],
     "b2m_gemm1": [_p, _p, _i64, _i64, _p, _p, _i32, _i32, _p, _p, _p, _p, _p, _p, _p],
-    "b2m_gemm2": [_p, _p, _i64, _i32, _p, _p, _i32, _i64, _p, _p, _p, _p, _i64, _p, _p, _p, _p],
+    "b2m_gemm2": [_p, _p, _i64, _i32, _p, _p, _i32, _i64, _p, _p, _p, _p, _i64, _p, _p, _i64, _i64, _i32, _p, _p],
     "b2m_combine": [_p, _i64, _i32, _i64, _p, _p, _p, _p, _i64, _p],
+    "b2m_copy_async": [_p, _p, _i64, _p],
+    "b2m_copy2d_async": [_p, _i64, _p, _i64, _i64, _i64, _p],
     "b2m_symm_alloc": [_i64, _c.POINTER(_p)],
     "b2m_symm_free": [_p],
     "b2m_ipc_handle": [_p, _p],
@@ -36,8 +38,10 @@ SIGNATURES: dict[str, list] = {
     "b2m_quant_push": [_p, _i64, _i64, _i64, _i32, _p, _p, _i64, _p, _c.c_uint32, _p, _p],
     "b2m_quant_push_noalloc": [_p, _i64, _i64, _i64, _i32, _p, _p, _i64, _p, _c.c_uint32, _p],
     "b2m_dispatch_rows_wait": [_p, _p, _i64, _i64, _p, _i32, _p, _p, _i64, _p, _i32, _i32, _c.c_uint32, _p, _p],
-    "b2m_combine_push": [_p, _i64, _i32, _i64, _p, _p, _p, _i32, _i32, _p, _p, _c.c_uint32, _p, _p],
-    "b2m_rs_reduce": [_p, _i64, _i64, _i32, _p, _c.c_uint32, _p, _p, _p, _p],
+    "b2m_combine_push": [_p, _i64, _i32, _i64, _i64, _i64, _p, _p, _p, _i32, _i32, _p, _p, _c.c_uint32, _p, _i32,
+                         _p],
+    "b2m_signal": [_p, _i32, _c.c_uint32, _p],
+    "b2m_rs_reduce": [_p, _i64, _i64, _i32, _i32, _p, _c.c_uint32, _p, _p, _p, _p],
 }
 
 ERROR_NAMES = {1: "B2M_ERR_ARG", 2: "B2M_ERR_CUDA", 3: "B2M_ERR_UNSUPPORTED"}

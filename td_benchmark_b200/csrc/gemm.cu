@@ -85,7 +85,8 @@ struct GemmParams {
   int32_t numel;       // pad id
   int32_t top_k;
   int32_t num_kb;      // K / 128
-  int32_t num_nt;      // output tiles along N
+  int32_t num_nt;      // output tiles along N in this launch (window [nt_begin, nt_begin + num_nt))
+  int32_t nt_begin;    // first N tile of the window
   int32_t n_blocks;    // 128-row scale blocks per expert of B
   int32_t n_rows;      // rows of B per expert
   const float* a_scale;  // [KB, rows_cap]: scale of sorted row p, K block kb at kb * rows_cap + p
@@ -111,6 +112,7 @@ struct TileWalk {
   int64_t num_tiles;
   int num_mb;
   int num_nt;
+  int nt_begin;
 };
 
 // Tile t -> (M block, N tile): bands of GROUP_M consecutive M blocks (experts are
@@ -123,7 +125,7 @@ __device__ __forceinline__ void tile_coords(int64_t t, const TileWalk& tw, int& 
   const int rows = tw.num_mb - first < GROUP_M ? tw.num_mb - first : GROUP_M;
   const int64_t in_band = t - band * per_band;
   mb = first + static_cast<int>(in_band % rows);
-  nt = static_cast<int>(in_band / rows);
+  nt = tw.nt_begin + static_cast<int>(in_band / rows);
 }
 
 // ---------------------------------------------------------------- warp 0: B (+A for the down GEMM)
@@ -409,7 +411,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0 && blockIdx.x == 0) set_status(p.status, B2M_STATUS_BAD_ROUTING);
     num_mb = 0;
   }
-  const TileWalk tw{static_cast<int64_t>(num_mb) * p.num_nt, num_mb > 0 ? num_mb : 1, p.num_nt};
+  const TileWalk tw{static_cast<int64_t>(num_mb) * p.num_nt, num_mb > 0 ? num_mb : 1, p.num_nt, p.nt_begin};
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -501,6 +503,7 @@ struct PairWalk {
   int num_pairs;
   int num_nt;
   int64_t num_items;
+  int nt_begin;
 };
 
 struct PairItem {
@@ -515,7 +518,7 @@ __device__ __forceinline__ PairItem pair_item(int64_t w, const PairWalk& pw) {
   const int64_t in_band = w - band * per_band;
   const int pi = first + static_cast<int>(in_band % rows);
   PairItem it;
-  it.nt = static_cast<int>(in_band / rows);
+  it.nt = pw.nt_begin + static_cast<int>(in_band / rows);
   it.b0 = __ldg(pw.pairs + 1 + 2 * pi);
   it.b1 = __ldg(pw.pairs + 2 + 2 * pi);
   return it;
@@ -730,7 +733,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0 && blockIdx.x == 0) set_status(p.status, B2M_STATUS_BAD_ROUTING);
     num_pairs = 0;
   }
-  const PairWalk pw{block_pairs, num_pairs, p.num_nt, static_cast<int64_t>(num_pairs) * p.num_nt};
+  const PairWalk pw{block_pairs, num_pairs, p.num_nt, static_cast<int64_t>(num_pairs) * p.num_nt, p.nt_begin};
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PSTAGES; ++s) {
@@ -810,6 +813,7 @@ int encode_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t o
 
 template <bool kGateUp>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int num_sms, cudaStream_t s) {
+  // num_sms here is the CTA budget (all SMs, or fewer when the caller keeps SMs for comm kernels)
   static int attr_done[64] = {0};
   int dev = 0;
   B2M_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
@@ -899,7 +903,7 @@ extern "C" int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows
                          const float* w2_scale, int32_t num_experts, int64_t hidden, const int32_t* sorted_token_ids,
                          const int32_t* expert_ids, const int32_t* num_tokens_post_padded,
                          const int32_t* block_pairs, int64_t numel, const float* topk_weights, void* out_bf16,
-                         int32_t* dev_status, void* stream) {
+                         int64_t col_begin, int64_t col_end, int32_t max_ctas, int32_t* dev_status, void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
@@ -913,6 +917,11 @@ extern "C" int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows
   if (!aligned16(a_fp8) || !aligned16(a_scale_t) || !aligned16(w2) || !aligned16(out_bf16))
     return fail(B2M_ERR_ARG, "gemm2: A, A scales, W2 and out must be 16-byte aligned");
   if (rows_cap / BM > INT32_MAX || numel >= INT32_MAX) return fail(B2M_ERR_ARG, "gemm2: sizes overflow int32");
+  if (col_end <= 0) col_end = hidden;
+  if (col_begin < 0 || col_begin % BN || col_end > hidden || col_begin >= col_end || (col_end % BN && col_end != hidden))
+    return fail(B2M_ERR_ARG, "gemm2: column window [%lld, %lld) must be 256-aligned inside [0, %lld)",
+                (long long)col_begin, (long long)col_end, (long long)hidden);
+  if (max_ctas > 0 && max_ctas < num_sms) num_sms = max_ctas < 2 ? 2 : max_ctas;
   CUtensorMap ma, mb;
   B2M_TRY(encode_map_2d(&ma, a_fp8, inter, rows_cap, inter, BK, BM));
   B2M_TRY(encode_map_2d(&mb, w2, inter, static_cast<uint64_t>(num_experts) * hidden, inter, BK,
@@ -925,7 +934,8 @@ extern "C" int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows
   p.numel = static_cast<int32_t>(numel);
   p.top_k = 1;
   p.num_kb = inter / BK;
-  p.num_nt = static_cast<int32_t>((hidden + BN - 1) / BN);
+  p.nt_begin = static_cast<int32_t>(col_begin / BN);
+  p.num_nt = static_cast<int32_t>((col_end + BN - 1) / BN) - p.nt_begin;
   p.n_blocks = static_cast<int32_t>(hidden / 128);
   p.n_rows = static_cast<int32_t>(hidden);
   p.a_scale = a_scale_t;

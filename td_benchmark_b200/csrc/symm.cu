@@ -11,9 +11,11 @@
 //               rank (system-scope release).  b2m_dispatch_rows_wait then moves rows
 //               into expert order, reading a source rank's rows only after its flag
 //               (own rows first, bounded acquire spin per source).
-//  reduce-scatter  b2m_combine_push sums each token's top-k rows (+ shared expert) and
-//               stores the bf16 partial row into the owning rank's slot for this source;
-//               the last CTA publishes rs_flag[src] = epoch on every owner.
+//  reduce-scatter  b2m_combine_push sums each token's top-k rows (+ shared expert) over a
+//               column chunk and stores the bf16 partial into the owning rank's slot for
+//               this source; the last CTA publishes rs_flag[chunk][src] = epoch on every
+//               owner.  Chunk c's push runs on a side stream while the down GEMM of chunk
+//               c+1 runs on the remaining SMs.
 //               b2m_rs_reduce waits for all sources and sums the slots in rank order
 //               (deterministic, fp32, one rounding).
 //
@@ -23,6 +25,9 @@
 // gather buffer of call i (stream order); symmetrically for the slots.
 //
 // Symmetric buffers are plain cudaMalloc blocks shared through CUDA IPC handles.
+// b2m_copy_async / b2m_copy2d_async let the host drive the same exchange with the copy
+// engines instead (one cudaMemcpyAsync per peer block, then the epoch flag), which
+// needs no SMs and so overlaps a GEMM running on all of them.
 #include "b2m_common.cuh"
 #include "b2m_host.h"
 
@@ -160,38 +165,58 @@ __device__ __forceinline__ uint4 pack_bf16x8(const float (&a)[8]) {
 
 __global__ void __launch_bounds__(kThreads)
     combine_push_kernel(const __nv_bfloat16* __restrict__ staged, int64_t tokens, int top_k, int64_t hidden,
-                        const int32_t* __restrict__ topk_ids, const int32_t* __restrict__ expert_map,
-                        const __nv_bfloat16* __restrict__ shared, int world, int rank, PeerPtrs slots, FlagPtrs flags,
-                        uint32_t epoch, int32_t* counter) {
-  const int64_t vec = hidden / 8;
+                        int64_t col0, int64_t col1, const int32_t* __restrict__ topk_ids,
+                        const int32_t* __restrict__ expert_map, const __nv_bfloat16* __restrict__ shared, int world,
+                        int rank, PeerPtrs slots, FlagPtrs flags, uint32_t epoch, int32_t* counter) {
+  const int64_t vec = (col1 - col0) / 8;
   const int64_t per_rank = tokens / world;
   const int64_t total = tokens * vec;
   for (int64_t v = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; v < total;
        v += static_cast<int64_t>(gridDim.x) * kThreads) {
     const int64_t t = v / vec;
-    const int64_t c = (v - t * vec) * 8;
+    const int64_t c = col0 + (v - t * vec) * 8;
     float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < top_k; ++j) {
-      const int64_t pair = t * top_k + j;
-      if (expert_map && __ldg(expert_map + __ldg(topk_ids + pair)) < 0) continue;
-      acc_bf16x8(__ldg(reinterpret_cast<const uint4*>(staged + pair * hidden + c)), a);
+    // top-k rows in groups of 8: every load of a group is issued before the first add
+    for (int j0 = 0; j0 < top_k; j0 += 8) {
+      const int n = min(8, top_k - j0);
+      uint4 u[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        u[j] = make_uint4(0, 0, 0, 0);
+        if (j < n) {
+          const int64_t pair = t * top_k + j0 + j;
+          if (!expert_map || __ldg(expert_map + __ldg(topk_ids + pair)) >= 0)
+            u[j] = __ldg(reinterpret_cast<const uint4*>(staged + pair * hidden + c));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc_bf16x8(u[j], a);  // zero words add +0.0f
     }
     if (shared) acc_bf16x8(__ldg(reinterpret_cast<const uint4*>(shared + t * hidden + c)), a);
     const int owner = static_cast<int>(t / per_rank);
     const int64_t slot_row = static_cast<int64_t>(rank) * per_rank + (t - owner * per_rank);
     *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(slots.p[owner]) + slot_row * hidden + c) = pack_bf16x8(a);
   }
-  publish_when_grid_done(counter, flags, world, epoch);
+  if (counter) publish_when_grid_done(counter, flags, world, epoch);
+}
+
+// One thread: after every copy and kernel before it on this stream, publish `epoch`
+// to each flag (system scope), e.g. after copy-engine pushes into peer slots.
+__global__ void signal_kernel(FlagPtrs flags, int world, uint32_t epoch) {
+  if (threadIdx.x == 0) {
+    fence_sys();
+    for (int r = 0; r < world; ++r) st_release_sys(flags.p[r], epoch);
+  }
 }
 
 __global__ void __launch_bounds__(kThreads)
-    rs_reduce_kernel(const __nv_bfloat16* __restrict__ slots, int64_t rows, int64_t hidden, int world,
+    rs_reduce_kernel(const __nv_bfloat16* __restrict__ slots, int64_t rows, int64_t hidden, int world, int nflags,
                      const uint32_t* flags, uint32_t epoch, const __nv_bfloat16* __restrict__ add,
                      __nv_bfloat16* __restrict__ out, int32_t* status, uint64_t timeout_ns) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) s_ok = 1;
   __syncthreads();
-  if (threadIdx.x < world && !wait_flag_geq(flags + threadIdx.x, epoch, timeout_ns, status, B2M_STATUS_TIMEOUT_PEER))
+  if (threadIdx.x < nflags && !wait_flag_geq(flags + threadIdx.x, epoch, timeout_ns, status, B2M_STATUS_TIMEOUT_PEER))
     s_ok = 0;
   __syncthreads();
   if (!s_ok) return;  // status already records the timeout
@@ -291,6 +316,27 @@ int b2m_ipc_close(void* peer_ptr) {
   return check_cuda(cudaIpcCloseMemHandle(peer_ptr), "cudaIpcCloseMemHandle");
 }
 
+int b2m_copy_async(void* dst, const void* src, int64_t bytes, void* stream) {
+  using namespace b2m;
+  if (bytes < 0 || (bytes > 0 && (!dst || !src))) return fail(B2M_ERR_ARG, "copy_async: bad arguments");
+  if (bytes == 0) return B2M_OK;
+  return check_cuda(cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDefault,
+                                    static_cast<cudaStream_t>(stream)),
+                    "copy_async: cudaMemcpyAsync");
+}
+
+int b2m_copy2d_async(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+                     void* stream) {
+  using namespace b2m;
+  if (width < 0 || height < 0 || dpitch < width || spitch < width || ((width && height) && (!dst || !src)))
+    return fail(B2M_ERR_ARG, "copy2d_async: bad arguments");
+  if (width == 0 || height == 0) return B2M_OK;
+  return check_cuda(cudaMemcpy2DAsync(dst, static_cast<size_t>(dpitch), src, static_cast<size_t>(spitch),
+                                      static_cast<size_t>(width), static_cast<size_t>(height), cudaMemcpyDefault,
+                                      static_cast<cudaStream_t>(stream)),
+                    "copy2d_async: cudaMemcpy2DAsync");
+}
+
 int b2m_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world, void* const* q_dst,
                    void* const* s_dst, int64_t row0, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
                    void* stream) {
@@ -353,43 +399,61 @@ int b2m_dispatch_rows_wait(const void* xq, const float* xs, int64_t tokens, int6
   return check_cuda(cudaGetLastError(), "dispatch_rows_wait launch");
 }
 
-int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, const int32_t* topk_ids,
-                     const int32_t* expert_map, const void* shared, int32_t world, int32_t rank,
-                     void* const* slot_dst, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
-                     void* stream) {
+int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, int64_t col_begin,
+                     int64_t col_end, const int32_t* topk_ids, const int32_t* expert_map, const void* shared,
+                     int32_t world, int32_t rank, void* const* slot_dst, uint32_t* const* flag_dst, uint32_t epoch,
+                     int32_t* counter, int32_t max_ctas, void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
   if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || tokens <= 0 || tokens % world ||
       hidden % 8 || top_k <= 0)
     return fail(B2M_ERR_ARG, "combine_push: bad shape (tokens %% world == 0, hidden %% 8 == 0)");
-  if (!staged || !counter || !slot_dst || !flag_dst || (expert_map && !topk_ids) || !aligned16(staged))
+  if (!staged || !slot_dst || (counter && !flag_dst) || (expert_map && !topk_ids) || !aligned16(staged))
     return fail(B2M_ERR_ARG, "combine_push: bad pointers");
+  if (col_end <= 0) col_end = hidden;
+  if (col_begin < 0 || col_begin % 8 || col_end % 8 || col_end > hidden || col_begin >= col_end)
+    return fail(B2M_ERR_ARG, "combine_push: column window [%lld, %lld) outside [0, %lld) or not 8-aligned",
+                (long long)col_begin, (long long)col_end, (long long)hidden);
   PeerPtrs sl{};
   FlagPtrs f{};
   for (int r = 0; r < world; ++r) {
-    if (!slot_dst[r] || !flag_dst[r] || !aligned16(slot_dst[r]))
+    if (!slot_dst[r] || (counter && !flag_dst[r]) || !aligned16(slot_dst[r]))
       return fail(B2M_ERR_ARG, "combine_push: bad peer pointer %d", r);
     sl.p[r] = slot_dst[r];
-    f.p[r] = flag_dst[r];
+    f.p[r] = counter ? flag_dst[r] : nullptr;
   }
-  combine_push_kernel<<<grid_for(tokens * (hidden / 8), num_sms, 8), kThreads, 0,
-                        static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, topk_ids, expert_map,
+  int grid = grid_for(tokens * ((col_end - col_begin) / 8), num_sms, 8);
+  if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
+  combine_push_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, col_begin, col_end, topk_ids, expert_map,
       static_cast<const __nv_bfloat16*>(shared), world, rank, sl, f, epoch, counter);
   return check_cuda(cudaGetLastError(), "combine_push launch");
 }
 
-int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world, const uint32_t* flags,
-                  uint32_t epoch, const void* add, void* out, int32_t* dev_status, void* stream) {
+int b2m_signal(uint32_t* const* flag_dst, int32_t world, uint32_t epoch, void* stream) {
+  using namespace b2m;
+  if (world < 1 || world > kMaxWorld || !flag_dst) return fail(B2M_ERR_ARG, "signal: bad arguments");
+  FlagPtrs f{};
+  for (int r = 0; r < world; ++r) {
+    if (!flag_dst[r]) return fail(B2M_ERR_ARG, "signal: null flag %d", r);
+    f.p[r] = flag_dst[r];
+  }
+  signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(f, world, epoch);
+  return check_cuda(cudaGetLastError(), "signal launch");
+}
+
+int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world, int32_t nchunks,
+                  const uint32_t* flags, uint32_t epoch, const void* add, void* out, int32_t* dev_status,
+                  void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
   if (world < 1 || world > kMaxWorld || rows <= 0 || hidden % 8 || !slots || !flags || !out ||
-      !aligned16(slots) || !aligned16(out) || (add && !aligned16(add)))
-    return fail(B2M_ERR_ARG, "rs_reduce: bad shape/pointers");
+      !aligned16(slots) || !aligned16(out) || (add && !aligned16(add)) || nchunks < 1 || nchunks * world > kThreads)
+    return fail(B2M_ERR_ARG, "rs_reduce: bad shape/pointers/chunks");
   rs_reduce_kernel<<<grid_for(rows * (hidden / 8), num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(slots), rows, hidden, world, flags, epoch,
+      static_cast<const __nv_bfloat16*>(slots), rows, hidden, world, nchunks * world, flags, epoch,
       static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out), dev_status, timeout_ns());
   return check_cuda(cudaGetLastError(), "rs_reduce launch");
 }

@@ -143,7 +143,8 @@ class NullExchange:
         ops.quant_dispatch(x_local, layer.route.pair_pos, layer.top_k, layer.a_sorted, layer.as_t,
                            None if sh is None else sh.a, None if sh is None else sh.as_t)
 
-    def combine_scatter(self, layer: "MoELayer", ids, shared_out) -> torch.Tensor:
+    def down_and_scatter(self, layer: "MoELayer", topk_weights, ids, shared_out) -> torch.Tensor:
+        layer.gemm2(topk_weights)
         return ops.combine(layer.staged, layer.top_k, ids, layer.expert_map, shared_out, layer.out_local)
 
     def close(self) -> None:
@@ -183,7 +184,8 @@ class NcclExchange:
         if layer.shared is not None and not layer.ep:
             layer.shared.load_rows(layer.xq, layer.xs)
 
-    def combine_scatter(self, layer: "MoELayer", ids, shared_out) -> torch.Tensor:
+    def down_and_scatter(self, layer: "MoELayer", topk_weights, ids, shared_out) -> torch.Tensor:
+        layer.gemm2(topk_weights)
         ops.combine(layer.staged, layer.top_k, ids, layer.expert_map, shared_out, self.partial)
         self.dist.reduce_scatter_tensor(layer.out_local, self.partial, group=self.group)
         if layer.shared is not None and layer.ep:
@@ -195,23 +197,41 @@ class NcclExchange:
 
 
 class P2PExchange:
-    """Fused exchange over NVLink peer memory (``b2m_quant_push`` / ``b2m_dispatch_rows_wait`` /
-    ``b2m_combine_push`` / ``b2m_rs_reduce``): no NCCL on the data path.
+    """Fused exchange over NVLink peer memory: no NCCL on the data path.
 
-    The all-gather is the quant kernel storing into every rank's gather buffer; the
-    reduce-scatter is the combine kernel storing each token's partial into its
-    owner's slot, then an owner-side sum in rank order.  Flags are epochs.
+    All-gather: ``b2m_quant_push`` quantises the rank's tokens and stores them into
+    every rank's gather buffer; ``b2m_dispatch_rows_wait`` moves rows into expert
+    order as each source's flag arrives.
+
+    Reduce-scatter (``rs_mode``):
+      "sm" (default) -- after the whole down GEMM, ``b2m_combine_push`` stores each
+           token's partial into its owner's slot with SM stores and publishes the flags.
+      "ce" -- the down GEMM runs in ``chunks`` column chunks on all SMs; after each chunk
+           the combine writes the per-owner partials into a local staging buffer (own
+           block straight into the own slot) and the copy engines push each owner's block
+           of that chunk into its slot on side streams while the next chunk computes; one
+           ``b2m_signal`` publishes the epoch after the last copy.  Measured slower than
+           "sm" on 2 and 8 B200s for the Mixtral and DeepSeek-V3 shapes (the strided
+           copy-engine pushes ran below the SM stores' NVLink rate and the column chunks
+           cost the down GEMM time), kept as the alternative.
+    ``b2m_rs_reduce`` then sums the slots in rank order.  Flags are epochs.
     """
     name = "p2p"
+    MAX_CHUNKS = 8
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, chunks: int = 4, rs_mode: str = "sm", ce_streams: int = 2):
         import torch.distributed as dist
+        if rs_mode not in ("ce", "sm"):
+            raise ValueError(f"rs_mode must be 'ce' or 'sm', got {rs_mode!r}")
         self.dist = dist
         self.group = group
         self.world_size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.epoch = 0
         self.ws = None
+        self.chunks_req = chunks if rs_mode == "ce" else 1
+        self.rs_mode = rs_mode
+        self.ce_streams = max(1, ce_streams)
         # Diagnostic only (bench's exposed-communication split): run the same kernels on
         # local data with every peer flag treated as already set and nothing sent.
         self.compute_only = False
@@ -222,7 +242,7 @@ class P2PExchange:
         P, T, H, Tl = self.world_size, layer.T, layer.H, layer.T_local
         self.ws = SymmetricWorkspace({
             "xq": T * H, "xs": T * (H // 128) * 4, "slots": T * H * 2,
-            "ag_flags": 4 * P, "rs_flags": 4 * P, "counters": 16,
+            "ag_flags": 4 * P, "rs_flags": 4 * P * self.MAX_CHUNKS, "counters": 16,
         }, self.group, layer.device)
         ws = self.ws
         layer.xq = ws.tensor("xq", (T, H), torch.uint8).view(ops.FP8)
@@ -236,6 +256,27 @@ class P2PExchange:
         self._ag_dst = ptr_array([ws.peer("ag_flags", r) + 4 * self.rank for r in range(P)])
         self._slot_dst = ptr_array([ws.peer("slots", r) for r in range(P)])
         self._rs_dst = ptr_array([ws.peer("rs_flags", r) + 4 * self.rank for r in range(P)])
+        # column chunks of the down GEMM (multiples of its 256-column tile)
+        ntiles = (H + 255) // 256
+        n = max(1, min(self.chunks_req, ntiles, self.MAX_CHUNKS))
+        bounds = [round(i * ntiles / n) * 256 for i in range(n + 1)]
+        bounds[-1] = H
+        self.chunk_cols = [(bounds[i], bounds[i + 1]) for i in range(n) if bounds[i] < bounds[i + 1]]
+        if self.rs_mode == "ce":
+            # staging rows: token t's partial at row t; the own block goes to the own slot
+            self.partial = torch.empty((T, H), dtype=torch.bfloat16, device=layer.device)
+            pb, own = self.partial.data_ptr(), ws.peer("slots", self.rank)
+            self._stage_dst = ptr_array([own if r == self.rank else pb + (r - self.rank) * Tl * H * 2
+                                         for r in range(P)])
+            peers = [r for r in range(P) if r != self.rank]
+            ns = max(1, min(self.ce_streams, len(peers)))
+            lo, hi = torch.cuda.Stream.priority_range()
+            self.ce = [torch.cuda.Stream(layer.device, priority=hi) for _ in range(ns)]
+            self._copies = [[] for _ in range(ns)]   # per stream: (peer, byte offset of its block)
+            for i, r in enumerate(peers):
+                self._copies[i % ns].append(r)
+            self.chunk_ev = [torch.cuda.Event() for _ in self.chunk_cols]
+            self.join_ev = [torch.cuda.Event() for _ in self.ce]
         self.dist.barrier(group=self.group)
 
     def gather_dispatch(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
@@ -270,31 +311,61 @@ class P2PExchange:
         if layer.shared is not None and not layer.ep:
             layer.shared.load_rows(layer.xq, layer.xs)
 
-    def _combine_scatter_local(self, layer: "MoELayer", ids, shared_out) -> torch.Tensor:
+    def _down_and_scatter_local(self, layer: "MoELayer", topk_weights, ids, shared_out) -> torch.Tensor:
         from . import _lib
 
+        layer.gemm2(topk_weights)
+        layer._event("gemm2_end")
         st = ops._stream(layer.device)
         ops.combine(layer.staged, layer.top_k, ids, layer.expert_map, shared_out, self.slots)
+        layer._event("combine_end")
         add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
-        _lib.call("b2m_rs_reduce", self.slots.data_ptr(), layer.T_local, layer.H, self.world_size, self.rs_flags, 0,
-                  None if add is None else add.data_ptr(), layer.out_local.data_ptr(), layer.status.data_ptr(), st)
+        layer._event("shared_end")
+        _lib.call("b2m_rs_reduce", self.slots.data_ptr(), layer.T_local, layer.H, self.world_size, 1,
+                  self.rs_flags, 0, None if add is None else add.data_ptr(), layer.out_local.data_ptr(),
+                  layer.status.data_ptr(), st)
         return layer.out_local
 
-    def combine_scatter(self, layer: "MoELayer", ids, shared_out) -> torch.Tensor:
+    def down_and_scatter(self, layer: "MoELayer", topk_weights, ids, shared_out) -> torch.Tensor:
         from . import _lib
 
         if self.compute_only:
-            return self._combine_scatter_local(layer, ids, shared_out)
-        st = ops._stream(layer.device)
-        _lib.call("b2m_combine_push", layer.staged.data_ptr(), layer.T, layer.top_k, layer.H,
-                  None if ids is None else ids.data_ptr(),
-                  None if layer.expert_map is None else layer.expert_map.data_ptr(),
-                  None if shared_out is None else shared_out.data_ptr(), self.world_size, self.rank,
-                  self._slot_dst, self._rs_dst, self.epoch, self.counters + 4, st)
+            return self._down_and_scatter_local(layer, topk_weights, ids, shared_out)
+        compute = torch.cuda.current_stream(layer.device)
+        P, Tl, H = self.world_size, layer.T_local, layer.H
+        idsp = None if ids is None else ids.data_ptr()
+        emap = None if layer.expert_map is None else layer.expert_map.data_ptr()
+        shp = None if shared_out is None else shared_out.data_ptr()
+        if self.rs_mode == "sm":
+            layer.gemm2(topk_weights)
+            layer._event("gemm2_end")
+            _lib.call("b2m_combine_push", layer.staged.data_ptr(), layer.T, layer.top_k, H, 0, H, idsp, emap, shp,
+                      P, self.rank, self._slot_dst, self._rs_dst, self.epoch, self.counters + 4, 0,
+                      compute.cuda_stream)
+        else:
+            pb = self.partial.data_ptr()
+            for c, (c0, c1) in enumerate(self.chunk_cols):
+                layer.gemm2(topk_weights, cols=(c0, c1))
+                _lib.call("b2m_combine_push", layer.staged.data_ptr(), layer.T, layer.top_k, H, c0, c1, idsp, emap,
+                          shp, P, self.rank, self._stage_dst, None, 0, None, 0, compute.cuda_stream)
+                self.chunk_ev[c].record(compute)
+                for s, peers in zip(self.ce, self._copies):
+                    s.wait_event(self.chunk_ev[c])
+                    for r in peers:
+                        _lib.call("b2m_copy2d_async", self.ws.peer("slots", r) + (self.rank * Tl * H + c0) * 2, H * 2,
+                                  pb + (r * Tl * H + c0) * 2, H * 2, (c1 - c0) * 2, Tl, s.cuda_stream)
+            for s, ev in zip(self.ce[1:], self.join_ev[1:]):
+                ev.record(s)
+                self.ce[0].wait_event(ev)
+            _lib.call("b2m_signal", self._rs_dst, P, self.epoch, self.ce[0].cuda_stream)
+        layer._event("combine_end")
         add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
-        _lib.call("b2m_rs_reduce", self.slots.data_ptr(), layer.T_local, layer.H, self.world_size, self.rs_flags,
-                  self.epoch, None if add is None else add.data_ptr(), layer.out_local.data_ptr(),
-                  layer.status.data_ptr(), st)
+        layer._event("shared_end")
+        if self.rs_mode == "ce":
+            compute.wait_stream(self.ce[0])   # staging buffer reuse by the next call
+        _lib.call("b2m_rs_reduce", self.slots.data_ptr(), Tl, H, P, 1, self.rs_flags, self.epoch,
+                  None if add is None else add.data_ptr(), layer.out_local.data_ptr(), layer.status.data_ptr(),
+                  compute.cuda_stream)
         return layer.out_local
 
     def close(self) -> None:
@@ -365,18 +436,21 @@ class MoELayer:
         r = self.route
         ops.moe_align_block_size(topk_ids, BM, self.E, self.expert_map, out=(r.sorted_ids, r.expert_ids, r.ntpp),
                                  pair_pos=r.pair_pos, block_pairs=r.pairs(self.paired))
+        self._event("align_end")
         self.exchange.gather_dispatch(self, x_local)
 
-    def experts(self, topk_weights: torch.Tensor) -> None:
+    def gemm1(self) -> None:
         r = self.route
         self._event("gemm1_start")
-        bp = r.pairs(self.paired)
         ops.gemm1(self.a_sorted, self.as_t, self.w.w1i, self.w.w1i_scale, r.expert_ids, r.ntpp, self.inter_q,
-                  self.inter_st, self.status, block_pairs=bp)
+                  self.inter_st, self.status, block_pairs=r.pairs(self.paired))
         self._event("gemm1_end")
+
+    def gemm2(self, topk_weights: torch.Tensor, cols: tuple[int, int] | None = None, max_ctas: int = 0) -> None:
+        r = self.route
         ops.gemm2(self.inter_q, self.inter_st, self.w.w2, self.w.w2_scale, r.sorted_ids, r.expert_ids, r.ntpp,
-                  self.numel, topk_weights.reshape(-1), self.staged, self.status, block_pairs=bp)
-        self._event("gemm2_end")
+                  self.numel, topk_weights.reshape(-1), self.staged, self.status, block_pairs=r.pairs(self.paired),
+                  cols=cols, max_ctas=max_ctas)
 
     def kernel_launches(self) -> int:
         """b2m kernels one forward launches."""
@@ -386,7 +460,7 @@ class MoELayer:
             return 5 + (2 if sh else 0)             # align, quant+dispatch, GEMM1, GEMM2, combine (+shared GEMMs)
         n = 6                                      # align, quant(+push), dispatch, GEMM1, GEMM2, combine(+push)
         if name == "p2p":
-            n += 1                                 # owner-side reduce
+            n += 1 + 2 * (len(self.exchange.chunk_cols) - 1)   # owner-side reduce; GEMM2/push per chunk
         if sh:
             n += 3 + (1 if (self.ep and name == "nccl") else 0)
         return n
@@ -394,11 +468,14 @@ class MoELayer:
     def forward(self, x_local: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
         """x_local bf16 [T/P, H]; topk_ids int32 / topk_weights fp32 [T, k] (all tokens) -> bf16 [T/P, H]."""
         self.route_and_dispatch(x_local, topk_ids)
-        self.experts(topk_weights)
+        self.gemm1()
         shared_out = None
         if self.shared is not None and not self.ep:
             shared_out = self.shared.run(self.status)
-        return self.exchange.combine_scatter(self, topk_ids if self.ep else None, shared_out)
+            self._event("shared_end")
+        out = self.exchange.down_and_scatter(self, topk_weights, topk_ids if self.ep else None, shared_out)
+        self._event("scatter_end")
+        return out
 
     def check(self) -> None:
         ops.check_status(self.status, "MoELayer")

@@ -195,7 +195,8 @@ def gemm1(a_sorted: torch.Tensor, a_scale_t: torch.Tensor, w1i: torch.Tensor, w1
 def gemm2(a_q: torch.Tensor, a_scale_t: torch.Tensor, w2: torch.Tensor, w2_scale: torch.Tensor,
           sorted_ids: torch.Tensor, expert_ids: torch.Tensor, ntpp: torch.Tensor, numel: int,
           topk_weights: torch.Tensor | None, out: torch.Tensor | None = None,
-          status: torch.Tensor | None = None, block_pairs: torch.Tensor | None = None) -> torch.Tensor:
+          status: torch.Tensor | None = None, block_pairs: torch.Tensor | None = None,
+          cols: tuple[int, int] | None = None, max_ctas: int = 0) -> torch.Tensor:
     """Down grouped GEMM, routed weight in the epilogue.  Returns bf16 [numel, H] indexed by flat pair."""
     _cuda(a_q, "a_q")
     rows_cap, inter = a_q.shape
@@ -209,7 +210,8 @@ def gemm2(a_q: torch.Tensor, a_scale_t: torch.Tensor, w2: torch.Tensor, w2_scale
         out = torch.empty((numel, hidden), dtype=torch.bfloat16, device=a_q.device)
     _lib.call("b2m_gemm2", a_q.data_ptr(), a_scale_t.data_ptr(), rows_cap, inter, w2.data_ptr(), w2_scale.data_ptr(),
               e, hidden, sorted_ids.data_ptr(), expert_ids.data_ptr(), ntpp.data_ptr(), _ptr(block_pairs), numel,
-              _ptr(topk_weights), out.data_ptr(), _ptr(status), _stream(a_q.device))
+              _ptr(topk_weights), out.data_ptr(), 0 if cols is None else cols[0], 0 if cols is None else cols[1],
+              max_ctas, _ptr(status), _stream(a_q.device))
     return out
 
 
