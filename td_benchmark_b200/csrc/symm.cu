@@ -65,34 +65,52 @@ __device__ __forceinline__ void publish_when_grid_done(int32_t* counter, const F
 }
 
 // ---------------------------------------------------------------- all-gather push
+// Eight lanes share one 128-group (16 consecutive values each), so a warp covers four
+// consecutive groups of a row and every store to a destination is one coalesced
+// 512-byte warp write (16 B per lane) -- NVLink carries full lines, not 8-byte pieces.
+// The group scale and codes are computed exactly as by b2m_quant_g128 (amax / 448,
+// IEEE division, clamp, RNE).  Destinations are visited starting after the source's
+// own rank so that the ranks do not all hit the same peer first.
 __global__ void __launch_bounds__(kThreads)
     quant_push_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t rows, int64_t gpr, int world,
                       PeerPtrs qdst, PeerPtrs sdst, int64_t row0, FlagPtrs flags, uint32_t epoch, int32_t* counter) {
   const int lane = threadIdx.x & 31;
-  const int half = lane >> 4;
-  const int hl = lane & 15;
+  const int sub = lane >> 3;  // group of the warp's four
+  const int gl = lane & 7;    // 16-value slice of that group
   const int64_t cols = gpr * 128;
   const int64_t groups = rows * gpr;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
-  for (int64_t base = warp * 2; base < groups; base += nwarps * 2) {
-    const int64_t g = base + half;
-    uint4 raw = make_uint4(0, 0, 0, 0);
+  const int first = static_cast<int>((row0 / rows + 1) % world);
+  for (int64_t base = warp * 4; base < groups; base += nwarps * 4) {
+    const int64_t g = base + sub;
+    uint4 raw0 = make_uint4(0, 0, 0, 0), raw1 = raw0;
     int64_t row = 0, gi = 0;
     if (g < groups) {
       row = g / gpr;
       gi = g - row * gpr;
-      raw = __ldg(reinterpret_cast<const uint4*>(x + row * ldx + gi * 128 + hl * 8));
+      const uint4* src = reinterpret_cast<const uint4*>(x + row * ldx + gi * 128 + gl * 16);
+      raw0 = __ldg(src);
+      raw1 = __ldg(src + 1);
     }
-    float f[8];
-    bf16x8_to_f32(raw, f);
-    const float s = fmaxf(halfwarp_amax(f) / 448.0f, 1e-12f);
+    float f0[8], f1[8];
+    bf16x8_to_f32(raw0, f0);
+    bf16x8_to_f32(raw1, f1);
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fmaxf(fabsf(f0[i]), fabsf(f1[i])));
+#pragma unroll
+    for (int off = 4; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const float s = fmaxf(amax / 448.0f, 1e-12f);
     if (g < groups) {
-      const uint2 q = quant8(f, s);
+      const uint2 q0 = quant8(f0, s);
+      const uint2 q1 = quant8(f1, s);
+      const uint4 q = make_uint4(q0.x, q0.y, q1.x, q1.y);
       const int64_t dst_row = row0 + row;
-      for (int r = 0; r < world; ++r) {
-        *reinterpret_cast<uint2*>(static_cast<uint8_t*>(qdst.p[r]) + dst_row * cols + gi * 128 + hl * 8) = q;
-        if (hl == 0) static_cast<float*>(sdst.p[r])[dst_row * gpr + gi] = s;
+      for (int i = 0; i < world; ++i) {
+        const int r = first + i < world ? first + i : first + i - world;
+        *reinterpret_cast<uint4*>(static_cast<uint8_t*>(qdst.p[r]) + dst_row * cols + gi * 128 + gl * 16) = q;
+        if (gl == 0) static_cast<float*>(sdst.p[r])[dst_row * gpr + gi] = s;
       }
     }
   }
@@ -356,7 +374,7 @@ int b2m_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int
     f.p[r] = flag_dst[r];
   }
   const int64_t groups = rows * (hidden / 128);
-  quant_push_kernel<<<grid_for(groups * 16, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  quant_push_kernel<<<grid_for(groups * 8, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, rows, hidden / 128, world, q, s, row0, f, epoch, counter);
   return check_cuda(cudaGetLastError(), "quant_push launch");
 }

@@ -38,6 +38,37 @@ def test_quant_bit_exact(rows, cols):
     assert np.array_equal(s.cpu().numpy(), sr)
 
 
+@pytest.mark.parametrize("rows,cols,world", [(1, 128, 1), (7, 4096, 2), (33, 7168, 3), (512, 4096, 8),
+                                             (1024, 7168, 2)])
+def test_quant_push_bit_exact(rows, cols, world):
+    """All-gather push (peers emulated by buffers on this GPU): every destination holds the
+    oracle's codes and scales at the source's rows, and every flag holds the epoch."""
+    from td_benchmark_b200 import _lib
+    from td_benchmark_b200.symm import ptr_array
+
+    x = _bf16((rows, cols), rows * 31 + cols, 3.0)
+    if rows > 2:
+        x[1, :128] = 0
+        x[2, 5] = 3.0e4
+    xd = x.to(DEV)
+    row0 = rows  # the source owns rows [rows, 2 rows) of a 2-rank-tall gather buffer
+    qs = [torch.zeros((2 * rows, cols), dtype=torch.uint8, device=DEV) for _ in range(world)]
+    ss = [torch.zeros((2 * rows, cols // 128), dtype=torch.float32, device=DEV) for _ in range(world)]
+    flags = torch.zeros(world, dtype=torch.int32, device=DEV)
+    counter = torch.zeros(4, dtype=torch.int32, device=DEV)
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.call("b2m_quant_push", xd.data_ptr(), rows, cols, cols, world, ptr_array([q.data_ptr() for q in qs]),
+              ptr_array([s.data_ptr() for s in ss]), row0, ptr_array([flags.data_ptr() + 4 * r for r in range(world)]),
+              7, counter.data_ptr(), st)
+    torch.cuda.synchronize()
+    qr, sr = oquant.quant_g128(x.float().numpy())
+    for q, s in zip(qs, ss):
+        assert np.array_equal(q[row0:].cpu().numpy(), qr)
+        assert np.array_equal(s[row0:].cpu().numpy(), sr)
+        assert not q[:row0].any()
+    assert flags.tolist() == [7] * world and counter[0].item() == 0
+
+
 def test_quant_strided_rows_and_offset_output():
     big = _bf16((64, 1024), 5)
     x = big[:, 256:768]                    # row stride 1024
