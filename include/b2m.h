@@ -247,8 +247,10 @@ int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t 
                      int32_t world, int32_t rank, void* const* slot_dst, uint32_t* const* flag_dst, uint32_t epoch,
                      int32_t* counter, int32_t max_ctas, void* stream);
 
-/* One thread publishes epoch to every flag_dst[r] (system-scope release after a
- * system fence), ordered after all earlier work on `stream`. */
+/* Publishes epoch to every flag_dst[r] (own, peer or host-mapped memory) as stream
+ * memory operations (cuStreamWriteValue32): ordered after all earlier work on
+ * `stream`, each preceded by a fence equivalent to __threadfence_system, executed
+ * without an SM (so it cannot be starved by kernels that spin on flags). */
 int b2m_signal(uint32_t* const* flag_dst, int32_t world, uint32_t epoch, void* stream);
 
 /* Owner side of the reduce-scatter: once the nchunks*world flags (chunk-major) are all

@@ -25,9 +25,11 @@
 // gather buffer of call i (stream order); symmetrically for the slots.
 //
 // Symmetric buffers are plain cudaMalloc blocks shared through CUDA IPC handles.
-// b2m_copy_async / b2m_copy2d_async let the host drive the same exchange with the copy
-// engines instead (one cudaMemcpyAsync per peer block, then the epoch flag), which
-// needs no SMs and so overlaps a GEMM running on all of them.
+// b2m_copy_async / b2m_copy2d_async / b2m_signal let the host drive the same exchange
+// with the copy engines instead (one cudaMemcpyAsync per peer block, then the epoch
+// flag as a stream memory operation), which occupies no SM.
+#include <cudaTypedefs.h>
+
 #include "b2m_common.cuh"
 #include "b2m_host.h"
 
@@ -218,15 +220,6 @@ __global__ void __launch_bounds__(kThreads)
   if (counter) publish_when_grid_done(counter, flags, world, epoch);
 }
 
-// One thread: after every copy and kernel before it on this stream, publish `epoch`
-// to each flag (system scope), e.g. after copy-engine pushes into peer slots.
-__global__ void signal_kernel(FlagPtrs flags, int world, uint32_t epoch) {
-  if (threadIdx.x == 0) {
-    fence_sys();
-    for (int r = 0; r < world; ++r) st_release_sys(flags.p[r], epoch);
-  }
-}
-
 __global__ void __launch_bounds__(kThreads)
     rs_reduce_kernel(const __nv_bfloat16* __restrict__ slots, int64_t rows, int64_t hidden, int world, int nflags,
                      const uint32_t* flags, uint32_t epoch, const __nv_bfloat16* __restrict__ add,
@@ -275,6 +268,25 @@ namespace {
 constexpr int kPushScratchInts = 64;
 constexpr int kPushScratchNeeded = 1;  // one grid-completion counter per call
 static __device__ __align__(256) int32_t g_push_scratch[kPushScratchInts];
+
+// cuStreamWriteValue32 from the driver (the runtime is linked statically and has no
+// equivalent): a stream memory operation that writes a 32-bit value after all earlier
+// work on the stream, preceded by a fence with the effect of __threadfence_system, and
+// executed by the GPU front end rather than by an SM.
+int stream_write_fn(PFN_cuStreamWriteValue32_v11070* out) {
+  static PFN_cuStreamWriteValue32_v11070 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    B2M_TRY(check_cuda(cudaGetDriverEntryPoint("cuStreamWriteValue32", &p, cudaEnableDefault, &q),
+                       "cudaGetDriverEntryPoint(cuStreamWriteValue32)"));
+    if (q != cudaDriverEntryPointSuccess || !p)
+      return fail(B2M_ERR_UNSUPPORTED, "cuStreamWriteValue32 not available from the driver");
+    fn = reinterpret_cast<PFN_cuStreamWriteValue32_v11070>(p);
+  }
+  *out = fn;
+  return B2M_OK;
+}
 
 // Device address of g_push_scratch on the current device, looked up once per device
 // (the host-side name is only a stand-in and must never be handed to a kernel).
@@ -452,13 +464,15 @@ int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t 
 int b2m_signal(uint32_t* const* flag_dst, int32_t world, uint32_t epoch, void* stream) {
   using namespace b2m;
   if (world < 1 || world > kMaxWorld || !flag_dst) return fail(B2M_ERR_ARG, "signal: bad arguments");
-  FlagPtrs f{};
+  PFN_cuStreamWriteValue32_v11070 write = nullptr;
+  B2M_TRY(stream_write_fn(&write));
   for (int r = 0; r < world; ++r) {
     if (!flag_dst[r]) return fail(B2M_ERR_ARG, "signal: null flag %d", r);
-    f.p[r] = flag_dst[r];
+    const CUresult rc = write(static_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(flag_dst[r]), epoch,
+                              CU_STREAM_WRITE_VALUE_DEFAULT);
+    if (rc != CUDA_SUCCESS) return fail(B2M_ERR_CUDA, "signal: cuStreamWriteValue32 failed (%d) on flag %d", (int)rc, r);
   }
-  signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(f, world, epoch);
-  return check_cuda(cudaGetLastError(), "signal launch");
+  return B2M_OK;
 }
 
 int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world, int32_t nchunks,

@@ -199,9 +199,15 @@ class NcclExchange:
 class P2PExchange:
     """Fused exchange over NVLink peer memory: no NCCL on the data path.
 
-    All-gather: ``b2m_quant_push`` quantises the rank's tokens and stores them into
-    every rank's gather buffer; ``b2m_dispatch_rows_wait`` moves rows into expert
-    order as each source's flag arrives.
+    All-gather (``ag_mode``):
+      "sm" (default) -- ``b2m_quant_push`` quantises the rank's tokens and stores them
+           into every rank's gather buffer with SM stores, then publishes the flags.
+      "ce" -- ``b2m_quant_g128`` quantises into the rank's own rows of its gather buffer;
+           copy engines copy that contiguous block (codes, then scales) to each peer on
+           side streams, and ``b2m_signal`` (a stream memory write, no SM) publishes each
+           peer's flag right after its copies.
+    Either way ``b2m_dispatch_rows_wait`` then moves rows into expert order as each
+    source's flag arrives (own rows first).
 
     Reduce-scatter (``rs_mode``):
       "sm" (default) -- after the whole down GEMM, ``b2m_combine_push`` stores each
@@ -219,10 +225,11 @@ class P2PExchange:
     name = "p2p"
     MAX_CHUNKS = 8
 
-    def __init__(self, group=None, chunks: int = 4, rs_mode: str = "sm", ce_streams: int = 2):
+    def __init__(self, group=None, chunks: int = 4, rs_mode: str = "sm", ce_streams: int = 2, ag_mode: str = "sm"):
         import torch.distributed as dist
-        if rs_mode not in ("ce", "sm"):
-            raise ValueError(f"rs_mode must be 'ce' or 'sm', got {rs_mode!r}")
+        if rs_mode not in ("ce", "sm") or ag_mode not in ("ce", "sm"):
+            raise ValueError(f"rs_mode and ag_mode must be 'ce' or 'sm', got {rs_mode!r}, {ag_mode!r}")
+        self.ag_mode = ag_mode
         self.dist = dist
         self.group = group
         self.world_size = dist.get_world_size(group)
@@ -262,21 +269,28 @@ class P2PExchange:
         bounds = [round(i * ntiles / n) * 256 for i in range(n + 1)]
         bounds[-1] = H
         self.chunk_cols = [(bounds[i], bounds[i + 1]) for i in range(n) if bounds[i] < bounds[i + 1]]
+        if "ce" in (self.rs_mode, self.ag_mode):
+            # side streams for the copy engines; peers are dealt round-robin, starting after
+            # the own rank so that the ranks do not all copy to the same peer first
+            peers = [(self.rank + i) % P for i in range(1, P)]
+            ns = max(1, min(self.ce_streams, len(peers)))
+            lo, hi = torch.cuda.Stream.priority_range()
+            self.ce = [torch.cuda.Stream(layer.device, priority=hi) for _ in range(ns)]
+            self._copies = [[] for _ in range(ns)]   # per stream: the peers it copies to
+            for i, r in enumerate(peers):
+                self._copies[i % ns].append(r)
+            self.join_ev = [torch.cuda.Event() for _ in self.ce]
+            self.ag_ev = torch.cuda.Event()
+            self._ag_own = ptr_array([self.ag_flags + 4 * self.rank])
+            self._ag_peer = {r: ptr_array([ws.peer("ag_flags", r) + 4 * self.rank]) for r in peers}
+            self._pending_side = False
         if self.rs_mode == "ce":
             # staging rows: token t's partial at row t; the own block goes to the own slot
             self.partial = torch.empty((T, H), dtype=torch.bfloat16, device=layer.device)
             pb, own = self.partial.data_ptr(), ws.peer("slots", self.rank)
             self._stage_dst = ptr_array([own if r == self.rank else pb + (r - self.rank) * Tl * H * 2
                                          for r in range(P)])
-            peers = [r for r in range(P) if r != self.rank]
-            ns = max(1, min(self.ce_streams, len(peers)))
-            lo, hi = torch.cuda.Stream.priority_range()
-            self.ce = [torch.cuda.Stream(layer.device, priority=hi) for _ in range(ns)]
-            self._copies = [[] for _ in range(ns)]   # per stream: (peer, byte offset of its block)
-            for i, r in enumerate(peers):
-                self._copies[i % ns].append(r)
             self.chunk_ev = [torch.cuda.Event() for _ in self.chunk_cols]
-            self.join_ev = [torch.cuda.Event() for _ in self.ce]
         self.dist.barrier(group=self.group)
 
     def gather_dispatch(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
@@ -287,8 +301,11 @@ class P2PExchange:
         self.epoch += 1
         st = ops._stream(layer.device)
         Tl, H = layer.T_local, layer.H
-        _lib.call("b2m_quant_push", x_local.data_ptr(), Tl, H, x_local.stride(0), self.world_size, self._q_dst,
-                  self._s_dst, self.rank * Tl, self._ag_dst, self.epoch, self.counters, st)
+        if self.ag_mode == "sm":
+            _lib.call("b2m_quant_push", x_local.data_ptr(), Tl, H, x_local.stride(0), self.world_size, self._q_dst,
+                      self._s_dst, self.rank * Tl, self._ag_dst, self.epoch, self.counters, st)
+        else:
+            self._gather_ce(layer, x_local)
         if layer.shared is not None and layer.ep:
             r0 = self.rank * Tl
             layer.shared.load_rows(layer.xq[r0:r0 + Tl], layer.xs[r0:r0 + Tl])
@@ -301,6 +318,34 @@ class P2PExchange:
             _lib.call("b2m_dispatch_rows_wait", layer.xq.data_ptr(), layer.xs.data_ptr(), layer.T, H,
                       sh.route.pair_pos.data_ptr(), 1, sh.a.data_ptr(), sh.as_t.data_ptr(), sh.route.rows_cap,
                       self.ag_flags, self.world_size, self.rank, self.epoch, layer.status.data_ptr(), st)
+
+    def _join_side(self, compute) -> None:
+        """The compute stream waits for every copy issued on the side streams so far."""
+        if getattr(self, "_pending_side", False):
+            for s, ev in zip(self.ce, self.join_ev):
+                ev.record(s)
+                compute.wait_event(ev)
+            self._pending_side = False
+
+    def _gather_ce(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
+        from . import _lib
+
+        compute = torch.cuda.current_stream(layer.device)
+        self._join_side(compute)   # the previous call's copies read the own rows rewritten here
+        Tl, H, ws = layer.T_local, layer.H, self.ws
+        r0 = self.rank * Tl
+        ops.quant_g128(x_local, layer.xq[r0:r0 + Tl], layer.xs[r0:r0 + Tl])
+        _lib.call("b2m_signal", self._ag_own, 1, self.epoch, compute.cuda_stream)
+        self.ag_ev.record(compute)
+        qb, sb = Tl * H, Tl * (H // 128) * 4
+        q_off, s_off = r0 * H, r0 * (H // 128) * 4
+        for s, peers in zip(self.ce, self._copies):
+            s.wait_event(self.ag_ev)
+            for r in peers:
+                _lib.call("b2m_copy_async", ws.peer("xq", r) + q_off, ws.local("xq") + q_off, qb, s.cuda_stream)
+                _lib.call("b2m_copy_async", ws.peer("xs", r) + s_off, ws.local("xs") + s_off, sb, s.cuda_stream)
+                _lib.call("b2m_signal", self._ag_peer[r], 1, self.epoch, s.cuda_stream)
+        self._pending_side = True
 
     def _gather_dispatch_local(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
         r0 = self.rank * layer.T_local
@@ -358,11 +403,12 @@ class P2PExchange:
                 ev.record(s)
                 self.ce[0].wait_event(ev)
             _lib.call("b2m_signal", self._rs_dst, P, self.epoch, self.ce[0].cuda_stream)
+            self._pending_side = True
         layer._event("combine_end")
         add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
         layer._event("shared_end")
         if self.rs_mode == "ce":
-            compute.wait_stream(self.ce[0])   # staging buffer reuse by the next call
+            self._join_side(compute)   # staging buffer reuse by the next call
         _lib.call("b2m_rs_reduce", self.slots.data_ptr(), Tl, H, P, 1, self.rs_flags, self.epoch,
                   None if add is None else add.data_ptr(), layer.out_local.data_ptr(), layer.status.data_ptr(),
                   compute.cuda_stream)

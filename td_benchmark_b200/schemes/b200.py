@@ -19,23 +19,34 @@ from __future__ import annotations
 
 from typing import Any
 
-from .base import SchemeInstance, SchemeSpec, TunableSpec, make_lazy_instance, validate_tunables
+from .base import SchemeConfigError, SchemeInstance, SchemeSpec, TunableSpec, make_lazy_instance, validate_tunables
+
+EXCHANGE = {"d1": "nccl", "d2": "nccl", "d3": "p2p", "d4": "p2p"}
 
 B200_TUNABLES = {
     "check_status": TunableSpec(bool, False, "synchronise after every run() and raise on a device status code"),
 }
+# peer-memory exchange knobs of d3 / d4 (P2PExchange)
+P2P_TUNABLES = {
+    "ag_mode": TunableSpec(str, "sm", "all-gather by SM stores from the quant kernel ('sm') or copy engines ('ce')"),
+    "rs_mode": TunableSpec(str, "sm", "reduce-scatter by SM stores from the combine ('sm') or copy engines ('ce')"),
+    "rs_chunks": TunableSpec(int, 4, "down-GEMM column chunks of the copy-engine reduce-scatter (1..8)"),
+}
+_CHOICES = {"ag_mode": ("sm", "ce"), "rs_mode": ("sm", "ce")}
 
 
 def _spec(code: str, name: str, parallel: str, comm: str) -> SchemeSpec:
+    schema = dict(B200_TUNABLES)
+    if EXCHANGE.get(code) == "p2p":
+        schema.update(P2P_TUNABLES)
     return SchemeSpec(code=code, name=name, family="b200", parallel=parallel, comm=comm, weight_dtype="fp8",
-                      act_quant="group128", requires_nvshmem=False, tunables_schema=dict(B200_TUNABLES))
+                      act_quant="group128", requires_nvshmem=False, tunables_schema=schema)
 
 
 SPEC_D1 = _spec("d1", "B200-TP-NCCL", "TP", "quantize -> NCCL AG(fp8+scale) -> b2m GEMM1/GEMM2 -> NCCL RS(bf16)")
 SPEC_D2 = _spec("d2", "B200-EP-NCCL", "EP", "quantize -> NCCL AG(fp8+scale) -> b2m GEMMs(local experts) -> NCCL RS -> +shared")
 SPEC_D3 = _spec("d3", "B200-TP-P2P", "TP", "quantize+push(peer memory) -> b2m GEMM1/GEMM2 -> combine+push -> owner reduce")
 SPEC_D4 = _spec("d4", "B200-EP-P2P", "EP", "quantize+push(peer memory) -> b2m GEMMs(local experts) -> combine+push -> owner reduce(+shared)")
-EXCHANGE = {"d1": "nccl", "d2": "nccl", "d3": "p2p", "d4": "p2p"}
 
 
 def require_data(data: Any) -> Any:
@@ -44,7 +55,8 @@ def require_data(data: Any) -> Any:
     return data
 
 
-def build_layer(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, exchange: Any = None):
+def build_layer(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, exchange: Any = None,
+                tunables: dict[str, Any] | None = None):
     """Shard views + prepared weights + MoELayer for this rank."""
     import torch
 
@@ -67,7 +79,12 @@ def build_layer(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, exchange: Any =
         sv = tp_views(*sargs, ctx.rank, ctx.world_size) if spec.parallel == "TP" else tp_views(*sargs, 0, 1)
         shared = ExpertWeights.prepare(sv["w1"], sv["w1_scale"], sv["w2"], sv["w2_scale"])
     if exchange is None and ctx.world_size > 1:
-        exchange = P2PExchange(ctx.group) if EXCHANGE.get(spec.code) == "p2p" else NcclExchange(ctx.group)
+        if EXCHANGE.get(spec.code) == "p2p":
+            t = {k: v.default for k, v in P2P_TUNABLES.items()}
+            t.update({k: v for k, v in (tunables or {}).items() if k in P2P_TUNABLES})
+            exchange = P2PExchange(ctx.group, chunks=t["rs_chunks"], rs_mode=t["rs_mode"], ag_mode=t["ag_mode"])
+        else:
+            exchange = NcclExchange(ctx.group)
     expert_map = views.get("expert_map")
     layer = MoELayer(weights, T, s.top_k, s.E, expert_map=expert_map, shared=shared, exchange=exchange,
                      device=device)
@@ -78,8 +95,13 @@ def build_instance(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, scheme_cfg: 
     import torch
 
     tunables = validate_tunables(spec, scheme_cfg.tunables)
+    for name, allowed in _CHOICES.items():
+        if name in tunables and tunables[name] not in allowed:
+            raise SchemeConfigError(f"{spec.code}.{name}={tunables[name]!r} violates schema: expected one of {allowed}")
+    if "rs_chunks" in tunables and not 1 <= tunables["rs_chunks"] <= 8:
+        raise SchemeConfigError(f"{spec.code}.rs_chunks={tunables['rs_chunks']} violates schema: expected 1..8")
     bundle = require_data(data)
-    layer, level = build_layer(spec, cfg, ctx, bundle)
+    layer, level = build_layer(spec, cfg, ctx, bundle, tunables=tunables)
     device = layer.device
     topk_ids = bundle.routing.topk_ids_full.to(device=device, dtype=torch.int32).contiguous()
     topk_weights = bundle.routing.topk_weights_full.to(device=device, dtype=torch.float32).contiguous()

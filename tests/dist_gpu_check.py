@@ -23,6 +23,9 @@ def main() -> int:
     ap.add_argument("--preset", default="mixtral")
     ap.add_argument("--tokens", type=int, default=512)
     ap.add_argument("--zipf", action="store_true")
+    ap.add_argument("--ag-mode", default=None, help="d3/d4 tunable ag_mode")
+    ap.add_argument("--rs-mode", default=None, help="d3/d4 tunable rs_mode")
+    ap.add_argument("--rs-chunks", type=int, default=None, help="d3/d4 tunable rs_chunks")
     args = ap.parse_args()
 
     import torch
@@ -41,7 +44,11 @@ def main() -> int:
         over["imbalance_kind"] = "none"
     cfg = configs.preset(args.preset, **over)
     bundle = data.build_bundle(cfg, rank=ctx.rank, world_size=ctx.world_size, device=ctx.device)
-    inst = build_scheme(cfg, ctx, bundle, SchemeCfg(args.scheme, {"check_status": True}))
+    tun = {"check_status": True}
+    for key, val in (("ag_mode", args.ag_mode), ("rs_mode", args.rs_mode), ("rs_chunks", args.rs_chunks)):
+        if val is not None:
+            tun[key] = val
+    inst = build_scheme(cfg, ctx, bundle, SchemeCfg(args.scheme, tun))
     out1 = inst.run().clone()
     out2 = inst.run()
     torch.cuda.synchronize()
@@ -61,7 +68,8 @@ def main() -> int:
     flag = torch.tensor([1.0 if ok else 0.0], device=ctx.device)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if ctx.rank == 0:
-        print(json.dumps({"scheme": args.scheme, "preset": args.preset, "tokens": args.tokens, "world": ctx.world_size,
+        print(json.dumps({"scheme": args.scheme, "tunables": tun, "preset": args.preset, "tokens": args.tokens,
+                          "world": ctx.world_size,
                           "pass": bool(flag.item() > 0), "rank0": {k: rep[k] for k in ("cos_sim", "rel_p99", "max_abs",
                                                                                          "scale")},
                           "calib_max_abs": calib, "repeatable": same}), flush=True)

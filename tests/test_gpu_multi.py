@@ -30,6 +30,10 @@ def _port() -> int:
     ("d1", "mixtral", 512, []), ("d3", "mixtral", 512, []),
     ("d2", "dsv3", 512, []), ("d4", "dsv3", 512, []), ("d4", "dsv3", 1024, ["--zipf"]),
     ("d3", "qwen3", 256, []),
+    # copy-engine all-gather / reduce-scatter variants of the fused exchange
+    ("d3", "mixtral", 512, ["--ag-mode", "ce", "--rs-mode", "ce", "--rs-chunks", "2"]),
+    ("d4", "dsv3", 512, ["--ag-mode", "ce", "--rs-mode", "ce", "--rs-chunks", "1"]),
+    ("d3", "mixtral", 512, ["--ag-mode", "ce"]),
 ])
 def test_multi_gpu_scheme_matches_golden(scheme, preset, tokens, extra):
     n = min(_gpus(), 4)

@@ -108,6 +108,17 @@ def test_scheme_registry_and_tunables():
         build_scheme(configs.preset("tiny"), None, None, SchemeCfg("d1", {}))
 
 
+def test_p2p_exchange_tunables():
+    spec, _ = REGISTRY["d3"]
+    assert validate_tunables(spec, {}) == {"check_status": False, "ag_mode": "sm", "rs_mode": "sm", "rs_chunks": 4}
+    with pytest.raises(SchemeConfigError, match="violate schema"):
+        validate_tunables(REGISTRY["d1"][0], {"ag_mode": "ce"})   # NCCL schemes have no exchange knobs
+    with pytest.raises(SchemeConfigError, match="one of"):
+        build_scheme(configs.preset("tiny"), None, None, SchemeCfg("d4", {"ag_mode": "dma"}))
+    with pytest.raises(SchemeConfigError, match="1..8"):
+        build_scheme(configs.preset("tiny"), None, None, SchemeCfg("d3", {"rs_chunks": 9}))
+
+
 def test_int_tunable_rejects_bool():
     spec = SchemeSpec("x", "x", "f", "TP", "c", "fp8", "group128", False, {"n": TunableSpec(int, 2, "d")})
     with pytest.raises(SchemeConfigError):
