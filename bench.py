@@ -292,8 +292,8 @@ def main() -> int:
                     help="exchange of the multi-GPU layer: fused peer memory (default) or NCCL")
     ap.add_argument("--rs-mode", default="sm", choices=["sm", "ce"],
                     help="fused reduce-scatter: SM stores into the owners' slots (default) or copy-engine push")
-    ap.add_argument("--ag-mode", default="sm", choices=["sm", "ce"],
-                    help="fused all-gather: SM stores from the quant kernel (default) or copy-engine copies")
+    ap.add_argument("--ag-mode", default="auto", choices=["auto", "sm", "ce"],
+                    help="fused all-gather: SM stores from the quant kernel, copy-engine copies, or by block size")
     ap.add_argument("--chunks", type=int, default=4, help="down-GEMM column chunks of the copy-engine push")
     ap.add_argument("--ce-streams", type=int, default=2, help="side streams carrying the copy-engine push")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -500,7 +500,8 @@ def main() -> int:
             "config": {"workload": label, "tokens": T, "hidden": s.K, "intermediate": s.intermediate,
                        "experts": s.E, "top_k": s.top_k, "parallelism": f"{spec.parallel.lower()}{world}",
                        "scheme": code, "shard_level": level, "routing": cfg.routing.imbalance_kind,
-                       "exchange": (f"p2p ag={args.ag_mode} rs={args.rs_mode} chunks={len(layer.exchange.chunk_cols)}"
+                       "exchange": (f"p2p ag={layer.exchange.ag_mode} rs={args.rs_mode} "
+                                    f"chunks={len(layer.exchange.chunk_cols)}"
                                     if getattr(layer.exchange, "name", "") == "p2p" else
                                     getattr(layer.exchange, "name", "none")),
                        "l2": "weights > L2 and 256 MB L2 flush between timed steps"},

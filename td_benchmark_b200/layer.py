@@ -200,12 +200,16 @@ class P2PExchange:
     """Fused exchange over NVLink peer memory: no NCCL on the data path.
 
     All-gather (``ag_mode``):
-      "sm" (default) -- ``b2m_quant_push`` quantises the rank's tokens and stores them
-           into every rank's gather buffer with SM stores, then publishes the flags.
+      "sm" -- ``b2m_quant_push`` quantises the rank's tokens and stores them into every
+           rank's gather buffer with SM stores, then publishes the flags.
       "ce" -- ``b2m_quant_g128`` quantises into the rank's own rows of its gather buffer;
            copy engines copy that contiguous block (codes, then scales) to each peer on
            side streams, and ``b2m_signal`` (a stream memory write, no SM) publishes each
            peer's flag right after its copies.
+      "auto" (default) -- "ce" when a rank's block of codes is at least
+           ``AG_CE_MIN_BYTES``, else "sm".  On 8 B200s the copy engines won for the
+           DeepSeek-V3 EP shape (7.3 MB per peer: 1648 vs 1683 us per layer) and lost for
+           the Mixtral TP shape (2 MB per peer: 512 vs 457 us).
     Either way ``b2m_dispatch_rows_wait`` then moves rows into expert order as each
     source's flag arrives (own rows first).
 
@@ -224,11 +228,13 @@ class P2PExchange:
     """
     name = "p2p"
     MAX_CHUNKS = 8
+    AG_CE_MIN_BYTES = 4 << 20
 
-    def __init__(self, group=None, chunks: int = 4, rs_mode: str = "sm", ce_streams: int = 2, ag_mode: str = "sm"):
+    def __init__(self, group=None, chunks: int = 4, rs_mode: str = "sm", ce_streams: int = 2, ag_mode: str = "auto"):
         import torch.distributed as dist
-        if rs_mode not in ("ce", "sm") or ag_mode not in ("ce", "sm"):
-            raise ValueError(f"rs_mode and ag_mode must be 'ce' or 'sm', got {rs_mode!r}, {ag_mode!r}")
+        if rs_mode not in ("ce", "sm") or ag_mode not in ("ce", "sm", "auto"):
+            raise ValueError(f"rs_mode must be 'ce' or 'sm' and ag_mode 'ce', 'sm' or 'auto', got {rs_mode!r}, "
+                             f"{ag_mode!r}")
         self.ag_mode = ag_mode
         self.dist = dist
         self.group = group
@@ -247,6 +253,8 @@ class P2PExchange:
         from .symm import SymmetricWorkspace, ptr_array
 
         P, T, H, Tl = self.world_size, layer.T, layer.H, layer.T_local
+        if self.ag_mode == "auto":
+            self.ag_mode = "ce" if Tl * H >= self.AG_CE_MIN_BYTES else "sm"
         self.ws = SymmetricWorkspace({
             "xq": T * H, "xs": T * (H // 128) * 4, "slots": T * H * 2,
             "ag_flags": 4 * P, "rs_flags": 4 * P * self.MAX_CHUNKS, "counters": 16,

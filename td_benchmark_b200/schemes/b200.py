@@ -28,11 +28,12 @@ B200_TUNABLES = {
 }
 # peer-memory exchange knobs of d3 / d4 (P2PExchange)
 P2P_TUNABLES = {
-    "ag_mode": TunableSpec(str, "sm", "all-gather by SM stores from the quant kernel ('sm') or copy engines ('ce')"),
+    "ag_mode": TunableSpec(str, "auto", "all-gather by SM stores from the quant kernel ('sm'), copy engines ('ce') "
+                                        "or by block size ('auto')"),
     "rs_mode": TunableSpec(str, "sm", "reduce-scatter by SM stores from the combine ('sm') or copy engines ('ce')"),
     "rs_chunks": TunableSpec(int, 4, "down-GEMM column chunks of the copy-engine reduce-scatter (1..8)"),
 }
-_CHOICES = {"ag_mode": ("sm", "ce"), "rs_mode": ("sm", "ce")}
+_CHOICES = {"ag_mode": ("sm", "ce", "auto"), "rs_mode": ("sm", "ce")}
 
 
 def _spec(code: str, name: str, parallel: str, comm: str) -> SchemeSpec:
