@@ -1,14 +1,17 @@
-// K2: moe_align_block_size — histogram, scan and deterministic scatter in one CTA.
+// K2: moe_align_block_size — histogram, scan and deterministic scatter in one cluster.
 //
 // Contract: vLLM moe_align_block_size (moe_align_block_size.py:19-104), called by
 // the reference at moe_bench/overlap/overlap_forward.py:420-422.  Pairs of one
 // expert are emitted in ascending flat index, which makes the output unique.
 //
-// One CTA of 32 warps.  Warp w owns the contiguous pair range
-// [w*chunk, (w+1)*chunk).  Pass A: per-warp per-expert counts (warp_cnt[w][e], shared
-// atomics: a count does not depend on the order of the adds).
-// Scan: padded counts -> expert segment starts; per-(warp, expert) bases are the
-// segment start plus the counts of lower warps.  Pass C: each warp walks its range
+// One cluster of 8 CTAs x 32 warps.  Global warp g = cta * 32 + w owns the contiguous
+// pair range [g*chunk, (g+1)*chunk).  Pass A: per-warp per-expert counts (warp_cnt[w][e],
+// shared atomics: a count does not depend on the order of the adds); each CTA sums its
+// warps into ctot[e], and after a cluster barrier every CTA reads all eight ctot arrays
+// through distributed shared memory (no global scratch): the expert totals and the
+// counts of the lower CTAs.  Scan (redundant per CTA): padded counts -> expert segment
+// starts; per-(warp, expert) bases are the segment start plus the counts of lower CTAs
+// and lower warps.  Pass C: each warp walks its range
 // again in order and places every pair at base + rank inside its match group; the
 // optional inverse map pair_pos[pair] = sorted position (-1 for a non-local expert)
 // drives the row dispatch into the sorted operand layout of the gate/up GEMM, and the
@@ -19,20 +22,24 @@
 namespace b2m {
 namespace {
 
-constexpr int kAlignWarps = 32;
+constexpr int kAlignCtas = 8;  // one portable cluster
+constexpr int kAlignWarps = 32;  // per CTA
 constexpr int kAlignThreads = kAlignWarps * 32;
+constexpr int kAlignShared = kAlignWarps + 5;  // int32 arrays of E entries in shared memory
 constexpr int kMaxExperts = 1024;
 constexpr int kBatch = 8;  // ids loaded per lane before use (keeps 8 loads in flight per warp)
 
-__global__ void __launch_bounds__(kAlignThreads, 1)
+__global__ void __cluster_dims__(kAlignCtas, 1, 1) __launch_bounds__(kAlignThreads, 1)
     align_kernel(const int32_t* __restrict__ topk_ids, int64_t numel, int32_t num_experts, int32_t bs,
                  const int32_t* __restrict__ expert_map, int32_t* __restrict__ sorted_ids, int64_t sorted_cap,
                  int32_t* __restrict__ expert_ids, int64_t expert_ids_cap, int32_t* __restrict__ ntpp_out,
                  int32_t* __restrict__ pair_pos, int32_t* __restrict__ block_pairs) {
   extern __shared__ int32_t sm[];
   int32_t* warp_cnt = sm;                                  // [32][E] counts, then bases
-  int32_t* counts = warp_cnt + kAlignWarps * num_experts;  // [E]
-  int32_t* starts = counts + num_experts;                  // [E]
+  int32_t* ctot = warp_cnt + kAlignWarps * num_experts;    // [E] this CTA's counts (read by the cluster)
+  int32_t* counts = ctot + num_experts;                    // [E] totals
+  int32_t* lower = counts + num_experts;                   // [E] counts of the lower CTAs
+  int32_t* starts = lower + num_experts;                   // [E]
   int32_t* pstart = starts + num_experts;                  // [E] first pair index of each expert
   __shared__ int32_t s_total;
   __shared__ int32_t s_pairs;
@@ -40,8 +47,12 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int64_t chunk = (numel + kAlignWarps - 1) / kAlignWarps;
-  const int64_t lo = warp * chunk;
+  const uint32_t cta = cluster_ctarank();
+  const int64_t gthread = static_cast<int64_t>(cta) * kAlignThreads + tid;
+  constexpr int64_t kAllThreads = int64_t(kAlignCtas) * kAlignThreads;
+  const int64_t chunk = (numel + kAlignCtas * kAlignWarps - 1) / (kAlignCtas * kAlignWarps);
+  const int64_t lo_raw = (static_cast<int64_t>(cta) * kAlignWarps + warp) * chunk;
+  const int64_t lo = lo_raw < numel ? lo_raw : numel;
   const int64_t hi = lo + chunk < numel ? lo + chunk : numel;
 
   for (int i = tid; i < kAlignWarps * num_experts; i += kAlignThreads) warp_cnt[i] = 0;
@@ -62,13 +73,25 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
   }
   __syncthreads();
 
-  // Totals and padded sizes.
+  // This CTA's totals, then the cluster's: every CTA reads the eight ctot arrays.
   for (int e = tid; e < num_experts; e += kAlignThreads) {
     int32_t c = 0;
     for (int w = 0; w < kAlignWarps; ++w) c += warp_cnt[w * num_experts + e];
-    counts[e] = c;
+    ctot[e] = c;
   }
-  __syncthreads();
+  cluster_sync();  // every CTA's ctot is complete and visible to the cluster
+  for (int e = tid; e < num_experts; e += kAlignThreads) {
+    const uint32_t local = smem_u32(&ctot[e]);
+    int32_t all = 0, below = 0;
+    for (uint32_t c = 0; c < kAlignCtas; ++c) {
+      const int32_t v = c == cta ? ctot[e] : ld_dsmem_s32(mapa_shared(local, c));
+      all += v;
+      below += c < cta ? v : 0;
+    }
+    counts[e] = all;
+    lower[e] = below;
+  }
+  cluster_sync();  // no CTA reads another's shared memory after this point
 
   // Exclusive scan of padded counts (warp 0, 32 experts per step).
   if (warp == 0) {
@@ -113,7 +136,7 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
 
   // Per-(warp, expert) bases.
   for (int e = tid; e < num_experts; e += kAlignThreads) {
-    int32_t run = starts[e];
+    int32_t run = starts[e] + lower[e];
     for (int w = 0; w < kAlignWarps; ++w) {
       const int32_t c = warp_cnt[w * num_experts + e];
       warp_cnt[w * num_experts + e] = run;
@@ -149,9 +172,10 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
     }
   }
 
-  // Pads inside segments, block -> expert table.
+  // Pads inside segments, block -> expert table (each expert by one thread of the cluster).
   const int32_t pad_id = static_cast<int32_t>(numel);
-  for (int e = tid; e < num_experts; e += kAlignThreads) {
+  for (int64_t e64 = gthread; e64 < num_experts; e64 += kAllThreads) {
+    const int e = static_cast<int>(e64);
     const int32_t c = counts[e];
     const int32_t st = starts[e];
     const int32_t p = (c + bs - 1) / bs * bs;
@@ -167,11 +191,11 @@ __global__ void __launch_bounds__(kAlignThreads, 1)
       }
     }
   }
-  if (block_pairs && tid == 0) block_pairs[0] = s_pairs;
+  if (block_pairs && gthread == 0) block_pairs[0] = s_pairs;
   // Tails.
-  for (int64_t s = total + tid; s < sorted_cap; s += kAlignThreads) sorted_ids[s] = pad_id;
-  for (int64_t b = total / bs + tid; b < expert_ids_cap; b += kAlignThreads) expert_ids[b] = -1;
-  if (tid == 0) *ntpp_out = total;
+  for (int64_t s = total + gthread; s < sorted_cap; s += kAllThreads) sorted_ids[s] = pad_id;
+  for (int64_t b = total / bs + gthread; b < expert_ids_cap; b += kAllThreads) expert_ids[b] = -1;
+  if (gthread == 0) *ntpp_out = total;
 }
 
 }  // namespace
@@ -198,12 +222,12 @@ extern "C" int b2m_align(const int32_t* topk_ids, int64_t numel, int32_t num_exp
   if ((sorted_cap > 0 && !sorted_token_ids) || (expert_ids_cap > 0 && !expert_ids) || !num_tokens_post_padded ||
       (numel > 0 && !topk_ids))
     return fail(B2M_ERR_ARG, "align: null pointer");
-  const size_t smem = (size_t(kAlignWarps) + 3) * num_experts * sizeof(int32_t);
+  const size_t smem = size_t(kAlignShared) * num_experts * sizeof(int32_t);
   if (smem > 48 * 1024)
     B2M_TRY(check_cuda(
         cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
         "align: cudaFuncSetAttribute"));
-  align_kernel<<<1, kAlignThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+  align_kernel<<<kAlignCtas, kAlignThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       topk_ids, numel, num_experts, block_size, expert_map, sorted_token_ids, sorted_cap, expert_ids,
       expert_ids_cap, num_tokens_post_padded, pair_pos, block_pairs);
   return check_cuda(cudaGetLastError(), "align launch");

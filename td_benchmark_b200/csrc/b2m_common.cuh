@@ -269,8 +269,8 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   return r;
 }
 
-// All threads of both CTAs of the cluster.  Every exit path of a paired kernel must
-// reach it (a CTA's shared memory must stay alive while its peer may still read it).
+// All threads of all CTAs of the cluster.  Every exit path of a cluster kernel must
+// reach it (a CTA's shared memory must stay alive while a peer may still read it).
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -280,6 +280,13 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t local_addr, uint32_t ct
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(cta));
   return r;
+}
+
+// Load from another CTA's shared memory (distributed shared memory of the cluster).
+__device__ __forceinline__ int32_t ld_dsmem_s32(uint32_t cluster_addr) {
+  int32_t v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
