@@ -404,4 +404,63 @@ __device__ __forceinline__ float halfwarp_amax(const float (&f)[8]) {
 }
 
 
+// ------------------------------------------------------------------ top-k combine pieces
+__device__ __forceinline__ void acc_bf16x8(const uint4& u, float (&a)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    a[2 * i] += __uint_as_float(w[i] << 16);
+    a[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float (&a)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a[2 * i], a[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Bit j set when pair (t, j) counts on this rank: its expert is local, or there is no
+// expert map (tensor parallel).  Called by a whole warp; lanes j < top_k read the ids.
+__device__ __forceinline__ uint32_t local_pair_mask(const int32_t* __restrict__ topk_ids,
+                                                    const int32_t* __restrict__ expert_map, int64_t t, int top_k,
+                                                    int lane) {
+  if (!expert_map) return 0xffffffffu;
+  bool local = false;
+  if (lane < top_k) local = __ldg(expert_map + __ldg(topk_ids + t * top_k + lane)) >= 0;
+  return __ballot_sync(0xffffffffu, local);
+}
+
+// Eight columns [c, c + 8) of token t's combined row: the staged rows of its counting
+// pairs summed in ascending j in fp32 (pairs j >= 32 are tested one by one), then the
+// shared expert's row, one rounding to bf16.  All loads of a group of eight pairs are
+// issued before the first add.
+__device__ __forceinline__ uint4 combine_vec(const __nv_bfloat16* __restrict__ staged, int64_t t, int top_k,
+                                             int64_t hidden, int64_t c, uint32_t mask,
+                                             const int32_t* __restrict__ topk_ids,
+                                             const int32_t* __restrict__ expert_map,
+                                             const __nv_bfloat16* __restrict__ shared) {
+  float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int j0 = 0; j0 < top_k; j0 += 8) {
+    uint4 u[8];
+    bool use[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int jj = j0 + j;
+      use[j] = jj < top_k && (jj < 32 ? ((mask >> jj) & 1u) != 0
+                                      : (!expert_map || __ldg(expert_map + __ldg(topk_ids + t * top_k + jj)) >= 0));
+      if (use[j]) u[j] = __ldg(reinterpret_cast<const uint4*>(staged + (t * top_k + jj) * hidden + c));
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (use[j]) acc_bf16x8(u[j], a);
+  }
+  if (shared) acc_bf16x8(__ldg(reinterpret_cast<const uint4*>(shared + t * hidden + c)), a);
+  return pack_bf16x8(a);
+}
+
 }  // namespace b2m

@@ -7,44 +7,22 @@ namespace {
 
 constexpr int kCombineThreads = 256;
 
-__device__ __forceinline__ void acc_bf16x8(const uint4& u, float (&a)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    a[2 * i] += __uint_as_float(w[i] << 16);
-    a[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
-  }
-}
-
-__device__ __forceinline__ uint4 pack_bf16x8(const float (&a)[8]) {
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(a[2 * i], a[2 * i + 1]);
-    w[i] = *reinterpret_cast<const uint32_t*>(&h);
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
-}
-
-// out[t, :] = bf16(sum_j staged[t*k + j, :] + shared[t, :]); one thread per 8 columns.
+// out[t, :] = bf16(sum_j staged[t*k + j, :] + shared[t, :]): one warp per token, so the
+// token's expert ids and map entries are read once (a warp-uniform pair mask) and the
+// lanes walk the row 8 columns at a time.
 __global__ void __launch_bounds__(kCombineThreads)
     combine_kernel(const __nv_bfloat16* __restrict__ staged, int64_t tokens, int top_k, int64_t hidden,
                    const int32_t* __restrict__ topk_ids, const int32_t* __restrict__ expert_map,
                    const __nv_bfloat16* __restrict__ shared, __nv_bfloat16* __restrict__ out, int64_t ld_out) {
-  const int64_t vec_per_row = hidden / 8;
-  const int64_t total = tokens * vec_per_row;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * kCombineThreads + threadIdx.x; v < total;
-       v += static_cast<int64_t>(gridDim.x) * kCombineThreads) {
-    const int64_t t = v / vec_per_row;
-    const int64_t c = (v - t * vec_per_row) * 8;
-    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < top_k; ++j) {
-      const int64_t pair = t * top_k + j;
-      if (expert_map && __ldg(expert_map + __ldg(topk_ids + pair)) < 0) continue;
-      acc_bf16x8(__ldg(reinterpret_cast<const uint4*>(staged + pair * hidden + c)), a);
-    }
-    if (shared) acc_bf16x8(__ldg(reinterpret_cast<const uint4*>(shared + t * hidden + c)), a);
-    *reinterpret_cast<uint4*>(out + t * ld_out + c) = pack_bf16x8(a);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kCombineThreads + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kCombineThreads) >> 5;
+  for (int64_t t = warp; t < tokens; t += nwarps) {
+    const uint32_t mask = local_pair_mask(topk_ids, expert_map, t, top_k, lane);
+#pragma unroll 2
+    for (int64_t c = lane * 8; c < hidden; c += 256)
+      *reinterpret_cast<uint4*>(out + t * ld_out + c) =
+          combine_vec(staged, t, top_k, hidden, c, mask, topk_ids, expert_map, shared);
   }
 }
 
@@ -99,8 +77,7 @@ extern "C" int b2m_combine(const void* staged, int64_t tokens, int32_t top_k, in
   if (!staged || !out || (expert_map && !topk_ids)) return fail(B2M_ERR_ARG, "combine: null pointer");
   if (!aligned16(staged) || !aligned16(out) || (shared && !aligned16(shared)))
     return fail(B2M_ERR_ARG, "combine: pointers must be 16-byte aligned");
-  const int64_t total = tokens * (hidden / 8);
-  int64_t blocks = (total + kCombineThreads - 1) / kCombineThreads;
+  int64_t blocks = (tokens * 32 + kCombineThreads - 1) / kCombineThreads;  // a warp per token
   if (blocks > int64_t(num_sms) * 8) blocks = int64_t(num_sms) * 8;
   combine_kernel<<<static_cast<unsigned>(blocks), kCombineThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, topk_ids, expert_map,

@@ -164,58 +164,25 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // ---------------------------------------------------------------- reduce-scatter push
-__device__ __forceinline__ void acc_bf16x8(const uint4& u, float (&a)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    a[2 * i] += __uint_as_float(w[i] << 16);
-    a[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
-  }
-}
-
-__device__ __forceinline__ uint4 pack_bf16x8(const float (&a)[8]) {
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(a[2 * i], a[2 * i + 1]);
-    w[i] = *reinterpret_cast<const uint32_t*>(&h);
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
-}
-
+// One warp per token (pair mask read once), lanes over the column window 8 at a time;
+// the combined row goes to the owner's slot for this source.
 __global__ void __launch_bounds__(kThreads)
     combine_push_kernel(const __nv_bfloat16* __restrict__ staged, int64_t tokens, int top_k, int64_t hidden,
                         int64_t col0, int64_t col1, const int32_t* __restrict__ topk_ids,
                         const int32_t* __restrict__ expert_map, const __nv_bfloat16* __restrict__ shared, int world,
                         int rank, PeerPtrs slots, FlagPtrs flags, uint32_t epoch, int32_t* counter) {
-  const int64_t vec = (col1 - col0) / 8;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
   const int64_t per_rank = tokens / world;
-  const int64_t total = tokens * vec;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; v < total;
-       v += static_cast<int64_t>(gridDim.x) * kThreads) {
-    const int64_t t = v / vec;
-    const int64_t c = col0 + (v - t * vec) * 8;
-    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    // top-k rows in groups of 8: every load of a group is issued before the first add
-    for (int j0 = 0; j0 < top_k; j0 += 8) {
-      const int n = min(8, top_k - j0);
-      uint4 u[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        u[j] = make_uint4(0, 0, 0, 0);
-        if (j < n) {
-          const int64_t pair = t * top_k + j0 + j;
-          if (!expert_map || __ldg(expert_map + __ldg(topk_ids + pair)) >= 0)
-            u[j] = __ldg(reinterpret_cast<const uint4*>(staged + pair * hidden + c));
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc_bf16x8(u[j], a);  // zero words add +0.0f
-    }
-    if (shared) acc_bf16x8(__ldg(reinterpret_cast<const uint4*>(shared + t * hidden + c)), a);
+  for (int64_t t = warp; t < tokens; t += nwarps) {
+    const uint32_t mask = local_pair_mask(topk_ids, expert_map, t, top_k, lane);
     const int owner = static_cast<int>(t / per_rank);
     const int64_t slot_row = static_cast<int64_t>(rank) * per_rank + (t - owner * per_rank);
-    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(slots.p[owner]) + slot_row * hidden + c) = pack_bf16x8(a);
+    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(slots.p[owner]) + slot_row * hidden;
+#pragma unroll 2
+    for (int64_t c = col0 + lane * 8; c < col1; c += 256)
+      *reinterpret_cast<uint4*>(dst + c) = combine_vec(staged, t, top_k, hidden, c, mask, topk_ids, expert_map, shared);
   }
   if (counter) publish_when_grid_done(counter, flags, world, epoch);
 }
@@ -453,7 +420,7 @@ int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t 
     sl.p[r] = slot_dst[r];
     f.p[r] = counter ? flag_dst[r] : nullptr;
   }
-  int grid = grid_for(tokens * ((col_end - col_begin) / 8), num_sms, 8);
+  int grid = grid_for(tokens * 32, num_sms, 8);  // a warp per token
   if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
   combine_push_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, col_begin, col_end, topk_ids, expert_map,
