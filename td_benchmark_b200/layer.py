@@ -519,8 +519,21 @@ class MoELayer:
             n += 3 + (1 if (self.ep and name == "nccl") else 0)
         return n
 
-    def forward(self, x_local: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
-        """x_local bf16 [T/P, H]; topk_ids int32 / topk_weights fp32 [T, k] (all tokens) -> bf16 [T/P, H]."""
+    def forward(self, x_local: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        """x_local bf16 [T/P, H]; topk_ids int32 / topk_weights fp32 [T, k] (all tokens) -> bf16 [T/P, H].
+
+        The result goes to ``out`` (contiguous bf16 [T/P, H] on this device) when given, else to
+        the layer's own output buffer, which the next call overwrites."""
+        if out is not None:
+            if out.shape != self.out_local.shape or out.dtype != torch.bfloat16 or out.device != self.device or \
+                    not out.is_contiguous():
+                raise ValueError(f"out must be contiguous bf16 {tuple(self.out_local.shape)} on {self.device}")
+            own, self.out_local = self.out_local, out
+            try:
+                return self.forward(x_local, topk_ids, topk_weights)
+            finally:
+                self.out_local = own
         self.route_and_dispatch(x_local, topk_ids)
         self.gemm1()
         shared_out = None

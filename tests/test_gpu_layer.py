@@ -104,3 +104,33 @@ def test_baseline_shapes_vs_torch_golden(name, over):
                                          bundle.routing.topk_weights_full, ck.w1.fp8, ck.w1.scale, ck.w2.fp8,
                                          ck.w2.scale, sw)
     _gates(out.float().cpu().numpy(), g.cpu().numpy(), calib)
+
+
+def test_host_pipeline_matches_direct_forward():
+    """Double-buffered host pipeline: each step's pinned-host result equals a direct forward
+    of that step's inputs (different inputs per step, slots reused)."""
+    from td_benchmark_b200.pipeline import HostPipeline
+    from td_benchmark_b200.schemes import REGISTRY
+    from td_benchmark_b200.schemes.b200 import build_layer
+
+    cfg = configs.preset("mixtral", M=256)
+    bundle = data.build_bundle(cfg, device=DEV)
+    ctx = DistContext(rank=0, world_size=1, local_rank=0, device=DEV)
+    layer, _ = build_layer(REGISTRY["d1"][0], cfg, ctx, bundle)
+    ids = bundle.routing.topk_ids_full.contiguous()
+    wts = bundle.routing.topk_weights_full.contiguous()
+    xs = [(bundle.hidden_local * (1.0 + 0.25 * i)).to(torch.bfloat16).contiguous() for i in range(5)]
+    want = [layer.forward(x, ids, wts).clone() for x in xs]
+    torch.cuda.synchronize()
+    pipe = HostPipeline(layer)
+    outs = [torch.empty(want[0].shape, dtype=torch.bfloat16).pin_memory() for _ in xs]
+    for x, o in zip(xs, outs):
+        pipe.submit(x.cpu().pin_memory(), ids.cpu().pin_memory(), wts.cpu().pin_memory(), o)
+    pipe.drain()
+    layer.check()
+    for w, o in zip(want, outs):
+        assert torch.equal(w.cpu(), o)
+    out_dev = torch.empty_like(want[0])
+    assert layer.forward(xs[2], ids, wts, out=out_dev) is out_dev and torch.equal(out_dev, want[2])
+    with pytest.raises(ValueError):
+        layer.forward(xs[0], ids, wts, out=torch.empty(3, dtype=torch.bfloat16, device=DEV))
