@@ -290,8 +290,9 @@ def main() -> int:
     ap.add_argument("--impl", default="b2m", choices=["b2m", "reference"])
     ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"],
                     help="exchange of the multi-GPU layer: fused peer memory (default) or NCCL")
-    ap.add_argument("--rs-mode", default="sm", choices=["sm", "ce"],
-                    help="fused reduce-scatter: SM stores into the owners' slots (default) or copy-engine push")
+    ap.add_argument("--rs-mode", default="sm", choices=["sm", "gemm", "ce"],
+                    help="fused reduce-scatter: SM stores from the combine (default), from the down GEMM's epilogue, "
+                         "or copy-engine push")
     ap.add_argument("--ag-mode", default="auto", choices=["auto", "sm", "ce"],
                     help="fused all-gather: SM stores from the quant kernel, copy-engine copies, or by block size")
     ap.add_argument("--chunks", type=int, default=4, help="down-GEMM column chunks of the copy-engine push")

@@ -169,6 +169,23 @@ int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int32
               int64_t numel, const float* topk_weights, void* out_bf16, int64_t col_begin, int64_t col_end,
               int32_t max_ctas, int32_t* dev_status, void* stream);
 
+/* Down GEMM fused with the reduce-scatter push (replaces the down GEMM's bf16 output, the
+ * top-k sum and reduce_scatter_tensor, overlap_forward.py:564-608): b2m_gemm2 whose
+ * routed-weighted bf16 row of pair p is stored straight into its owner's receive buffer
+ * (peer memory) as its tile finishes, so the NVLink transfer runs under the GEMM:
+ * owner q = p / pairs_per_owner, row row0 + p - q * pairs_per_owner of owner_dst[q]
+ * (bf16 rows of `hidden`).  pairs_per_owner * world == numel, world <= 8.  Tensor
+ * parallel: every rank writes its partial of every pair, row0 = rank * pairs_per_owner
+ * into owner buffers of world * pairs_per_owner rows; expert parallel: each pair is
+ * computed by exactly one rank, row0 = 0 into buffers of pairs_per_owner rows.  The
+ * owner sums with b2m_rs_combine once every source has published its flag (b2m_signal
+ * after this kernel on the same stream). */
+int b2m_gemm2_scatter(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int32_t inter, const void* w2,
+                      const float* w2_scale, int32_t num_experts, int64_t hidden, const int32_t* sorted_token_ids,
+                      const int32_t* expert_ids, const int32_t* num_tokens_post_padded, const int32_t* block_pairs,
+                      int64_t numel, const float* topk_weights, void* const* owner_dst, int32_t world,
+                      int64_t pairs_per_owner, int64_t row0, int32_t* dev_status, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Top-k combine (+ shared expert add).
  * Replaces the torch.sum over top-k and the shared add of
@@ -252,6 +269,16 @@ int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t 
  * `stream`, each preceded by a fence equivalent to __threadfence_system, executed
  * without an SM (so it cannot be starved by kernels that spin on flags). */
 int b2m_signal(uint32_t* const* flag_dst, int32_t world, uint32_t epoch, void* stream);
+
+/* Owner side of the scattered reduce-scatter (after b2m_gemm2_scatter on every source):
+ * once flags[0..nflags) are all >= epoch,
+ *   out[t, :] = bf16( sum_{s < nsrc} sum_{j < top_k} recv[(s*rows + t)*top_k + j, :] + add[t, :] )
+ * in fp32 with one rounding (the top-k sum and the cross-rank sum of
+ * overlap_forward.py:581-608 in one pass).  add (bf16 [rows, hidden]) may be NULL;
+ * a flag wait that runs out records B2M_STATUS_TIMEOUT_PEER in dev_status. */
+int b2m_rs_combine(const void* recv, int64_t rows, int32_t top_k, int64_t hidden, int32_t nsrc,
+                   const uint32_t* flags, int32_t nflags, uint32_t epoch, const void* add, void* out,
+                   int32_t* dev_status, void* stream);
 
 /* Owner side of the reduce-scatter: once the nchunks*world flags (chunk-major) are all
  * >= epoch, out[t, :] = bf16( sum_{r=0..world-1} slots[r*rows + t, :] + add[t, :] )

@@ -27,6 +27,8 @@ SIGNATURES: dict[str, list] = {
     "b2m_w1_interleave": [_p, _p, _i32, _i32, _i64, _p, _p, _p],
     "b2m_gemm1": [_p, _p, _i64, _i64, _p, _p, _i32, _i32, _p, _p, _p, _p, _p, _p, _p],
     "b2m_gemm2": [_p, _p, _i64, _i32, _p, _p, _i32, _i64, _p, _p, _p, _p, _i64, _p, _p, _i64, _i64, _i32, _p, _p],
+    "b2m_gemm2_scatter": [_p, _p, _i64, _i32, _p, _p, _i32, _i64, _p, _p, _p, _p, _i64, _p, _p, _i32, _i64, _i64, _p,
+                          _p],
     "b2m_combine": [_p, _i64, _i32, _i64, _p, _p, _p, _p, _i64, _p],
     "b2m_copy_async": [_p, _p, _i64, _p],
     "b2m_copy2d_async": [_p, _i64, _p, _i64, _i64, _i64, _p],
@@ -41,6 +43,7 @@ SIGNATURES: dict[str, list] = {
     "b2m_combine_push": [_p, _i64, _i32, _i64, _i64, _i64, _p, _p, _p, _i32, _i32, _p, _p, _c.c_uint32, _p, _i32,
                          _p],
     "b2m_signal": [_p, _i32, _c.c_uint32, _p],
+    "b2m_rs_combine": [_p, _i64, _i32, _i64, _i32, _p, _i32, _c.c_uint32, _p, _p, _p, _p],
     "b2m_rs_reduce": [_p, _i64, _i64, _i32, _i32, _p, _c.c_uint32, _p, _p, _p, _p],
 }
 

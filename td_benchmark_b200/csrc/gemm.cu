@@ -101,6 +101,13 @@ struct GemmParams {
   int64_t hidden;
   int32_t* status;
   uint64_t timeout_ns;
+  // Down GEMM scatter (rs_world > 0): the row of pair p goes to owner q = p / rs_pairs_per_owner,
+  // row rs_row0 + p - q * rs_pairs_per_owner of rs_dst[q] (another rank's receive buffer),
+  // instead of row p of out_bf16.
+  __nv_bfloat16* rs_dst[8];
+  int64_t rs_pairs_per_owner;
+  int64_t rs_row0;
+  int32_t rs_world;
 };
 
 // silu(x) = x * sigmoid(x).  The gate/up intermediate is requantised to e4m3 right
@@ -280,7 +287,12 @@ __device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)
   } else {
     const bool cols_valid = 2 * nt + h < p.n_blocks;
     if (valid && cols_valid) {
-      __nv_bfloat16* dst = p.out_bf16 + static_cast<int64_t>(pair) * p.hidden + nt * BN + 128 * h;
+      __nv_bfloat16* row = p.out_bf16 + static_cast<int64_t>(pair) * p.hidden;
+      if (p.rs_world > 0) {
+        const int q = static_cast<int>(pair / p.rs_pairs_per_owner);
+        row = p.rs_dst[q] + (p.rs_row0 + pair - q * p.rs_pairs_per_owner) * p.hidden;
+      }
+      __nv_bfloat16* dst = row + nt * BN + 128 * h;
 #pragma unroll
       for (int i = 0; i < 128; i += 8) {
         uint32_t u[4];
@@ -899,12 +911,21 @@ extern "C" int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t r
   return launch_gemm<true>(ma, mb, p, num_sms, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int32_t inter, const void* w2,
-                         const float* w2_scale, int32_t num_experts, int64_t hidden, const int32_t* sorted_token_ids,
-                         const int32_t* expert_ids, const int32_t* num_tokens_post_padded,
-                         const int32_t* block_pairs, int64_t numel, const float* topk_weights, void* out_bf16,
-                         int64_t col_begin, int64_t col_end, int32_t max_ctas, int32_t* dev_status, void* stream) {
-  using namespace b2m;
+namespace b2m {
+namespace {
+
+struct Scatter {
+  void* const* dst;
+  int32_t world;
+  int64_t pairs_per_owner;
+  int64_t row0;
+};
+
+int gemm2_impl(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int32_t inter, const void* w2,
+               const float* w2_scale, int32_t num_experts, int64_t hidden, const int32_t* sorted_token_ids,
+               const int32_t* expert_ids, const int32_t* num_tokens_post_padded, const int32_t* block_pairs,
+               int64_t numel, const float* topk_weights, void* out_bf16, int64_t col_begin, int64_t col_end,
+               int32_t max_ctas, const Scatter* sc, int32_t* dev_status, void* stream) {
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
   if (hidden <= 0 || hidden % 128 || inter <= 0 || inter % 128 || num_experts <= 0 || rows_cap <= 0 ||
@@ -912,9 +933,9 @@ extern "C" int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows
     return fail(B2M_ERR_ARG, "gemm2: need hidden%%128==0 (%lld), inter%%128==0 (%d), rows_cap%%128==0 (%lld)",
                 (long long)hidden, inter, (long long)rows_cap);
   if (!a_fp8 || !a_scale_t || !w2 || !w2_scale || !sorted_token_ids || !expert_ids || !num_tokens_post_padded ||
-      !out_bf16)
+      (!sc && !out_bf16))
     return fail(B2M_ERR_ARG, "gemm2: null pointer");
-  if (!aligned16(a_fp8) || !aligned16(a_scale_t) || !aligned16(w2) || !aligned16(out_bf16))
+  if (!aligned16(a_fp8) || !aligned16(a_scale_t) || !aligned16(w2) || (out_bf16 && !aligned16(out_bf16)))
     return fail(B2M_ERR_ARG, "gemm2: A, A scales, W2 and out must be 16-byte aligned");
   if (rows_cap / BM > INT32_MAX || numel >= INT32_MAX) return fail(B2M_ERR_ARG, "gemm2: sizes overflow int32");
   if (col_end <= 0) col_end = hidden;
@@ -947,7 +968,45 @@ extern "C" int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows
   p.hidden = hidden;
   p.status = dev_status;
   p.timeout_ns = timeout_ns();
+  if (sc) {
+    if (sc->world < 1 || sc->world > 8 || !sc->dst || sc->pairs_per_owner <= 0 || sc->row0 < 0 ||
+        sc->pairs_per_owner * sc->world != numel)
+      return fail(B2M_ERR_ARG, "gemm2_scatter: need 1 <= world <= 8, pairs_per_owner * world == numel (%lld), row0 >= 0",
+                  (long long)numel);
+    for (int r = 0; r < sc->world; ++r) {
+      if (!sc->dst[r] || !aligned16(sc->dst[r])) return fail(B2M_ERR_ARG, "gemm2_scatter: bad owner buffer %d", r);
+      p.rs_dst[r] = static_cast<__nv_bfloat16*>(sc->dst[r]);
+    }
+    p.rs_world = sc->world;
+    p.rs_pairs_per_owner = sc->pairs_per_owner;
+    p.rs_row0 = sc->row0;
+  }
   if (block_pairs)
     return launch_gemm_pair<false>(ma, mb, p, block_pairs, num_sms, static_cast<cudaStream_t>(stream));
   return launch_gemm<false>(ma, mb, p, num_sms, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+}  // namespace b2m
+
+extern "C" int b2m_gemm2(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int32_t inter, const void* w2,
+                         const float* w2_scale, int32_t num_experts, int64_t hidden, const int32_t* sorted_token_ids,
+                         const int32_t* expert_ids, const int32_t* num_tokens_post_padded,
+                         const int32_t* block_pairs, int64_t numel, const float* topk_weights, void* out_bf16,
+                         int64_t col_begin, int64_t col_end, int32_t max_ctas, int32_t* dev_status, void* stream) {
+  return b2m::gemm2_impl(a_fp8, a_scale_t, rows_cap, inter, w2, w2_scale, num_experts, hidden, sorted_token_ids,
+                         expert_ids, num_tokens_post_padded, block_pairs, numel, topk_weights, out_bf16, col_begin,
+                         col_end, max_ctas, nullptr, dev_status, stream);
+}
+
+extern "C" int b2m_gemm2_scatter(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int32_t inter,
+                                 const void* w2, const float* w2_scale, int32_t num_experts, int64_t hidden,
+                                 const int32_t* sorted_token_ids, const int32_t* expert_ids,
+                                 const int32_t* num_tokens_post_padded, const int32_t* block_pairs, int64_t numel,
+                                 const float* topk_weights, void* const* owner_dst, int32_t world,
+                                 int64_t pairs_per_owner, int64_t row0, int32_t* dev_status, void* stream) {
+  const b2m::Scatter sc{owner_dst, world, pairs_per_owner, row0};
+  return b2m::gemm2_impl(a_fp8, a_scale_t, rows_cap, inter, w2, w2_scale, num_experts, hidden, sorted_token_ids,
+                         expert_ids, num_tokens_post_padded, block_pairs, numel, topk_weights, nullptr, 0, 0, 0, &sc,
+                         dev_status, stream);
 }

@@ -212,6 +212,47 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Owner side of the scattered reduce-scatter (b2m_gemm2_scatter wrote every pair row of this
+// owner's tokens into recv): out[t] = bf16(sum over sources s, then pairs j, of
+// recv[(s * rows + t) * top_k + j] + add[t]) in fp32 with one rounding, after every flag
+// reached epoch.  One warp per token; all loads of a group of eight rows are issued first.
+__global__ void __launch_bounds__(kThreads)
+    rs_combine_kernel(const __nv_bfloat16* __restrict__ recv, int64_t rows, int top_k, int64_t hidden, int nsrc,
+                      const uint32_t* flags, int nflags, uint32_t epoch, const __nv_bfloat16* __restrict__ add,
+                      __nv_bfloat16* __restrict__ out, int32_t* status, uint64_t timeout_ns) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if (threadIdx.x < nflags && !wait_flag_geq(flags + threadIdx.x, epoch, timeout_ns, status, B2M_STATUS_TIMEOUT_PEER))
+    s_ok = 0;
+  __syncthreads();
+  if (!s_ok) return;  // status already records the timeout
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
+  const int nrow = nsrc * top_k;
+  for (int64_t t = warp; t < rows; t += nwarps) {
+    for (int64_t c = lane * 8; c < hidden; c += 256) {
+      float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int i0 = 0; i0 < nrow; i0 += 8) {
+        uint4 u[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (i0 + i < nrow) {
+            const int src = (i0 + i) / top_k, j = (i0 + i) - src * top_k;
+            u[i] = __ldcg(reinterpret_cast<const uint4*>(recv + ((src * rows + t) * top_k + j) * hidden + c));
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (i0 + i < nrow) acc_bf16x8(u[i], a);
+      }
+      if (add) acc_bf16x8(*reinterpret_cast<const uint4*>(add + t * hidden + c), a);
+      *reinterpret_cast<uint4*>(out + t * hidden + c) = pack_bf16x8(a);
+    }
+  }
+}
+
 int grid_for(int64_t work, int num_sms, int per_sm) {
   int64_t b = (work + kThreads - 1) / kThreads;
   if (b > int64_t(num_sms) * per_sm) b = int64_t(num_sms) * per_sm;
@@ -440,6 +481,21 @@ int b2m_signal(uint32_t* const* flag_dst, int32_t world, uint32_t epoch, void* s
     if (rc != CUDA_SUCCESS) return fail(B2M_ERR_CUDA, "signal: cuStreamWriteValue32 failed (%d) on flag %d", (int)rc, r);
   }
   return B2M_OK;
+}
+
+int b2m_rs_combine(const void* recv, int64_t rows, int32_t top_k, int64_t hidden, int32_t nsrc,
+                   const uint32_t* flags, int32_t nflags, uint32_t epoch, const void* add, void* out,
+                   int32_t* dev_status, void* stream) {
+  using namespace b2m;
+  int num_sms = 0;
+  B2M_TRY(require_sm100(&num_sms));
+  if (rows <= 0 || hidden <= 0 || hidden % 8 || top_k < 1 || nsrc < 1 || nsrc > kMaxWorld || nflags < 1 ||
+      nflags > kThreads || !recv || !flags || !out || !aligned16(recv) || !aligned16(out) || (add && !aligned16(add)))
+    return fail(B2M_ERR_ARG, "rs_combine: bad shape/pointers (hidden %% 8 == 0, 1 <= nsrc <= 8, 16-byte rows)");
+  rs_combine_kernel<<<grid_for(rows * 32, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(recv), rows, top_k, hidden, nsrc, flags, nflags, epoch,
+      static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out), dev_status, timeout_ns());
+  return check_cuda(cudaGetLastError(), "rs_combine launch");
 }
 
 int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world, int32_t nchunks,

@@ -214,6 +214,16 @@ class P2PExchange:
     source's flag arrives (own rows first).
 
     Reduce-scatter (``rs_mode``):
+      "gemm" -- the down GEMM itself stores each pair's routed-weighted row into its
+           owner's receive buffer as the tile finishes (``b2m_gemm2_scatter``), so the
+           NVLink traffic runs under the GEMM; ``b2m_signal`` publishes the flags after it
+           and the owner sums sources and top-k rows in one pass (``b2m_rs_combine``).  Not
+           with a tensor-parallel shared expert (its partials must join before the push).
+           Correct but slower as built: every epilogue thread stores 16 bytes of a different
+           row per instruction, and such small remote writes stall the GEMM (DeepSeek-V3
+           EP8: down GEMM 1424 us instead of 448, layer 2464 vs 1648 us; Mixtral TP2 1015
+           vs 995 us).  Rows would have to leave through shared memory as whole-row bulk
+           copies, for which the GEMM has no shared memory to spare.
       "sm" (default) -- after the whole down GEMM, ``b2m_combine_push`` stores each
            token's partial into its owner's slot with SM stores and publishes the flags.
       "ce" -- the down GEMM runs in ``chunks`` column chunks on all SMs; after each chunk
@@ -232,9 +242,9 @@ class P2PExchange:
 
     def __init__(self, group=None, chunks: int = 4, rs_mode: str = "sm", ce_streams: int = 2, ag_mode: str = "auto"):
         import torch.distributed as dist
-        if rs_mode not in ("ce", "sm") or ag_mode not in ("ce", "sm", "auto"):
-            raise ValueError(f"rs_mode must be 'ce' or 'sm' and ag_mode 'ce', 'sm' or 'auto', got {rs_mode!r}, "
-                             f"{ag_mode!r}")
+        if rs_mode not in ("ce", "sm", "gemm") or ag_mode not in ("ce", "sm", "auto"):
+            raise ValueError(f"rs_mode must be 'gemm', 'ce' or 'sm' and ag_mode 'ce', 'sm' or 'auto', got "
+                             f"{rs_mode!r}, {ag_mode!r}")
         self.ag_mode = ag_mode
         self.dist = dist
         self.group = group
@@ -255,21 +265,33 @@ class P2PExchange:
         P, T, H, Tl = self.world_size, layer.T, layer.H, layer.T_local
         if self.ag_mode == "auto":
             self.ag_mode = "ce" if Tl * H >= self.AG_CE_MIN_BYTES else "sm"
-        self.ws = SymmetricWorkspace({
-            "xq": T * H, "xs": T * (H // 128) * 4, "slots": T * H * 2,
-            "ag_flags": 4 * P, "rs_flags": 4 * P * self.MAX_CHUNKS, "counters": 16,
-        }, self.group, layer.device)
+        if self.rs_mode == "gemm" and layer.shared is not None and not layer.ep:
+            raise ValueError("rs_mode='gemm' cannot add a tensor-parallel shared expert; use 'sm'")
+        # receive rows of the scattered reduce-scatter: one block of T/P*k rows per source (TP)
+        # or a single block (EP: every pair has exactly one writer)
+        self.rs_nsrc = (1 if layer.ep else P)
+        layout = {"xq": T * H, "xs": T * (H // 128) * 4, "ag_flags": 4 * P, "rs_flags": 4 * P * self.MAX_CHUNKS,
+                  "counters": 16}
+        if self.rs_mode == "gemm":
+            layout["recv"] = self.rs_nsrc * Tl * layer.top_k * H * 2
+        else:
+            layout["slots"] = T * H * 2
+        self.ws = SymmetricWorkspace(layout, self.group, layer.device)
         ws = self.ws
         layer.xq = ws.tensor("xq", (T, H), torch.uint8).view(ops.FP8)
         layer.xs = ws.tensor("xs", (T, H // 128), torch.float32)
-        self.slots = ws.tensor("slots", (T, H), torch.bfloat16)   # [P source blocks of T/P rows, H]
+        if self.rs_mode == "gemm":
+            self._recv_dst = ptr_array([ws.peer("recv", r) for r in range(P)])
+        else:
+            self.slots = ws.tensor("slots", (T, H), torch.bfloat16)   # [P source blocks of T/P rows, H]
         self.ag_flags = ws.local("ag_flags")
         self.rs_flags = ws.local("rs_flags")
         self.counters = ws.local("counters")
         self._q_dst = ptr_array([ws.peer("xq", r) for r in range(P)])
         self._s_dst = ptr_array([ws.peer("xs", r) for r in range(P)])
         self._ag_dst = ptr_array([ws.peer("ag_flags", r) + 4 * self.rank for r in range(P)])
-        self._slot_dst = ptr_array([ws.peer("slots", r) for r in range(P)])
+        if self.rs_mode != "gemm":
+            self._slot_dst = ptr_array([ws.peer("slots", r) for r in range(P)])
         self._rs_dst = ptr_array([ws.peer("rs_flags", r) + 4 * self.rank for r in range(P)])
         # column chunks of the down GEMM (multiples of its 256-column tile)
         ntiles = (H + 255) // 256
@@ -364,8 +386,38 @@ class P2PExchange:
         if layer.shared is not None and not layer.ep:
             layer.shared.load_rows(layer.xq, layer.xs)
 
+    def _gemm2_scatter(self, layer: "MoELayer", topk_weights, dst) -> None:
+        from . import _lib
+
+        r, P, Tl, k = layer.route, self.world_size, layer.T_local, layer.top_k
+        bp = r.pairs(layer.paired)
+        row0 = 0 if layer.ep else self.rank * Tl * k
+        _lib.call("b2m_gemm2_scatter", layer.inter_q.data_ptr(), layer.inter_st.data_ptr(), r.rows_cap, layer.w.inter,
+                  layer.w.w2.data_ptr(), layer.w.w2_scale.data_ptr(), layer.w.num_experts, layer.H,
+                  r.sorted_ids.data_ptr(), r.expert_ids.data_ptr(), r.ntpp.data_ptr(),
+                  None if bp is None else bp.data_ptr(), layer.numel, topk_weights.reshape(-1).data_ptr(), dst, P,
+                  Tl * k, row0, layer.status.data_ptr(), ops._stream(layer.device))
+
+    def _rs_combine(self, layer: "MoELayer", add, epoch: int) -> None:
+        from . import _lib
+
+        _lib.call("b2m_rs_combine", self.ws.local("recv"), layer.T_local, layer.top_k, layer.H, self.rs_nsrc,
+                  self.rs_flags, self.world_size, epoch, None if add is None else add.data_ptr(),
+                  layer.out_local.data_ptr(), layer.status.data_ptr(), ops._stream(layer.device))
+
     def _down_and_scatter_local(self, layer: "MoELayer", topk_weights, ids, shared_out) -> torch.Tensor:
         from . import _lib
+
+        if self.rs_mode == "gemm":
+            # every owner pointer is the own receive buffer: rows of other owners land in
+            # (and overwrite) own rows -- a timing stand-in that sends nothing
+            self._gemm2_scatter(layer, topk_weights, self._local_recv_dst())
+            layer._event("gemm2_end")
+            layer._event("combine_end")
+            add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
+            layer._event("shared_end")
+            self._rs_combine(layer, add, 0)
+            return layer.out_local
 
         layer.gemm2(topk_weights)
         layer._event("gemm2_end")
@@ -389,6 +441,15 @@ class P2PExchange:
         idsp = None if ids is None else ids.data_ptr()
         emap = None if layer.expert_map is None else layer.expert_map.data_ptr()
         shp = None if shared_out is None else shared_out.data_ptr()
+        if self.rs_mode == "gemm":
+            self._gemm2_scatter(layer, topk_weights, self._recv_dst)
+            layer._event("gemm2_end")
+            _lib.call("b2m_signal", self._rs_dst, P, self.epoch, compute.cuda_stream)
+            layer._event("combine_end")
+            add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
+            layer._event("shared_end")
+            self._rs_combine(layer, add, self.epoch)
+            return layer.out_local
         if self.rs_mode == "sm":
             layer.gemm2(topk_weights)
             layer._event("gemm2_end")
@@ -421,6 +482,19 @@ class P2PExchange:
                   None if add is None else add.data_ptr(), layer.out_local.data_ptr(), layer.status.data_ptr(),
                   compute.cuda_stream)
         return layer.out_local
+
+    def _local_recv_dst(self):
+        from .symm import ptr_array
+
+        if getattr(self, "_local_dst", None) is None:
+            self._local_dst = ptr_array([self.ws.local("recv")] * self.world_size)
+        return self._local_dst
+
+    def extra_launches(self) -> int:
+        """Kernels per forward beyond align, quant(+push), dispatch, GEMM1, GEMM2, combine(+push)."""
+        if self.rs_mode == "gemm":
+            return 0                                   # GEMM2 pushes, the owner combine replaces the combine
+        return 1 + 2 * (len(self.chunk_cols) - 1)      # owner-side reduce; GEMM2/combine per extra chunk
 
     def close(self) -> None:
         if self.ws is not None:
@@ -514,7 +588,7 @@ class MoELayer:
             return 5 + (2 if sh else 0)             # align, quant+dispatch, GEMM1, GEMM2, combine (+shared GEMMs)
         n = 6                                      # align, quant(+push), dispatch, GEMM1, GEMM2, combine(+push)
         if name == "p2p":
-            n += 1 + 2 * (len(self.exchange.chunk_cols) - 1)   # owner-side reduce; GEMM2/push per chunk
+            n += self.exchange.extra_launches()
         if sh:
             n += 3 + (1 if (self.ep and name == "nccl") else 0)
         return n

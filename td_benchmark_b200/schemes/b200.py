@@ -30,10 +30,11 @@ B200_TUNABLES = {
 P2P_TUNABLES = {
     "ag_mode": TunableSpec(str, "auto", "all-gather by SM stores from the quant kernel ('sm'), copy engines ('ce') "
                                         "or by block size ('auto')"),
-    "rs_mode": TunableSpec(str, "sm", "reduce-scatter by SM stores from the combine ('sm') or copy engines ('ce')"),
+    "rs_mode": TunableSpec(str, "sm", "reduce-scatter by SM stores from the combine ('sm'), from the down GEMM's "
+                                      "epilogue ('gemm') or copy engines ('ce')"),
     "rs_chunks": TunableSpec(int, 4, "down-GEMM column chunks of the copy-engine reduce-scatter (1..8)"),
 }
-_CHOICES = {"ag_mode": ("sm", "ce", "auto"), "rs_mode": ("sm", "ce")}
+_CHOICES = {"ag_mode": ("sm", "ce", "auto"), "rs_mode": ("sm", "ce", "gemm")}
 
 
 def _spec(code: str, name: str, parallel: str, comm: str) -> SchemeSpec:

@@ -330,3 +330,59 @@ def test_combine_bit_exact(T, k, H, shared):
         acc = (acc + sh.float().numpy()).astype(np.float32)
     exp = ofp8.f32_to_bf16_bits(acc)
     assert np.array_equal(out.view(torch.int16).cpu().numpy().astype(np.uint16), exp)
+
+
+@pytest.mark.parametrize("world,src,paired", [(2, 1, False), (4, 0, False), (4, 3, True)])
+def test_gemm2_scatter_and_rs_combine(world, src, paired):
+    """Down GEMM storing into owner buffers (owners emulated by buffers on this GPU): every
+    pair row lands bit-identical to b2m_gemm2's row at owner p // ppo, row row0 + p - q*ppo;
+    the owner combine equals a sequential fp32 sum over sources and top-k rows."""
+    from td_benchmark_b200 import _lib
+    from td_benchmark_b200.symm import ptr_array
+
+    T, H, I, E, k = 256, 512, 256, 4, 2
+    x, w1q, w1s, w2q, w2s, ids, wts = _gemm_problem(T, H, I, E, k, 77 + world, False)
+    xq, xs = ops.quant_g128(x.to(DEV))
+    w1i, w1is = ops.w1_interleave(w1q.to(DEV), w1s.to(DEV))
+    pp = torch.empty(T * k, dtype=torch.int32, device=DEV)
+    bp = torch.empty(1 + 2 * ops.align_sizes(T * k, E, 128)[1], dtype=torch.int32, device=DEV) if paired else None
+    sorted_ids, eids, ntpp = ops.moe_align_block_size(ids.to(DEV), 128, E, pair_pos=pp, block_pairs=bp)
+    rows_cap = eids.numel() * 128
+    a_sorted = torch.empty((rows_cap, H), dtype=torch.float8_e4m3fn, device=DEV)
+    a_st = torch.empty((H // 128, rows_cap), dtype=torch.float32, device=DEV)
+    ops.dispatch_rows(xq, xs, pp, k, a_sorted, a_st)
+    status = ops.new_status(DEV)
+    hq, hst = ops.gemm1(a_sorted, a_st, w1i, w1is, eids, ntpp, status=status, block_pairs=bp)
+    w2d, w2sd, wd = w2q.to(DEV), w2s.to(DEV), wts.reshape(-1).to(DEV).contiguous()
+    staged = ops.gemm2(hq, hst, w2d, w2sd, sorted_ids, eids, ntpp, T * k, wd, status=status, block_pairs=bp)
+    ppo = T * k // world
+    recv = [torch.zeros((world * ppo, H), dtype=torch.bfloat16, device=DEV) for _ in range(world)]
+    _lib.call("b2m_gemm2_scatter", hq.data_ptr(), hst.data_ptr(), rows_cap, I, w2d.data_ptr(), w2sd.data_ptr(), E, H,
+              sorted_ids.data_ptr(), eids.data_ptr(), ntpp.data_ptr(), None if bp is None else bp.data_ptr(), T * k,
+              wd.data_ptr(), ptr_array([r.data_ptr() for r in recv]), world, ppo, src * ppo, status.data_ptr(),
+              torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ops.check_status(status)
+    for q in range(world):
+        assert torch.equal(recv[q][src * ppo:(src + 1) * ppo], staged[q * ppo:(q + 1) * ppo])
+        assert not recv[q][:src * ppo].any() and not recv[q][(src + 1) * ppo:].any()
+    # owner combine over `world` sources of top-k rows (+ an added row), flags already at the epoch
+    q = world - 1
+    for s in range(world):                        # fill the other sources' blocks with distinct rows
+        if s != src:
+            recv[q][s * ppo:(s + 1) * ppo] = (staged[q * ppo:(q + 1) * ppo].float() * (0.5 + s)).to(torch.bfloat16)
+    rows = T // world
+    add = _bf16((rows, H), 5)
+    flags = torch.full((world,), 3, dtype=torch.int32, device=DEV)
+    out = torch.empty((rows, H), dtype=torch.bfloat16, device=DEV)
+    _lib.call("b2m_rs_combine", recv[q].data_ptr(), rows, k, H, world, flags.data_ptr(), world, 3,
+              add.to(DEV).data_ptr(), out.data_ptr(), status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ops.check_status(status)
+    r = recv[q].float().cpu().numpy().reshape(world, rows, k, H)
+    acc = np.zeros((rows, H), dtype=np.float32)
+    for s in range(world):
+        for j in range(k):
+            acc = acc + r[s, :, j]
+    acc = acc + add.float().numpy()
+    assert torch.equal(out.cpu(), torch.from_numpy(acc).to(torch.bfloat16))

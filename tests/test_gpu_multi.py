@@ -34,7 +34,11 @@ def _port() -> int:
     ("d3", "mixtral", 512, ["--ag-mode", "ce", "--rs-mode", "ce", "--rs-chunks", "2"]),
     ("d4", "dsv3", 512, ["--ag-mode", "ce", "--rs-mode", "ce", "--rs-chunks", "1"]),
     ("d3", "mixtral", 512, ["--ag-mode", "ce"]),
-])
+    # down GEMM storing straight into the owners' receive buffers
+    ("d3", "mixtral", 512, ["--rs-mode", "gemm"]),
+    ("d4", "dsv3", 1024, ["--zipf", "--rs-mode", "gemm"]),
+    ("d3", "qwen3", 256, ["--rs-mode", "gemm"]),
+], ids=lambda v: "-".join(a.strip("-") for a in v) if isinstance(v, list) else str(v))
 def test_multi_gpu_scheme_matches_golden(scheme, preset, tokens, extra):
     n = min(_gpus(), 4)
     if n < 2:
