@@ -293,7 +293,7 @@ def main() -> int:
     ap.add_argument("--rs-mode", default="sm", choices=["sm", "gemm", "ce"],
                     help="fused reduce-scatter: SM stores from the combine (default), from the down GEMM's epilogue, "
                          "or copy-engine push")
-    ap.add_argument("--ag-mode", default="auto", choices=["auto", "sm", "ce"],
+    ap.add_argument("--ag-mode", default="auto", choices=["auto", "sm", "ce", "push"],
                     help="fused all-gather: SM stores from the quant kernel, copy-engine copies, or by block size")
     ap.add_argument("--chunks", type=int, default=4, help="down-GEMM column chunks of the copy-engine push")
     ap.add_argument("--ce-streams", type=int, default=2, help="side streams carrying the copy-engine push")

@@ -110,6 +110,15 @@ int b2m_align(const int32_t* topk_ids, int64_t numel, int32_t num_experts, int32
               int64_t expert_ids_cap, int32_t* num_tokens_post_padded, int32_t* pair_pos, int32_t* block_pairs,
               void* stream);
 
+/* M-block visiting order for b2m_gemm1_wait: block b (of *num_tokens_post_padded / 128)
+ * gets key max over its rows of (source - rank) mod world (the step at which
+ * b2m_quant_dispatch_push delivers that source here), source of pair p =
+ * (p / top_k) / tokens_per_src; order lists the blocks by key, ascending block index
+ * within a key.  order_cap <= 16384.  One CTA. */
+int b2m_block_order(const int32_t* sorted_token_ids, const int32_t* num_tokens_post_padded, int64_t numel,
+                    int32_t top_k, int64_t tokens_per_src, int32_t world, int32_t rank, int32_t* order,
+                    int64_t order_cap, int32_t* dev_status, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Gate/up weight layout for K3.  The reference stores w1 as [E, 2I, H] with all
  * gate rows before all up rows (moe_bench/schemes/runtime.py:154-159).  K3 wants,
@@ -146,6 +155,20 @@ int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, in
               const float* w1_scale, int32_t num_experts, int32_t inter, const int32_t* expert_ids,
               const int32_t* num_tokens_post_padded, const int32_t* block_pairs, void* out_q, float* out_scale_t,
               int32_t* dev_status, void* stream);
+
+/* b2m_gemm1 for a tensor-parallel layer whose A rows are stored by the source ranks
+ * (b2m_quant_dispatch_push) while it runs, so the all-gather overlaps the GEMM: M blocks
+ * are visited in block_order (b2m_block_order: own rows first), and before a block's loads
+ * the producer waits until src_flags[s] >= epoch for every source s among its rows
+ * (source of pair p = (p / top_k) / tokens_per_src, from sorted_token_ids; pads = numel).
+ * Waits are bounded (timeout -> B2M_STATUS_TIMEOUT_PEER in dev_status).  No paired-CTA
+ * variant.  Replaces the gate/up GEMM after the all-gather of overlap_forward.py:494-552. */
+int b2m_gemm1_wait(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden, const void* w1,
+                   const float* w1_scale, int32_t num_experts, int32_t inter, const int32_t* expert_ids,
+                   const int32_t* num_tokens_post_padded, const int32_t* block_order,
+                   const int32_t* sorted_token_ids, int64_t numel, int32_t top_k, int64_t tokens_per_src,
+                   const uint32_t* src_flags, uint32_t epoch, void* out_q, float* out_scale_t, int32_t* dev_status,
+                   void* stream);
 
 /* ---------------------------------------------------------------------------
  * K4  down grouped GEMM with the routed top-k weight in the epilogue.
@@ -244,6 +267,20 @@ int b2m_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int
 int b2m_quant_push_noalloc(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world,
                            void* const* q_dst, void* const* s_dst, int64_t row0, uint32_t* const* flag_dst,
                            uint32_t epoch, void* stream);
+
+/* All-gather straight into every rank's expert-sorted operand (tensor parallel: the
+ * alignment, hence pair_pos [T*top_k], is identical on every rank; replaces the FP8
+ * all_gather_into_tensor of overlap_forward.py:494-505 and the row dispatch): quantise
+ * x [rows, hidden] (this rank's tokens token0 .. token0+rows-1) exactly as b2m_quant_g128
+ * and store each token's codes at row pair_pos[t*top_k + j] of a_dst[d] (e4m3
+ * [rows_cap, hidden]) and its scales at s_dst[d][kb * rows_cap + pos] for every j with
+ * pos >= 0 and every rank d: the own rank first, then rank-1, rank-2, ...  When the grid
+ * is done with destination d, *flag_dst[d] = epoch.  counters: world int32, zero before
+ * the first call (calls leave them zero). */
+int b2m_quant_dispatch_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, const int32_t* pair_pos,
+                            int32_t top_k, int64_t token0, int32_t world, int32_t rank, void* const* a_dst,
+                            void* const* s_dst, int64_t rows_cap, uint32_t* const* flag_dst, uint32_t epoch,
+                            int32_t* counters, void* stream);
 
 /* b2m_dispatch_rows on the gather buffer, reading source rank s's rows
  * (tokens [s*T/world, (s+1)*T/world)) only once flags[s] >= epoch (own rank first).

@@ -24,8 +24,11 @@ SIGNATURES: dict[str, list] = {
     "b2m_quant_dispatch": [_p, _i64, _i64, _i64, _p, _i32, _p, _p, _i64, _p, _p, _i64, _p],
     "b2m_dispatch_rows": [_p, _p, _i64, _i64, _p, _i32, _p, _p, _i64, _p],
     "b2m_align": [_p, _i64, _i32, _i32, _p, _p, _i64, _p, _i64, _p, _p, _p, _p],
+    "b2m_block_order": [_p, _p, _i64, _i32, _i64, _i32, _i32, _p, _i64, _p, _p],
     "b2m_w1_interleave": [_p, _p, _i32, _i32, _i64, _p, _p, _p],
     "b2m_gemm1": [_p, _p, _i64, _i64, _p, _p, _i32, _i32, _p, _p, _p, _p, _p, _p, _p],
+    "b2m_gemm1_wait": [_p, _p, _i64, _i64, _p, _p, _i32, _i32, _p, _p, _p, _p, _i64, _i32, _i64, _p, _c.c_uint32, _p,
+                       _p, _p, _p],
     "b2m_gemm2": [_p, _p, _i64, _i32, _p, _p, _i32, _i64, _p, _p, _p, _p, _i64, _p, _p, _i64, _i64, _i32, _p, _p],
     "b2m_gemm2_scatter": [_p, _p, _i64, _i32, _p, _p, _i32, _i64, _p, _p, _p, _p, _i64, _p, _p, _i32, _i64, _i64, _p,
                           _p],
@@ -39,6 +42,8 @@ SIGNATURES: dict[str, list] = {
     "b2m_ipc_close": [_p],
     "b2m_quant_push": [_p, _i64, _i64, _i64, _i32, _p, _p, _i64, _p, _c.c_uint32, _p, _p],
     "b2m_quant_push_noalloc": [_p, _i64, _i64, _i64, _i32, _p, _p, _i64, _p, _c.c_uint32, _p],
+    "b2m_quant_dispatch_push": [_p, _i64, _i64, _i64, _p, _i32, _i64, _i32, _i32, _p, _p, _i64, _p, _c.c_uint32, _p,
+                                _p],
     "b2m_dispatch_rows_wait": [_p, _p, _i64, _i64, _p, _i32, _p, _p, _i64, _p, _i32, _i32, _c.c_uint32, _p, _p],
     "b2m_combine_push": [_p, _i64, _i32, _i64, _i64, _i64, _p, _p, _p, _i32, _i32, _p, _p, _c.c_uint32, _p, _i32,
                          _p],

@@ -27,7 +27,8 @@ constexpr int kAlignWarps = 32;  // per CTA
 constexpr int kAlignThreads = kAlignWarps * 32;
 constexpr int kAlignShared = kAlignWarps + 5;  // int32 arrays of E entries in shared memory
 constexpr int kMaxExperts = 1024;
-constexpr int kBatch = 8;  // ids loaded per lane before use (keeps 8 loads in flight per warp)
+constexpr int kBatch = 8;
+constexpr int BM_ORDER = 128;  // M block of the grouped GEMMs  // ids loaded per lane before use (keeps 8 loads in flight per warp)
 
 __global__ void __cluster_dims__(kAlignCtas, 1, 1) __launch_bounds__(kAlignThreads, 1)
     align_kernel(const int32_t* __restrict__ topk_ids, int64_t numel, int32_t num_experts, int32_t bs,
@@ -198,6 +199,64 @@ __global__ void __cluster_dims__(kAlignCtas, 1, 1) __launch_bounds__(kAlignThrea
   if (gthread == 0) *ntpp_out = total;
 }
 
+// M-block visiting order of a gate/up GEMM whose rows arrive per source rank
+// (b2m_quant_dispatch_push, which serves the own rank first, then rank-1, rank-2, ...; so
+// source s reaches this rank at step (s - rank) mod world): block b's key is the latest
+// step among its rows' sources, the source of pair p being (p / top_k) / tokens_per_src;
+// blocks are listed by key, ascending block index within a key.  One CTA: a warp per block
+// computes the key, then one stable compaction pass per key.
+constexpr int kOrderThreads = 1024;
+constexpr int kOrderMaxBlocks = 16384;
+
+__global__ void __launch_bounds__(kOrderThreads, 1)
+    block_order_kernel(const int32_t* __restrict__ sorted_ids, const int32_t* __restrict__ ntpp, int64_t numel,
+                       int top_k, int64_t tokens_per_src, int world, int rank, int32_t* __restrict__ order,
+                       int64_t order_cap, int32_t* status) {
+  __shared__ uint8_t s_key[kOrderMaxBlocks];
+  __shared__ int32_t s_warp[kOrderThreads / 32];
+  __shared__ int32_t s_base;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  int64_t nblk = __ldg(ntpp) / BM_ORDER;
+  if (nblk < 0 || nblk > order_cap || nblk > kOrderMaxBlocks) {
+    if (tid == 0) set_status(status, B2M_STATUS_BAD_ROUTING);
+    nblk = 0;
+  }
+  for (int64_t b = warp; b < nblk; b += kOrderThreads / 32) {
+    int hi = -1;
+    for (int i = lane; i < BM_ORDER; i += 32) {
+      const int32_t id = __ldg(sorted_ids + b * BM_ORDER + i);
+      if (id >= 0 && id < numel) {
+        const int src = static_cast<int>((id / top_k) / tokens_per_src);
+        hi = max(hi, ((src - rank) % world + world) % world);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, off));
+    if (lane == 0) s_key[b] = static_cast<uint8_t>(hi < 0 ? 0 : hi);
+  }
+  if (tid == 0) s_base = 0;
+  __syncthreads();
+  for (int key = 0; key < world; ++key) {
+    for (int64_t b0 = 0; b0 < nblk; b0 += kOrderThreads) {
+      const int64_t b = b0 + tid;
+      const int flag = (b < nblk && s_key[b] == key) ? 1 : 0;
+      const uint32_t bal = __ballot_sync(0xffffffffu, flag);
+      if (lane == 0) s_warp[warp] = __popc(bal);
+      __syncthreads();
+      int before = 0, total = 0;
+      for (int w = 0; w < kOrderThreads / 32; ++w) {
+        const int c = s_warp[w];
+        before += w < warp ? c : 0;
+        total += c;
+      }
+      if (flag) order[s_base + before + __popc(bal & ((1u << lane) - 1u))] = static_cast<int32_t>(b);
+      __syncthreads();
+      if (tid == 0) s_base += total;
+      __syncthreads();
+    }
+  }
+}
+
 }  // namespace
 }  // namespace b2m
 
@@ -231,4 +290,20 @@ extern "C" int b2m_align(const int32_t* topk_ids, int64_t numel, int32_t num_exp
       topk_ids, numel, num_experts, block_size, expert_map, sorted_token_ids, sorted_cap, expert_ids,
       expert_ids_cap, num_tokens_post_padded, pair_pos, block_pairs);
   return check_cuda(cudaGetLastError(), "align launch");
+}
+
+extern "C" int b2m_block_order(const int32_t* sorted_token_ids, const int32_t* num_tokens_post_padded, int64_t numel,
+                               int32_t top_k, int64_t tokens_per_src, int32_t world, int32_t rank, int32_t* order,
+                               int64_t order_cap, int32_t* dev_status, void* stream) {
+  using namespace b2m;
+  B2M_TRY(require_sm100(nullptr));
+  if (world < 1 || world > 255 || rank < 0 || rank >= world || top_k < 1 || tokens_per_src < 1 || numel < 0 ||
+      order_cap < 0 || order_cap > kOrderMaxBlocks)
+    return fail(B2M_ERR_ARG, "block_order: bad world/rank/top_k/tokens_per_src or order_cap > %d", kOrderMaxBlocks);
+  if (!sorted_token_ids || !num_tokens_post_padded || (order_cap > 0 && !order))
+    return fail(B2M_ERR_ARG, "block_order: null pointer");
+  block_order_kernel<<<1, kOrderThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      sorted_token_ids, num_tokens_post_padded, numel, top_k, tokens_per_src, world, rank, order, order_cap,
+      dev_status);
+  return check_cuda(cudaGetLastError(), "block_order launch");
 }

@@ -108,6 +108,14 @@ struct GemmParams {
   int64_t rs_pairs_per_owner;
   int64_t rs_row0;
   int32_t rs_world;
+  // Gate/up GEMM whose A rows are stored by the source ranks (b2m_quant_dispatch_push):
+  // before loading a block, the producer waits until src_flags[s] >= src_epoch for every
+  // source s among the block's rows (token of pair p = p / top_k, source = token /
+  // tokens_per_src).  src_flags == nullptr: no waits.  block_order: M-block visiting order.
+  const uint32_t* src_flags;
+  uint32_t src_epoch;
+  int64_t tokens_per_src;
+  const int32_t* block_order;
 };
 
 // silu(x) = x * sigmoid(x).  The gate/up intermediate is requantised to e4m3 right
@@ -120,6 +128,7 @@ struct TileWalk {
   int num_mb;
   int num_nt;
   int nt_begin;
+  const int32_t* order;  // M-block visiting order (nullptr: 0, 1, 2, ...)
 };
 
 // Tile t -> (M block, N tile): bands of GROUP_M consecutive M blocks (experts are
@@ -133,6 +142,47 @@ __device__ __forceinline__ void tile_coords(int64_t t, const TileWalk& tw, int& 
   const int64_t in_band = t - band * per_band;
   mb = first + static_cast<int>(in_band % rows);
   nt = tw.nt_begin + static_cast<int>(in_band / rows);
+  if (tw.order) mb = __ldg(tw.order + mb);
+}
+
+// Producer warp, before the loads of block mb: the lowest and highest source rank among the
+// block's rows (pairs ascend inside an expert segment, so the rows of one source are
+// contiguous), then lane 0 waits (bounded) for each of those sources' flags not seen yet and
+// orders the copies that follow after the peers' stores (acquire, then a proxy fence: the
+// operand and scale copies are async-proxy reads of memory the peers wrote with ordinary
+// stores).  Returns false after a timeout (status recorded, the CTA aborts).
+__device__ __forceinline__ bool wait_block_sources(const GemmParams& p, int mb, uint32_t& ready, int lane,
+                                                   volatile int* abort) {
+  int lo = 1 << 30, hi = -1;
+#pragma unroll
+  for (int i = 0; i < BM / 32; ++i) {
+    const int32_t id = __ldg(p.sorted_ids + static_cast<int64_t>(mb) * BM + i * 32 + lane);
+    if (id >= 0 && id < p.numel) {
+      const int src = static_cast<int>((id / p.top_k) / p.tokens_per_src);
+      lo = min(lo, src);
+      hi = max(hi, src);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, off));
+    hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, off));
+  }
+  int ok = 1;
+  if (lane == 0) {
+    for (int src = lo; src <= hi && ok; ++src) {
+      if (src < 0 || src >= 32 || (ready >> src) & 1u) continue;
+      if (!wait_flag_geq(p.src_flags + src, p.src_epoch, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_PEER)) {
+        ok = 0;
+        *abort = 1;
+      } else {
+        ready |= 1u << src;
+      }
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
+  ready = __shfl_sync(0xffffffffu, ready, 0);
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
 // ---------------------------------------------------------------- warp 0: B (+A for the down GEMM)
@@ -143,6 +193,7 @@ __device__ __forceinline__ void stage_producer(const CUtensorMap* map_a, const C
   volatile int* abort = &C->abort;
   uint32_t kbg = 0;
   bool alive = true;
+  uint32_t ready = 0;  // sources whose rows have arrived (gate/up GEMM fed by peers)
   const uint32_t tx = A_BYTES + B_BYTES;
   for (int64_t tile = blockIdx.x; tile < tw.num_tiles && alive; tile += gridDim.x) {
     int mb, nt;
@@ -154,6 +205,10 @@ __device__ __forceinline__ void stage_producer(const CUtensorMap* map_a, const C
     const float* bs0 = p.b_scale + (static_cast<int64_t>(e) * p.n_blocks + blk0) * p.num_kb;
     const float* bs1 = p.b_scale + (static_cast<int64_t>(e) * p.n_blocks + blk1) * p.num_kb;
     const int b_row = e * p.n_rows + nt * BN;
+    if (p.src_flags && !wait_block_sources(p, mb, ready, lane, abort)) {
+      alive = false;
+      break;
+    }
     float pre0 = 0.0f, pre1 = 0.0f;
     for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
       if ((kb & 31) == 0) {  // lane j holds the scales of K block kb + j
@@ -423,7 +478,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0 && blockIdx.x == 0) set_status(p.status, B2M_STATUS_BAD_ROUTING);
     num_mb = 0;
   }
-  const TileWalk tw{static_cast<int64_t>(num_mb) * p.num_nt, num_mb > 0 ? num_mb : 1, p.num_nt, p.nt_begin};
+  const TileWalk tw{static_cast<int64_t>(num_mb) * p.num_nt, num_mb > 0 ? num_mb : 1, p.num_nt, p.nt_begin,
+                    p.block_order};
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -867,12 +923,23 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmPar
 }  // namespace
 }  // namespace b2m
 
-extern "C" int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden,
-                         const void* w1, const float* w1_scale, int32_t num_experts, int32_t inter,
-                         const int32_t* expert_ids, const int32_t* num_tokens_post_padded,
-                         const int32_t* block_pairs, void* out_q, float* out_scale_t, int32_t* dev_status,
-                         void* stream) {
-  using namespace b2m;
+namespace b2m {
+namespace {
+
+struct SourceWait {
+  const int32_t* block_order;
+  const int32_t* sorted_ids;
+  int64_t numel;
+  int32_t top_k;
+  int64_t tokens_per_src;
+  const uint32_t* flags;
+  uint32_t epoch;
+};
+
+int gemm1_impl(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden, const void* w1,
+               const float* w1_scale, int32_t num_experts, int32_t inter, const int32_t* expert_ids,
+               const int32_t* num_tokens_post_padded, const int32_t* block_pairs, void* out_q, float* out_scale_t,
+               const SourceWait* sw, int32_t* dev_status, void* stream) {
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
   if (hidden <= 0 || hidden % 128 || inter <= 0 || inter % 128 || num_experts <= 0 || rows_cap <= 0 ||
@@ -907,8 +974,44 @@ extern "C" int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t r
   p.hidden = hidden;
   p.status = dev_status;
   p.timeout_ns = timeout_ns();
+  if (sw) {
+    if (block_pairs) return fail(B2M_ERR_UNSUPPORTED, "gemm1_wait: no paired-CTA variant");
+    if (!sw->block_order || !sw->sorted_ids || !sw->flags || sw->top_k < 1 || sw->tokens_per_src < 1 ||
+        sw->numel < 0 || sw->numel >= INT32_MAX)
+      return fail(B2M_ERR_ARG, "gemm1_wait: block_order, sorted_ids and flags are required; top_k, tokens_per_src >= 1");
+    p.block_order = sw->block_order;
+    p.sorted_ids = sw->sorted_ids;
+    p.numel = static_cast<int32_t>(sw->numel);
+    p.top_k = sw->top_k;
+    p.tokens_per_src = sw->tokens_per_src;
+    p.src_flags = sw->flags;
+    p.src_epoch = sw->epoch;
+  }
   if (block_pairs) return launch_gemm_pair<true>(ma, mb, p, block_pairs, num_sms, static_cast<cudaStream_t>(stream));
   return launch_gemm<true>(ma, mb, p, num_sms, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+}  // namespace b2m
+
+extern "C" int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden,
+                         const void* w1, const float* w1_scale, int32_t num_experts, int32_t inter,
+                         const int32_t* expert_ids, const int32_t* num_tokens_post_padded,
+                         const int32_t* block_pairs, void* out_q, float* out_scale_t, int32_t* dev_status,
+                         void* stream) {
+  return b2m::gemm1_impl(a_sorted, a_scale_t, rows_cap, hidden, w1, w1_scale, num_experts, inter, expert_ids,
+                         num_tokens_post_padded, block_pairs, out_q, out_scale_t, nullptr, dev_status, stream);
+}
+
+extern "C" int b2m_gemm1_wait(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden,
+                              const void* w1, const float* w1_scale, int32_t num_experts, int32_t inter,
+                              const int32_t* expert_ids, const int32_t* num_tokens_post_padded,
+                              const int32_t* block_order, const int32_t* sorted_token_ids, int64_t numel,
+                              int32_t top_k, int64_t tokens_per_src, const uint32_t* src_flags, uint32_t epoch,
+                              void* out_q, float* out_scale_t, int32_t* dev_status, void* stream) {
+  const b2m::SourceWait sw{block_order, sorted_token_ids, numel, top_k, tokens_per_src, src_flags, epoch};
+  return b2m::gemm1_impl(a_sorted, a_scale_t, rows_cap, hidden, w1, w1_scale, num_experts, inter, expert_ids,
+                         num_tokens_post_padded, nullptr, out_q, out_scale_t, &sw, dev_status, stream);
 }
 
 namespace b2m {

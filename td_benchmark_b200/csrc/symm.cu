@@ -75,7 +75,8 @@ __device__ __forceinline__ void publish_when_grid_done(int32_t* counter, const F
 // own rank so that the ranks do not all hit the same peer first.
 __global__ void __launch_bounds__(kThreads)
     quant_push_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t rows, int64_t gpr, int world,
-                      PeerPtrs qdst, PeerPtrs sdst, int64_t row0, FlagPtrs flags, uint32_t epoch, int32_t* counter) {
+                      const __grid_constant__ PeerPtrs qdst, const __grid_constant__ PeerPtrs sdst, int64_t row0,
+                      const __grid_constant__ FlagPtrs flags, uint32_t epoch, int32_t* counter) {
   const int lane = threadIdx.x & 31;
   const int sub = lane >> 3;  // group of the warp's four
   const int gl = lane & 7;    // 16-value slice of that group
@@ -117,6 +118,79 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
   publish_when_grid_done(counter, flags, world, epoch);
+}
+
+// ---------------------------------------------------------------- all-gather into the peers' sorted operand
+// Tensor parallel only: every rank aligns the same topk_ids, so pair_pos (sorted position of
+// each (token, j) pair) is the same on every rank and a source can store its quantised rows
+// straight into each destination's expert-sorted A operand (top_k copies per token) and the
+// K-block-major A scales -- no gather buffer, no dispatch kernel.  Destination-major: the
+// grid serves the own rank first, then rank-1, rank-2, ...; a CTA that finished its share of
+// a destination counts itself on that destination's counter and moves on, and the last CTA
+// publishes the flag.  Destination d thus receives source d+1 first, then d+2, ..., the order
+// in which its gate/up GEMM visits the blocks (b2m_block_order).  Quantisation is that of
+// b2m_quant_g128 (recomputed per destination from x, which stays in L2).
+__global__ void __launch_bounds__(kThreads)
+    quant_dispatch_push_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t rows, int64_t gpr,
+                               const int32_t* __restrict__ pair_pos, int top_k, int64_t token0, int world, int rank,
+                               const __grid_constant__ PeerPtrs adst, const __grid_constant__ PeerPtrs sdst,
+                               int64_t rows_cap, const __grid_constant__ FlagPtrs flags, uint32_t epoch,
+                               int32_t* counters) {
+  const int lane = threadIdx.x & 31;
+  const int sub = lane >> 3;
+  const int gl = lane & 7;
+  const int64_t cols = gpr * 128;
+  const int64_t groups = rows * gpr;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
+  for (int i = 0; i < world; ++i) {
+    const int d = (rank - i + world) % world;
+    uint8_t* a = static_cast<uint8_t*>(adst.p[d]);
+    float* sc = static_cast<float*>(sdst.p[d]);
+    for (int64_t base = warp * 4; base < groups; base += nwarps * 4) {
+      const int64_t g = base + sub;
+      uint4 raw0 = make_uint4(0, 0, 0, 0), raw1 = raw0;
+      int64_t row = 0, gi = 0;
+      if (g < groups) {
+        row = g / gpr;
+        gi = g - row * gpr;
+        const uint4* src = reinterpret_cast<const uint4*>(x + row * ldx + gi * 128 + gl * 16);
+        raw0 = __ldg(src);
+        raw1 = __ldg(src + 1);
+      }
+      float f0[8], f1[8];
+      bf16x8_to_f32(raw0, f0);
+      bf16x8_to_f32(raw1, f1);
+      float amax = 0.0f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) amax = fmaxf(amax, fmaxf(fabsf(f0[u]), fabsf(f1[u])));
+#pragma unroll
+      for (int off = 4; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      const float s = fmaxf(amax / 448.0f, 1e-12f);
+      if (g < groups) {
+        const uint2 q0 = quant8(f0, s);
+        const uint2 q1 = quant8(f1, s);
+        const uint4 q = make_uint4(q0.x, q0.y, q1.x, q1.y);
+        const int32_t* pp = pair_pos + (token0 + row) * top_k;
+        for (int j = 0; j < top_k; ++j) {
+          const int64_t pos = __ldg(pp + j);
+          if (pos < 0) continue;
+          *reinterpret_cast<uint4*>(a + pos * cols + gi * 128 + gl * 16) = q;
+          if (gl == 0) sc[gi * rows_cap + pos] = s;
+        }
+      }
+    }
+    __threadfence_system();  // this thread's stores to destination d are visible system-wide
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int prev = atomicAdd(counters + d, 1);
+      if (prev == static_cast<int>(gridDim.x) - 1) {  // the grid is done with destination d
+        fence_sys();
+        st_release_sys(flags.p[d], epoch);
+        atomicExch(counters + d, 0);
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------- dispatch with arrival waits
@@ -170,7 +244,8 @@ __global__ void __launch_bounds__(kThreads)
     combine_push_kernel(const __nv_bfloat16* __restrict__ staged, int64_t tokens, int top_k, int64_t hidden,
                         int64_t col0, int64_t col1, const int32_t* __restrict__ topk_ids,
                         const int32_t* __restrict__ expert_map, const __nv_bfloat16* __restrict__ shared, int world,
-                        int rank, PeerPtrs slots, FlagPtrs flags, uint32_t epoch, int32_t* counter) {
+                        int rank, const __grid_constant__ PeerPtrs slots, const __grid_constant__ FlagPtrs flags,
+                        uint32_t epoch, int32_t* counter) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
@@ -417,6 +492,34 @@ int b2m_quant_push_noalloc(const void* x, int64_t rows, int64_t hidden, int64_t 
                                      static_cast<cudaStream_t>(stream)),
                      "quant_push_noalloc: clear scratch"));
   return b2m_quant_push(x, rows, hidden, ldx, world, q_dst, s_dst, row0, flag_dst, epoch, counter, stream);
+}
+
+int b2m_quant_dispatch_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, const int32_t* pair_pos,
+                            int32_t top_k, int64_t token0, int32_t world, int32_t rank, void* const* a_dst,
+                            void* const* s_dst, int64_t rows_cap, uint32_t* const* flag_dst, uint32_t epoch,
+                            int32_t* counters, void* stream) {
+  using namespace b2m;
+  int num_sms = 0;
+  B2M_TRY(require_sm100(&num_sms));
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world)
+    return fail(B2M_ERR_ARG, "quant_dispatch_push: world=%d / rank=%d outside [1, 8]", world, rank);
+  if (rows <= 0 || hidden <= 0 || hidden % 128 || ldx < hidden || ldx % 8 || top_k < 1 || token0 < 0 ||
+      rows_cap <= 0 || !x || !aligned16(x) || !pair_pos || !a_dst || !s_dst || !flag_dst || !counters)
+    return fail(B2M_ERR_ARG, "quant_dispatch_push: bad shape/pointers (hidden %% 128 == 0, 16-byte rows)");
+  PeerPtrs a{}, sc{};
+  FlagPtrs f{};
+  for (int r = 0; r < world; ++r) {
+    if (!a_dst[r] || !s_dst[r] || !flag_dst[r] || !aligned16(a_dst[r]))
+      return fail(B2M_ERR_ARG, "quant_dispatch_push: bad peer pointer %d", r);
+    a.p[r] = a_dst[r];
+    sc.p[r] = s_dst[r];
+    f.p[r] = flag_dst[r];
+  }
+  const int64_t groups = rows * (hidden / 128);
+  quant_dispatch_push_kernel<<<grid_for(groups * 8, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, rows, hidden / 128, pair_pos, top_k, token0, world, rank, a, sc,
+      rows_cap, f, epoch, counters);
+  return check_cuda(cudaGetLastError(), "quant_dispatch_push launch");
 }
 
 int b2m_dispatch_rows_wait(const void* xq, const float* xs, int64_t tokens, int64_t hidden, const int32_t* pair_pos,

@@ -206,6 +206,17 @@ class P2PExchange:
            copy engines copy that contiguous block (codes, then scales) to each peer on
            side streams, and ``b2m_signal`` (a stream memory write, no SM) publishes each
            peer's flag right after its copies.
+      "push" -- tensor parallel only: ``b2m_quant_dispatch_push`` stores each token's rows
+           straight into every rank's expert-sorted operand (every rank aligns the same
+           routing, so the sorted positions agree), own rank first, then rank-1, rank-2, ...
+           with a flag per destination; the gate/up GEMM (``b2m_gemm1_wait``) visits its M
+           blocks own-rows-first (``b2m_block_order``) and waits per block for the flags of
+           the sources the block holds.  No gather buffer and no dispatch kernel; top_k
+           copies of each token cross NVLink.  As built the push is a kernel of its own
+           that runs to completion before the GEMM on the same GPU, so only the peers'
+           skew is hidden while the push itself (k copies, destination by destination)
+           costs more than the plain push + dispatch: Mixtral TP2 1084 vs 995 us.  Its
+           payoff needs the pushes issued from inside the GEMM (its idle warps).
       "auto" (default) -- "ce" when a rank's block of codes is at least
            ``AG_CE_MIN_BYTES``, else "sm".  On 8 B200s the copy engines won for the
            DeepSeek-V3 EP shape (7.3 MB per peer: 1648 vs 1683 us per layer) and lost for
@@ -242,8 +253,8 @@ class P2PExchange:
 
     def __init__(self, group=None, chunks: int = 4, rs_mode: str = "sm", ce_streams: int = 2, ag_mode: str = "auto"):
         import torch.distributed as dist
-        if rs_mode not in ("ce", "sm", "gemm") or ag_mode not in ("ce", "sm", "auto"):
-            raise ValueError(f"rs_mode must be 'gemm', 'ce' or 'sm' and ag_mode 'ce', 'sm' or 'auto', got "
+        if rs_mode not in ("ce", "sm", "gemm") or ag_mode not in ("ce", "sm", "auto", "push"):
+            raise ValueError(f"rs_mode must be 'gemm', 'ce' or 'sm' and ag_mode 'push', 'ce', 'sm' or 'auto', got "
                              f"{rs_mode!r}, {ag_mode!r}")
         self.ag_mode = ag_mode
         self.dist = dist
@@ -267,6 +278,8 @@ class P2PExchange:
             self.ag_mode = "ce" if Tl * H >= self.AG_CE_MIN_BYTES else "sm"
         if self.rs_mode == "gemm" and layer.shared is not None and not layer.ep:
             raise ValueError("rs_mode='gemm' cannot add a tensor-parallel shared expert; use 'sm'")
+        if self.ag_mode == "push" and (layer.ep or layer.shared is not None):
+            raise ValueError("ag_mode='push' needs a tensor-parallel layer without a shared expert")
         # receive rows of the scattered reduce-scatter: one block of T/P*k rows per source (TP)
         # or a single block (EP: every pair has exactly one writer)
         self.rs_nsrc = (1 if layer.ep else P)
@@ -276,8 +289,22 @@ class P2PExchange:
             layout["recv"] = self.rs_nsrc * Tl * layer.top_k * H * 2
         else:
             layout["slots"] = T * H * 2
+        rows_cap = layer.route.rows_cap
+        if self.ag_mode == "push":
+            layout.update({"a_sorted": rows_cap * H, "as_t": (H // 128) * rows_cap * 4, "push_counters": 4 * P})
         self.ws = SymmetricWorkspace(layout, self.group, layer.device)
         ws = self.ws
+        if self.ag_mode == "push":
+            # the expert-sorted operand and its scales are written by every source rank
+            layer.a_sorted = ws.tensor("a_sorted", (rows_cap, H), torch.uint8).view(ops.FP8)
+            layer.as_t = ws.tensor("as_t", (H // 128, rows_cap), torch.float32)
+            self._a_dst = ptr_array([ws.peer("a_sorted", r) for r in range(P)])
+            self._as_dst = ptr_array([ws.peer("as_t", r) for r in range(P)])
+            self.push_counters = ws.local("push_counters")
+            self.block_order = torch.empty(layer.route.nblk, dtype=torch.int32, device=layer.device)
+            # compute-only stand-in: every destination is the own operand, every flag the own one
+            self._own_a = ptr_array([ws.local("a_sorted")] * P)
+            self._own_as = ptr_array([ws.local("as_t")] * P)
         layer.xq = ws.tensor("xq", (T, H), torch.uint8).view(ops.FP8)
         layer.xs = ws.tensor("xs", (T, H // 128), torch.float32)
         if self.rs_mode == "gemm":
@@ -290,6 +317,7 @@ class P2PExchange:
         self._q_dst = ptr_array([ws.peer("xq", r) for r in range(P)])
         self._s_dst = ptr_array([ws.peer("xs", r) for r in range(P)])
         self._ag_dst = ptr_array([ws.peer("ag_flags", r) + 4 * self.rank for r in range(P)])
+        self._ag_own_all = ptr_array([self.ag_flags + 4 * self.rank] * P)
         if self.rs_mode != "gemm":
             self._slot_dst = ptr_array([ws.peer("slots", r) for r in range(P)])
         self._rs_dst = ptr_array([ws.peer("rs_flags", r) + 4 * self.rank for r in range(P)])
@@ -331,6 +359,9 @@ class P2PExchange:
         self.epoch += 1
         st = ops._stream(layer.device)
         Tl, H = layer.T_local, layer.H
+        if self.ag_mode == "push":
+            self._push(layer, x_local, self._a_dst, self._as_dst, self._ag_dst, self.epoch)
+            return
         if self.ag_mode == "sm":
             _lib.call("b2m_quant_push", x_local.data_ptr(), Tl, H, x_local.stride(0), self.world_size, self._q_dst,
                       self._s_dst, self.rank * Tl, self._ag_dst, self.epoch, self.counters, st)
@@ -377,7 +408,36 @@ class P2PExchange:
                 _lib.call("b2m_signal", self._ag_peer[r], 1, self.epoch, s.cuda_stream)
         self._pending_side = True
 
+    def _push(self, layer: "MoELayer", x_local: torch.Tensor, a_dst, as_dst, flag_dst, epoch: int) -> None:
+        from . import _lib
+
+        r, st, Tl, P = layer.route, ops._stream(layer.device), layer.T_local, self.world_size
+        _lib.call("b2m_block_order", r.sorted_ids.data_ptr(), r.ntpp.data_ptr(), layer.numel, layer.top_k, Tl, P,
+                  self.rank, self.block_order.data_ptr(), self.block_order.numel(), layer.status.data_ptr(), st)
+        _lib.call("b2m_quant_dispatch_push", x_local.data_ptr(), Tl, layer.H, x_local.stride(0), r.pair_pos.data_ptr(),
+                  layer.top_k, self.rank * Tl, P, self.rank, a_dst, as_dst, r.rows_cap, flag_dst, epoch,
+                  self.push_counters, st)
+
+    def gemm1(self, layer: "MoELayer") -> bool:
+        """Runs the gate/up GEMM when the rows arrive by push; False: the layer runs its own."""
+        from . import _lib
+
+        if self.ag_mode != "push":
+            return False
+        r = layer.route
+        _lib.call("b2m_gemm1_wait", layer.a_sorted.data_ptr(), layer.as_t.data_ptr(), r.rows_cap, layer.H,
+                  layer.w.w1i.data_ptr(), layer.w.w1i_scale.data_ptr(), layer.w.num_experts, layer.w.inter,
+                  r.expert_ids.data_ptr(), r.ntpp.data_ptr(), self.block_order.data_ptr(), r.sorted_ids.data_ptr(),
+                  layer.numel, layer.top_k, layer.T_local, self.ag_flags, 0 if self.compute_only else self.epoch,
+                  layer.inter_q.data_ptr(), layer.inter_st.data_ptr(), layer.status.data_ptr(),
+                  ops._stream(layer.device))
+        return True
+
     def _gather_dispatch_local(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
+        if self.ag_mode == "push":
+            # same kernels, own memory only: every row copy lands in the own operand, flag epoch 0
+            self._push(layer, x_local, self._own_a, self._own_as, self._ag_own_all, 0)
+            return
         r0 = self.rank * layer.T_local
         ops.quant_g128(x_local, layer.xq[r0:r0 + layer.T_local], layer.xs[r0:r0 + layer.T_local])
         if layer.shared is not None and layer.ep:
@@ -570,8 +630,10 @@ class MoELayer:
     def gemm1(self) -> None:
         r = self.route
         self._event("gemm1_start")
-        ops.gemm1(self.a_sorted, self.as_t, self.w.w1i, self.w.w1i_scale, r.expert_ids, r.ntpp, self.inter_q,
-                  self.inter_st, self.status, block_pairs=r.pairs(self.paired))
+        hook = getattr(self.exchange, "gemm1", None)
+        if hook is None or not hook(self):
+            ops.gemm1(self.a_sorted, self.as_t, self.w.w1i, self.w.w1i_scale, r.expert_ids, r.ntpp, self.inter_q,
+                      self.inter_st, self.status, block_pairs=r.pairs(self.paired))
         self._event("gemm1_end")
 
     def gemm2(self, topk_weights: torch.Tensor, cols: tuple[int, int] | None = None, max_ctas: int = 0) -> None:

@@ -28,13 +28,14 @@ B200_TUNABLES = {
 }
 # peer-memory exchange knobs of d3 / d4 (P2PExchange)
 P2P_TUNABLES = {
-    "ag_mode": TunableSpec(str, "auto", "all-gather by SM stores from the quant kernel ('sm'), copy engines ('ce') "
-                                        "or by block size ('auto')"),
+    "ag_mode": TunableSpec(str, "auto", "all-gather by SM stores from the quant kernel ('sm'), copy engines ('ce'), "
+                                        "by block size ('auto'), or (TP) straight into the peers' sorted operand "
+                                        "under the gate/up GEMM ('push')"),
     "rs_mode": TunableSpec(str, "sm", "reduce-scatter by SM stores from the combine ('sm'), from the down GEMM's "
                                       "epilogue ('gemm') or copy engines ('ce')"),
     "rs_chunks": TunableSpec(int, 4, "down-GEMM column chunks of the copy-engine reduce-scatter (1..8)"),
 }
-_CHOICES = {"ag_mode": ("sm", "ce", "auto"), "rs_mode": ("sm", "ce", "gemm")}
+_CHOICES = {"ag_mode": ("sm", "ce", "auto", "push"), "rs_mode": ("sm", "ce", "gemm")}
 
 
 def _spec(code: str, name: str, parallel: str, comm: str) -> SchemeSpec:

@@ -386,3 +386,104 @@ def test_gemm2_scatter_and_rs_combine(world, src, paired):
             acc = acc + r[s, :, j]
     acc = acc + add.float().numpy()
     assert torch.equal(out.cpu(), torch.from_numpy(acc).to(torch.bfloat16))
+
+
+def _route(T, k, E, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+
+
+@pytest.mark.parametrize("T,H,k,E,world,src", [(512, 1024, 2, 8, 4, 2), (256, 2048, 8, 16, 2, 0), (96, 512, 3, 5, 3, 1)])
+def test_quant_dispatch_push_bit_exact(T, H, k, E, world, src):
+    """All-gather into the sorted operand (destinations emulated by buffers on this GPU): each
+    destination holds exactly the source's rows and scales that b2m_quant_dispatch writes."""
+    from td_benchmark_b200 import _lib
+    from td_benchmark_b200.symm import ptr_array
+
+    x = _bf16((T, H), T + H + k, 2.0).to(DEV)
+    ids = _route(T, k, E, 3).to(DEV)
+    pp = torch.empty(T * k, dtype=torch.int32, device=DEV)
+    sorted_ids, eids, ntpp = ops.moe_align_block_size(ids, 128, E, pair_pos=pp)
+    rows_cap = eids.numel() * 128
+    a_ref = torch.zeros((rows_cap, H), dtype=torch.float8_e4m3fn, device=DEV)
+    s_ref = torch.zeros((H // 128, rows_cap), dtype=torch.float32, device=DEV)
+    ops.quant_dispatch(x, pp, k, a_ref, s_ref)
+    Tl = T // world
+    a_d = [torch.zeros((rows_cap, H), dtype=torch.uint8, device=DEV) for _ in range(world)]
+    s_d = [torch.zeros((H // 128, rows_cap), dtype=torch.float32, device=DEV) for _ in range(world)]
+    flags = torch.zeros(world, dtype=torch.int32, device=DEV)
+    counters = torch.zeros(world, dtype=torch.int32, device=DEV)
+    xs = x[src * Tl:(src + 1) * Tl].contiguous()
+    for epoch in (5, 6):                            # second call: counters must have been re-armed
+        _lib.call("b2m_quant_dispatch_push", xs.data_ptr(), Tl, H, H, pp.data_ptr(), k, src * Tl, world, src,
+                  ptr_array([a.data_ptr() for a in a_d]), ptr_array([s.data_ptr() for s in s_d]), rows_cap,
+                  ptr_array([flags.data_ptr() + 4 * d for d in range(world)]), epoch, counters.data_ptr(),
+                  torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert flags.tolist() == [epoch] * world and not counters.any()
+    pos = pp.view(T, k)[src * Tl:(src + 1) * Tl].reshape(-1).long().cpu()
+    pos = pos[pos >= 0]
+    mask = torch.zeros(rows_cap, dtype=torch.bool)
+    mask[pos] = True
+    for a, s in zip(a_d, s_d):
+        assert torch.equal(a.cpu()[mask], a_ref.view(torch.uint8).cpu()[mask])
+        assert not a.cpu()[~mask].any()
+        assert torch.equal(s.cpu()[:, mask], s_ref.cpu()[:, mask])
+
+
+@pytest.mark.parametrize("T,k,E,world,rank", [(512, 2, 8, 8, 3), (256, 8, 128, 4, 0), (1000, 2, 8, 5, 4)])
+def test_block_order(T, k, E, world, rank):
+    from td_benchmark_b200 import _lib
+
+    ids = _route(T, k, E, T + world).to(DEV)
+    sorted_ids, eids, ntpp = ops.moe_align_block_size(ids, 128, E)
+    Tl = (T + world - 1) // world
+    order = torch.full((eids.numel(),), -7, dtype=torch.int32, device=DEV)
+    status = ops.new_status(DEV)
+    _lib.call("b2m_block_order", sorted_ids.data_ptr(), ntpp.data_ptr(), T * k, k, Tl, world, rank, order.data_ptr(),
+              order.numel(), status.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ops.check_status(status)
+    nblk = int(ntpp.item()) // 128
+    srt = sorted_ids.cpu().numpy()[:nblk * 128].reshape(nblk, 128)
+    keys = []
+    for b in range(nblk):
+        v = srt[b][srt[b] < T * k]
+        keys.append(int((((v // k) // Tl - rank) % world).max()) if v.size else 0)
+    want = sorted(range(nblk), key=lambda b: (keys[b], b))
+    assert order.cpu().tolist()[:nblk] == want
+
+
+@pytest.mark.parametrize("world,rank", [(2, 1), (8, 5)])
+def test_gemm1_wait_matches_gemm1(world, rank):
+    """The gate/up GEMM in block order with its source waits satisfied equals b2m_gemm1."""
+    from td_benchmark_b200 import _lib
+
+    T, H, I, E, k = 512, 512, 256, 8, 2
+    x, w1q, w1s, w2q, w2s, ids, wts = _gemm_problem(T, H, I, E, k, 99 + world, False)
+    xq, xs = ops.quant_g128(x.to(DEV))
+    w1i, w1is = ops.w1_interleave(w1q.to(DEV), w1s.to(DEV))
+    pp = torch.empty(T * k, dtype=torch.int32, device=DEV)
+    sorted_ids, eids, ntpp = ops.moe_align_block_size(ids.to(DEV), 128, E, pair_pos=pp)
+    rows_cap = eids.numel() * 128
+    a_sorted = torch.zeros((rows_cap, H), dtype=torch.float8_e4m3fn, device=DEV)
+    a_st = torch.zeros((H // 128, rows_cap), dtype=torch.float32, device=DEV)
+    ops.dispatch_rows(xq, xs, pp, k, a_sorted, a_st)
+    status = ops.new_status(DEV)
+    hq, hst = ops.gemm1(a_sorted, a_st, w1i, w1is, eids, ntpp, status=status)
+    order = torch.empty(eids.numel(), dtype=torch.int32, device=DEV)
+    st = torch.cuda.current_stream().cuda_stream
+    Tl = T // world
+    _lib.call("b2m_block_order", sorted_ids.data_ptr(), ntpp.data_ptr(), T * k, k, Tl, world, rank, order.data_ptr(),
+              order.numel(), status.data_ptr(), st)
+    flags = torch.full((world,), 9, dtype=torch.int32, device=DEV)
+    hq2 = torch.zeros_like(hq)
+    hst2 = torch.zeros_like(hst)
+    _lib.call("b2m_gemm1_wait", a_sorted.data_ptr(), a_st.data_ptr(), rows_cap, H, w1i.data_ptr(), w1is.data_ptr(), E,
+              I, eids.data_ptr(), ntpp.data_ptr(), order.data_ptr(), sorted_ids.data_ptr(), T * k, k, Tl,
+              flags.data_ptr(), 9, hq2.data_ptr(), hst2.data_ptr(), status.data_ptr(), st)
+    torch.cuda.synchronize()
+    ops.check_status(status)
+    n = int(ntpp.item())
+    assert torch.equal(hq2.view(torch.uint8)[:n].cpu(), hq.view(torch.uint8)[:n].cpu())
+    assert torch.equal(hst2[:, :n].cpu(), hst[:, :n].cpu())

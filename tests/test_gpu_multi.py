@@ -38,6 +38,10 @@ def _port() -> int:
     ("d3", "mixtral", 512, ["--rs-mode", "gemm"]),
     ("d4", "dsv3", 1024, ["--zipf", "--rs-mode", "gemm"]),
     ("d3", "qwen3", 256, ["--rs-mode", "gemm"]),
+    # all-gather stored straight into the peers' sorted operand under the gate/up GEMM
+    ("d3", "mixtral", 512, ["--ag-mode", "push"]),
+    ("d3", "mixtral", 1024, ["--ag-mode", "push", "--rs-mode", "gemm"]),
+    ("d3", "qwen3", 256, ["--ag-mode", "push"]),
 ], ids=lambda v: "-".join(a.strip("-") for a in v) if isinstance(v, list) else str(v))
 def test_multi_gpu_scheme_matches_golden(scheme, preset, tokens, extra):
     n = min(_gpus(), 4)
