@@ -156,19 +156,25 @@ int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, in
               const int32_t* num_tokens_post_padded, const int32_t* block_pairs, void* out_q, float* out_scale_t,
               int32_t* dev_status, void* stream);
 
-/* b2m_gemm1 for a tensor-parallel layer whose A rows are stored by the source ranks
- * (b2m_quant_dispatch_push) while it runs, so the all-gather overlaps the GEMM: M blocks
- * are visited in block_order (b2m_block_order: own rows first), and before a block's loads
- * the producer waits until src_flags[s] >= epoch for every source s among its rows
- * (source of pair p = (p / top_k) / tokens_per_src, from sorted_token_ids; pads = numel).
- * Waits are bounded (timeout -> B2M_STATUS_TIMEOUT_PEER in dev_status).  No paired-CTA
- * variant.  Replaces the gate/up GEMM after the all-gather of overlap_forward.py:494-552. */
+/* b2m_gemm1 for a tensor-parallel layer whose A rows are stored by the source ranks while
+ * it runs, so the all-gather overlaps the GEMM (replaces the all-gather + gate/up GEMM of
+ * overlap_forward.py:494-552): M blocks are visited in block_order (b2m_block_order: own
+ * rows first), and before a block's loads the producer waits until src_flags[s] >= epoch
+ * for every source s among its rows (source of pair p = (p / top_k) / tokens_per_src,
+ * from sorted_token_ids; pads = numel).  With push_pos != NULL the GEMM also performs this
+ * rank's part of the all-gather: two otherwise idle warps per CTA copy the rows
+ * push_pos[0 .. push_pairs) of a_sorted (and their scales) to the same rows of push_a[d] /
+ * push_s[d] for every peer d (rank-1, rank-2, ...) and set *push_flags[d] = epoch when
+ * done (push_counters: world int32, zero before the first call).  The own rows must be in
+ * a_sorted before the call (b2m_quant_dispatch_push with world 1).  Waits are bounded
+ * (timeout -> B2M_STATUS_TIMEOUT_PEER in dev_status).  No paired-CTA variant. */
 int b2m_gemm1_wait(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden, const void* w1,
                    const float* w1_scale, int32_t num_experts, int32_t inter, const int32_t* expert_ids,
                    const int32_t* num_tokens_post_padded, const int32_t* block_order,
                    const int32_t* sorted_token_ids, int64_t numel, int32_t top_k, int64_t tokens_per_src,
-                   const uint32_t* src_flags, uint32_t epoch, void* out_q, float* out_scale_t, int32_t* dev_status,
-                   void* stream);
+                   const uint32_t* src_flags, uint32_t epoch, const int32_t* push_pos, int64_t push_pairs,
+                   void* const* push_a, void* const* push_s, uint32_t* const* push_flags, int32_t* push_counters,
+                   int32_t world, int32_t rank, void* out_q, float* out_scale_t, int32_t* dev_status, void* stream);
 
 /* ---------------------------------------------------------------------------
  * K4  down grouped GEMM with the routed top-k weight in the epilogue.

@@ -116,6 +116,20 @@ struct GemmParams {
   uint32_t src_epoch;
   int64_t tokens_per_src;
   const int32_t* block_order;
+  // All-gather pushed from inside the gate/up GEMM (push_world > 1): warps 2-3 of every CTA
+  // copy this rank's pair rows -- already quantised into the own sorted operand (A) and its
+  // K-block-major scales -- to the same rows of every peer, destination by destination
+  // (rank-1, rank-2, ...), and publish push_flag[d] = src_epoch when the grid is done with d.
+  const int32_t* push_pos;  // sorted position of each of this rank's pairs, -1: none
+  int64_t push_pairs;
+  const uint8_t* push_src_a;
+  const float* push_src_s;
+  uint8_t* push_a[8];
+  float* push_s[8];
+  uint32_t* push_flag[8];
+  int32_t* push_counters;   // [push_world], zero between calls
+  int32_t push_world;
+  int32_t push_rank;
 };
 
 // silu(x) = x * sigmoid(x).  The gate/up intermediate is requantised to e4m3 right
@@ -183,6 +197,54 @@ __device__ __forceinline__ bool wait_block_sources(const GemmParams& p, int mb, 
   }
   ready = __shfl_sync(0xffffffffu, ready, 0);
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// ---------------------------------------------------------------- warps 2-3: all-gather pusher
+// Pusher warp g of G = 2 * gridDim.x copies pair rows g, g + G, ...: the row (hidden e4m3
+// codes, 16 bytes per lane per step, 4 steps in flight) and its hidden/128 scales, from the
+// own sorted operand to the same row of each peer.  The warp counts itself on the peer's
+// counter after its last row for that peer; the last warp publishes the peer's flag.
+__device__ __forceinline__ void push_rows(const GemmParams& p, int lane) {
+  const int64_t g = static_cast<int64_t>(blockIdx.x) * 2 + ((threadIdx.x >> 5) - 2);
+  const int64_t G = static_cast<int64_t>(gridDim.x) * 2;
+  const int64_t cols = p.hidden;
+  const int kbn = static_cast<int>(cols / 128);
+  for (int i = 1; i < p.push_world; ++i) {
+    const int d = (p.push_rank - i + p.push_world) % p.push_world;
+    uint8_t* dst_a = p.push_a[d];
+    float* dst_s = p.push_s[d];
+    for (int64_t pr = g; pr < p.push_pairs; pr += G) {
+      const int64_t pos = __ldg(p.push_pos + pr);
+      if (pos < 0) continue;
+      const uint8_t* src = p.push_src_a + pos * cols;
+      uint8_t* dst = dst_a + pos * cols;
+      // 4 x 16 bytes in flight per lane: this role runs after setmaxnreg.dec to 72 registers
+      for (int64_t c0 = static_cast<int64_t>(lane) * 16; c0 < cols; c0 += 32 * 16 * 4) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t c = c0 + u * 512;
+          if (c < cols) v[u] = __ldg(reinterpret_cast<const uint4*>(src + c));
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t c = c0 + u * 512;
+          if (c < cols) *reinterpret_cast<uint4*>(dst + c) = v[u];
+        }
+      }
+      for (int kb = lane; kb < kbn; kb += 32) dst_s[kb * p.rows_cap + pos] = __ldg(p.push_src_s + kb * p.rows_cap + pos);
+    }
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) {
+      const int prev = atomicAdd(p.push_counters + d, 1);
+      if (prev == static_cast<int>(G) - 1) {
+        fence_sys();
+        st_release_sys(p.push_flag[d], p.src_epoch);
+        atomicExch(p.push_counters + d, 0);
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------- warp 0: B (+A for the down GEMM)
@@ -516,6 +578,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else if (warp == 1) {
       if (lane == 0) mma_thread(p, smem, C, tw, tmem_base);
       __syncwarp();
+    } else if (kGateUp && p.push_world > 1) {
+      push_rows(p, lane);
     }
   } else {
     reg_alloc<216>();
@@ -934,6 +998,14 @@ struct SourceWait {
   int64_t tokens_per_src;
   const uint32_t* flags;
   uint32_t epoch;
+  const int32_t* push_pos;  // nullptr: no pushing
+  int64_t push_pairs;
+  void* const* push_a;
+  void* const* push_s;
+  uint32_t* const* push_flags;
+  int32_t* push_counters;
+  int32_t world;
+  int32_t rank;
 };
 
 int gemm1_impl(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden, const void* w1,
@@ -986,6 +1058,25 @@ int gemm1_impl(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, i
     p.tokens_per_src = sw->tokens_per_src;
     p.src_flags = sw->flags;
     p.src_epoch = sw->epoch;
+    if (sw->push_pos) {
+      if (sw->world < 2 || sw->world > 8 || sw->rank < 0 || sw->rank >= sw->world || sw->push_pairs < 0 ||
+          !sw->push_a || !sw->push_s || !sw->push_flags || !sw->push_counters)
+        return fail(B2M_ERR_ARG, "gemm1_wait: push needs 2 <= world <= 8, 0 <= rank < world and every peer table");
+      for (int r = 0; r < sw->world; ++r) {
+        if (!sw->push_a[r] || !sw->push_s[r] || !sw->push_flags[r] || !aligned16(sw->push_a[r]))
+          return fail(B2M_ERR_ARG, "gemm1_wait: bad push pointer %d", r);
+        p.push_a[r] = static_cast<uint8_t*>(sw->push_a[r]);
+        p.push_s[r] = static_cast<float*>(sw->push_s[r]);
+        p.push_flag[r] = sw->push_flags[r];
+      }
+      p.push_pos = sw->push_pos;
+      p.push_pairs = sw->push_pairs;
+      p.push_src_a = static_cast<const uint8_t*>(a_sorted);
+      p.push_src_s = a_scale_t;
+      p.push_counters = sw->push_counters;
+      p.push_world = sw->world;
+      p.push_rank = sw->rank;
+    }
   }
   if (block_pairs) return launch_gemm_pair<true>(ma, mb, p, block_pairs, num_sms, static_cast<cudaStream_t>(stream));
   return launch_gemm<true>(ma, mb, p, num_sms, static_cast<cudaStream_t>(stream));
@@ -1008,8 +1099,12 @@ extern "C" int b2m_gemm1_wait(const void* a_sorted, const float* a_scale_t, int6
                               const int32_t* expert_ids, const int32_t* num_tokens_post_padded,
                               const int32_t* block_order, const int32_t* sorted_token_ids, int64_t numel,
                               int32_t top_k, int64_t tokens_per_src, const uint32_t* src_flags, uint32_t epoch,
-                              void* out_q, float* out_scale_t, int32_t* dev_status, void* stream) {
-  const b2m::SourceWait sw{block_order, sorted_token_ids, numel, top_k, tokens_per_src, src_flags, epoch};
+                              const int32_t* push_pos, int64_t push_pairs, void* const* push_a,
+                              void* const* push_s, uint32_t* const* push_flags, int32_t* push_counters,
+                              int32_t world, int32_t rank, void* out_q, float* out_scale_t, int32_t* dev_status,
+                              void* stream) {
+  const b2m::SourceWait sw{block_order, sorted_token_ids, numel, top_k, tokens_per_src, src_flags, epoch,
+                           push_pos, push_pairs, push_a, push_s, push_flags, push_counters, world, rank};
   return b2m::gemm1_impl(a_sorted, a_scale_t, rows_cap, hidden, w1, w1_scale, num_experts, inter, expert_ids,
                          num_tokens_post_padded, nullptr, out_q, out_scale_t, &sw, dev_status, stream);
 }

@@ -206,17 +206,19 @@ class P2PExchange:
            copy engines copy that contiguous block (codes, then scales) to each peer on
            side streams, and ``b2m_signal`` (a stream memory write, no SM) publishes each
            peer's flag right after its copies.
-      "push" -- tensor parallel only: ``b2m_quant_dispatch_push`` stores each token's rows
-           straight into every rank's expert-sorted operand (every rank aligns the same
-           routing, so the sorted positions agree), own rank first, then rank-1, rank-2, ...
-           with a flag per destination; the gate/up GEMM (``b2m_gemm1_wait``) visits its M
-           blocks own-rows-first (``b2m_block_order``) and waits per block for the flags of
-           the sources the block holds.  No gather buffer and no dispatch kernel; top_k
-           copies of each token cross NVLink.  As built the push is a kernel of its own
-           that runs to completion before the GEMM on the same GPU, so only the peers'
-           skew is hidden while the push itself (k copies, destination by destination)
-           costs more than the plain push + dispatch: Mixtral TP2 1084 vs 995 us.  Its
-           payoff needs the pushes issued from inside the GEMM (its idle warps).
+      "push" -- tensor parallel only: the all-gather runs inside the gate/up GEMM.  Every
+           rank aligns the same routing, so the sorted row of each (token, expert) pair is
+           the same on every rank.  ``b2m_quant_dispatch_push`` (world 1) quantises the own
+           tokens into the own expert-sorted operand; then ``b2m_gemm1_wait`` visits its M
+           blocks own-rows-first (``b2m_block_order``), waits per block for the flags of the
+           sources the block holds, and two otherwise idle warps per CTA copy the own rows
+           to the same rows of every peer (rank-1, rank-2, ...), publishing a flag per peer.
+           No gather buffer and no dispatch kernel; top_k copies of each token cross NVLink.
+           Measured on 2 B200s (Mixtral TP2): the exposed all-gather falls from 34 us to
+           3 us, but the gate/up GEMM runs 5 % slower beside its pusher warps and the own-row
+           kernel + block order cost 16 us more than quant + dispatch, so the layer is
+           slower there (1030 vs 995 us); at 8 GPUs, where the all-gather + dispatch it
+           hides take 63 us, it is expected to win but has not been measured.
       "auto" (default) -- "ce" when a rank's block of codes is at least
            ``AG_CE_MIN_BYTES``, else "sm".  On 8 B200s the copy engines won for the
            DeepSeek-V3 EP shape (7.3 MB per peer: 1648 vs 1683 us per layer) and lost for
@@ -291,7 +293,8 @@ class P2PExchange:
             layout["slots"] = T * H * 2
         rows_cap = layer.route.rows_cap
         if self.ag_mode == "push":
-            layout.update({"a_sorted": rows_cap * H, "as_t": (H // 128) * rows_cap * 4, "push_counters": 4 * P})
+            layout.update({"a_sorted": rows_cap * H, "as_t": (H // 128) * rows_cap * 4,
+                           "push_counters": 4 * (P + 1)})
         self.ws = SymmetricWorkspace(layout, self.group, layer.device)
         ws = self.ws
         if self.ag_mode == "push":
@@ -302,9 +305,8 @@ class P2PExchange:
             self._as_dst = ptr_array([ws.peer("as_t", r) for r in range(P)])
             self.push_counters = ws.local("push_counters")
             self.block_order = torch.empty(layer.route.nblk, dtype=torch.int32, device=layer.device)
-            # compute-only stand-in: every destination is the own operand, every flag the own one
-            self._own_a = ptr_array([ws.local("a_sorted")] * P)
-            self._own_as = ptr_array([ws.local("as_t")] * P)
+            self._own_a = ptr_array([ws.local("a_sorted")])
+            self._own_as = ptr_array([ws.local("as_t")])
         layer.xq = ws.tensor("xq", (T, H), torch.uint8).view(ops.FP8)
         layer.xs = ws.tensor("xs", (T, H // 128), torch.float32)
         if self.rs_mode == "gemm":
@@ -317,7 +319,7 @@ class P2PExchange:
         self._q_dst = ptr_array([ws.peer("xq", r) for r in range(P)])
         self._s_dst = ptr_array([ws.peer("xs", r) for r in range(P)])
         self._ag_dst = ptr_array([ws.peer("ag_flags", r) + 4 * self.rank for r in range(P)])
-        self._ag_own_all = ptr_array([self.ag_flags + 4 * self.rank] * P)
+        self._ag_own = ptr_array([self.ag_flags + 4 * self.rank])
         if self.rs_mode != "gemm":
             self._slot_dst = ptr_array([ws.peer("slots", r) for r in range(P)])
         self._rs_dst = ptr_array([ws.peer("rs_flags", r) + 4 * self.rank for r in range(P)])
@@ -360,7 +362,7 @@ class P2PExchange:
         st = ops._stream(layer.device)
         Tl, H = layer.T_local, layer.H
         if self.ag_mode == "push":
-            self._push(layer, x_local, self._a_dst, self._as_dst, self._ag_dst, self.epoch)
+            self._push_own(layer, x_local, self.epoch)
             return
         if self.ag_mode == "sm":
             _lib.call("b2m_quant_push", x_local.data_ptr(), Tl, H, x_local.stride(0), self.world_size, self._q_dst,
@@ -408,15 +410,16 @@ class P2PExchange:
                 _lib.call("b2m_signal", self._ag_peer[r], 1, self.epoch, s.cuda_stream)
         self._pending_side = True
 
-    def _push(self, layer: "MoELayer", x_local: torch.Tensor, a_dst, as_dst, flag_dst, epoch: int) -> None:
+    def _push_own(self, layer: "MoELayer", x_local: torch.Tensor, epoch: int) -> None:
+        """Block order, then the own tokens quantised into the own sorted operand (own flag)."""
         from . import _lib
 
         r, st, Tl, P = layer.route, ops._stream(layer.device), layer.T_local, self.world_size
         _lib.call("b2m_block_order", r.sorted_ids.data_ptr(), r.ntpp.data_ptr(), layer.numel, layer.top_k, Tl, P,
                   self.rank, self.block_order.data_ptr(), self.block_order.numel(), layer.status.data_ptr(), st)
         _lib.call("b2m_quant_dispatch_push", x_local.data_ptr(), Tl, layer.H, x_local.stride(0), r.pair_pos.data_ptr(),
-                  layer.top_k, self.rank * Tl, P, self.rank, a_dst, as_dst, r.rows_cap, flag_dst, epoch,
-                  self.push_counters, st)
+                  layer.top_k, self.rank * Tl, 1, 0, self._own_a, self._own_as, r.rows_cap, self._ag_own, epoch,
+                  self.push_counters + 4 * P, st)
 
     def gemm1(self, layer: "MoELayer") -> bool:
         """Runs the gate/up GEMM when the rows arrive by push; False: the layer runs its own."""
@@ -424,19 +427,21 @@ class P2PExchange:
 
         if self.ag_mode != "push":
             return False
-        r = layer.route
+        r, Tl, k, P = layer.route, layer.T_local, layer.top_k, self.world_size
+        push = not self.compute_only        # compute-only: same GEMM, nothing sent, waits satisfied
         _lib.call("b2m_gemm1_wait", layer.a_sorted.data_ptr(), layer.as_t.data_ptr(), r.rows_cap, layer.H,
                   layer.w.w1i.data_ptr(), layer.w.w1i_scale.data_ptr(), layer.w.num_experts, layer.w.inter,
                   r.expert_ids.data_ptr(), r.ntpp.data_ptr(), self.block_order.data_ptr(), r.sorted_ids.data_ptr(),
-                  layer.numel, layer.top_k, layer.T_local, self.ag_flags, 0 if self.compute_only else self.epoch,
-                  layer.inter_q.data_ptr(), layer.inter_st.data_ptr(), layer.status.data_ptr(),
-                  ops._stream(layer.device))
+                  layer.numel, k, Tl, self.ag_flags, self.epoch if push else 0,
+                  r.pair_pos.data_ptr() + 4 * self.rank * Tl * k if push else None, Tl * k,
+                  self._a_dst if push else None, self._as_dst if push else None, self._ag_dst if push else None,
+                  self.push_counters if push else None, P, self.rank, layer.inter_q.data_ptr(),
+                  layer.inter_st.data_ptr(), layer.status.data_ptr(), ops._stream(layer.device))
         return True
 
     def _gather_dispatch_local(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
         if self.ag_mode == "push":
-            # same kernels, own memory only: every row copy lands in the own operand, flag epoch 0
-            self._push(layer, x_local, self._own_a, self._own_as, self._ag_own_all, 0)
+            self._push_own(layer, x_local, 0)
             return
         r0 = self.rank * layer.T_local
         ops.quant_g128(x_local, layer.xq[r0:r0 + layer.T_local], layer.xs[r0:r0 + layer.T_local])

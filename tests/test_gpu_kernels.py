@@ -481,9 +481,71 @@ def test_gemm1_wait_matches_gemm1(world, rank):
     hst2 = torch.zeros_like(hst)
     _lib.call("b2m_gemm1_wait", a_sorted.data_ptr(), a_st.data_ptr(), rows_cap, H, w1i.data_ptr(), w1is.data_ptr(), E,
               I, eids.data_ptr(), ntpp.data_ptr(), order.data_ptr(), sorted_ids.data_ptr(), T * k, k, Tl,
-              flags.data_ptr(), 9, hq2.data_ptr(), hst2.data_ptr(), status.data_ptr(), st)
+              flags.data_ptr(), 9, None, 0, None, None, None, None, 0, 0, hq2.data_ptr(), hst2.data_ptr(),
+              status.data_ptr(), st)
     torch.cuda.synchronize()
     ops.check_status(status)
     n = int(ntpp.item())
     assert torch.equal(hq2.view(torch.uint8)[:n].cpu(), hq.view(torch.uint8)[:n].cpu())
     assert torch.equal(hst2[:, :n].cpu(), hst[:, :n].cpu())
+
+
+@pytest.mark.parametrize("world,rank", [(2, 0), (4, 2)])
+def test_gemm1_pushes_own_rows_to_peers(world, rank):
+    """The gate/up GEMM's pusher warps (peers emulated by buffers on this GPU, their waits
+    already satisfied): every peer gets exactly this rank's pair rows and scales, the flag of
+    every peer is published, counters are re-armed, and the GEMM output is unchanged."""
+    from td_benchmark_b200 import _lib
+    from td_benchmark_b200.symm import ptr_array
+
+    T, H, I, E, k = 512, 1024, 256, 8, 2
+    x, w1q, w1s, w2q, w2s, ids, wts = _gemm_problem(T, H, I, E, k, 7 * world + rank, False)
+    xq, xs = ops.quant_g128(x.to(DEV))
+    w1i, w1is = ops.w1_interleave(w1q.to(DEV), w1s.to(DEV))
+    pp = torch.empty(T * k, dtype=torch.int32, device=DEV)
+    sorted_ids, eids, ntpp = ops.moe_align_block_size(ids.to(DEV), 128, E, pair_pos=pp)
+    rows_cap = eids.numel() * 128
+    a_sorted = torch.zeros((rows_cap, H), dtype=torch.float8_e4m3fn, device=DEV)
+    a_st = torch.zeros((H // 128, rows_cap), dtype=torch.float32, device=DEV)
+    ops.dispatch_rows(xq, xs, pp, k, a_sorted, a_st)
+    status = ops.new_status(DEV)
+    hq, hst = ops.gemm1(a_sorted, a_st, w1i, w1is, eids, ntpp, status=status)
+    st = torch.cuda.current_stream().cuda_stream
+    Tl = T // world
+    order = torch.empty(eids.numel(), dtype=torch.int32, device=DEV)
+    _lib.call("b2m_block_order", sorted_ids.data_ptr(), ntpp.data_ptr(), T * k, k, Tl, world, rank, order.data_ptr(),
+              order.numel(), status.data_ptr(), st)
+    wait_flags = torch.full((world,), 4, dtype=torch.int32, device=DEV)
+    peers_a = [a_sorted.view(torch.uint8) if d == rank else torch.zeros((rows_cap, H), dtype=torch.uint8, device=DEV)
+               for d in range(world)]
+    peers_s = [a_st if d == rank else torch.zeros((H // 128, rows_cap), dtype=torch.float32, device=DEV)
+               for d in range(world)]
+    push_flags = torch.zeros(world, dtype=torch.int32, device=DEV)
+    counters = torch.zeros(world, dtype=torch.int32, device=DEV)
+    own_pos = pp[rank * Tl * k:(rank + 1) * Tl * k].contiguous()
+    hq2, hst2 = torch.zeros_like(hq), torch.zeros_like(hst)
+    for _ in range(2):                              # second call: counters re-armed by the first
+        _lib.call("b2m_gemm1_wait", a_sorted.data_ptr(), a_st.data_ptr(), rows_cap, H, w1i.data_ptr(),
+                  w1is.data_ptr(), E, I, eids.data_ptr(), ntpp.data_ptr(), order.data_ptr(), sorted_ids.data_ptr(),
+                  T * k, k, Tl, wait_flags.data_ptr(), 4, own_pos.data_ptr(), Tl * k,
+                  ptr_array([a.data_ptr() for a in peers_a]), ptr_array([s.data_ptr() for s in peers_s]),
+                  ptr_array([push_flags.data_ptr() + 4 * d for d in range(world)]), counters.data_ptr(), world, rank,
+                  hq2.data_ptr(), hst2.data_ptr(), status.data_ptr(), st)
+        torch.cuda.synchronize()
+        ops.check_status(status)
+        assert not counters.any()
+    want_flags = [0 if d == rank else 4 for d in range(world)]
+    assert push_flags.tolist() == want_flags
+    n = int(ntpp.item())
+    assert torch.equal(hq2.view(torch.uint8)[:n].cpu(), hq.view(torch.uint8)[:n].cpu())
+    assert torch.equal(hst2[:, :n].cpu(), hst[:, :n].cpu())
+    pos = own_pos.long().cpu()
+    pos = pos[pos >= 0]
+    mask = torch.zeros(rows_cap, dtype=torch.bool)
+    mask[pos] = True
+    for d in range(world):
+        if d == rank:
+            continue
+        assert torch.equal(peers_a[d].cpu()[mask], a_sorted.view(torch.uint8).cpu()[mask])
+        assert not peers_a[d].cpu()[~mask].any()
+        assert torch.equal(peers_s[d].cpu()[:, mask], a_st.cpu()[:, mask])
