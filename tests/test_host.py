@@ -117,6 +117,28 @@ def test_p2p_exchange_tunables():
         build_scheme(configs.preset("tiny"), None, None, SchemeCfg("d4", {"ag_mode": "dma"}))
     with pytest.raises(SchemeConfigError, match="1..8"):
         build_scheme(configs.preset("tiny"), None, None, SchemeCfg("d3", {"rs_chunks": 9}))
+    for ok in ({"ag_mode": "push"}, {"ag_mode": "ce", "rs_mode": "gemm"}, {"rs_mode": "ce", "rs_chunks": 8}):
+        with pytest.raises(RuntimeError, match="requires a DataBundle"):   # accepted; fails later for lack of data
+            build_scheme(configs.preset("tiny"), None, None, SchemeCfg("d3", ok))
+
+
+def test_p2p_exchange_rejects_unknown_modes():
+    import torch.distributed as dist
+    from td_benchmark_b200.layer import P2PExchange
+
+    own = not dist.is_initialized()
+    if own:
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:0", rank=0, world_size=1)
+    try:
+        with pytest.raises(ValueError, match="rs_mode"):
+            P2PExchange(rs_mode="dma")
+        with pytest.raises(ValueError, match="ag_mode"):
+            P2PExchange(ag_mode="ring")
+        ex = P2PExchange(ag_mode="push", rs_mode="gemm")
+        assert ex.world_size == 1 and ex.chunks_req == 1 and ex.extra_launches() == 0
+    finally:
+        if own:
+            dist.destroy_process_group()
 
 
 def test_int_tunable_rejects_bool():
