@@ -6,18 +6,20 @@
 // so here each rank writes straight into its peers' memory:
 //
 //  all-gather   b2m_quant_push quantises the rank's tokens and stores the codes and
-//               scales into the same rows of every rank's gather buffer (16-byte P2P
-//               stores); the last CTA to finish publishes ag_flag[src] = epoch on every
+//               scales into the same rows of every rank's gather buffer (512-byte warp
+//               writes); the last CTA to finish publishes ag_flag[src] = epoch on every
 //               rank (system-scope release).  b2m_dispatch_rows_wait then moves rows
 //               into expert order, reading a source rank's rows only after its flag
 //               (own rows first, bounded acquire spin per source).
+//               Tensor parallel alternative: b2m_quant_dispatch_push stores the rows
+//               straight into the ranks' expert-sorted operand (the sorted positions
+//               agree on every rank), destination by destination with a flag each.
 //  reduce-scatter  b2m_combine_push sums each token's top-k rows (+ shared expert) over a
-//               column chunk and stores the bf16 partial into the owning rank's slot for
-//               this source; the last CTA publishes rs_flag[chunk][src] = epoch on every
-//               owner.  Chunk c's push runs on a side stream while the down GEMM of chunk
-//               c+1 runs on the remaining SMs.
-//               b2m_rs_reduce waits for all sources and sums the slots in rank order
-//               (deterministic, fp32, one rounding).
+//               column window and stores the bf16 partial into the owning rank's slot
+//               for this source; the last CTA publishes rs_flag[src] = epoch on every
+//               owner.  b2m_rs_reduce waits for all sources and sums the slots in rank
+//               order (deterministic, fp32, one rounding).  b2m_rs_combine is the owner
+//               side when the down GEMM stored the pair rows itself (b2m_gemm2_scatter).
 //
 // Epochs only grow, so flags are never reset.  Buffers need no extra barrier between
 // calls: a rank starts call i+1 only after its reduce of call i saw every peer's
