@@ -33,7 +33,13 @@
 // and the scale (K-block-major scale layout for the down GEMM).
 // Down epilogue (replaces MUL_ROUTED_WEIGHT + bf16 store, kernels.py:221-310): the
 // row's routed weight times the accumulator, rounded to bf16, stored at the pair's
-// row of the top-k staging buffer.
+// row of the top-k staging buffer, or (b2m_gemm2_scatter) straight into the row's
+// owner rank's receive buffer.
+//
+// Gate/up GEMM fed by peers (b2m_gemm1_wait, tensor parallel): the M blocks are visited
+// in a given order (own rows first), the producer waits per block for the flags of the
+// source ranks the block holds, and warps 2-3 -- otherwise idle -- can push this rank's
+// rows to the same rows of every peer while the MMA pipeline runs.
 //
 // All waits are bounded (b2m_set_timeout_ns); on a timeout the kernel records the
 // site in dev_status, drains its own copies and MMAs and frees TMEM before returning.
