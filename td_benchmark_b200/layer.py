@@ -251,7 +251,7 @@ class P2PExchange:
     """
     name = "p2p"
     MAX_CHUNKS = 8
-    AG_CE_MIN_BYTES = 4 << 20
+    AG_CE_MIN_BYTES = 6 << 20   # between the measured win (7 MiB blocks) and loss (2 MiB blocks)
 
     def __init__(self, group=None, chunks: int = 4, rs_mode: str = "sm", ce_streams: int = 2, ag_mode: str = "auto"):
         import torch.distributed as dist
