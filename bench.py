@@ -1,26 +1,30 @@
 """Benchmark of the B200 FP8 MoE layer (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload mixtral|dsv3|qwen3|tiny] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dsv3|mixtral|qwen3|tiny] [--impl reference]
 
-A step is one forward of the MoE FFN layer of the workload through the scheme
-API (``SchemeInstance.run()``): quant -> all-gather -> align -> GEMM1 -> GEMM2 ->
-combine -> reduce-scatter.  Default workload: the Mixtral-8x7B shape of the
-BASELINE configs (T=4096 tokens, H=4096, I=14336, E=8, top-2) with TP=N over the
-N GPUs (strong scaling: the layer's T tokens are fixed, sharded T/N per rank).
-Inputs are seeded synthetic tensors with the config's shapes and value
-distributions (no dataset); the weights (>= 176 MB per rank) are larger than L2,
-and L2 is also flushed (256 MB write) between timed steps, outside the events.
+A step is one forward of the MoE FFN layer of the workload: align -> quant ->
+all-gather -> dispatch -> GEMM1 (+SiLU*mul+requant) -> GEMM2 (*routed weight) ->
+combine (+shared expert) -> reduce-scatter.  Default workload: the DeepSeek-V3
+shape of the BASELINE configs (T=8192 tokens, H=7168, I=2048, E=256, top-8, Zipf
+1.2 routing, one shared expert of I=2048) with EP=N over the N GPUs (strong
+scaling: the layer's T tokens are fixed, T/N per rank); ``--workload mixtral``
+is the Mixtral-8x7B TP shape.  Inputs are seeded synthetic tensors with the
+config's shapes and value distributions (no dataset); the weights are larger than
+L2, and L2 is also flushed (256 MB write) between timed steps, outside the events.
 
 ``value``: tokens/s of the whole layer (T / step time, step time = per-step max
 over ranks, mean over steps), device-timed with CUDA events on inputs resident
-in HBM.  ``e2e``: the same metric through ``SchemeInstance.run()`` with the
-inputs copied from pinned host memory and the output copied back inside the
-timed region.  ``roofline``: GEMM1 (gate/up, the dominant kernel) FP8 FLOPs of
-the routed (unpadded) pairs over its event-timed duration, against the measured
-FP8 dense peak in ``profiles/peaks.json``.  ``cpu_baseline``: the reference
-algorithm (``oracle.golden.golden_moe``, the numpy restatement of
-``moe_bench/verify.py:14-47``) timed on this host on a bounded token sample.
-``--impl reference`` times only that CPU path (rank 0; other ranks exit 0).
+in HBM.  ``e2e``: the same metric with the inputs copied from pinned host memory
+and the output copied back every step (``HostPipeline``).  ``roofline``: GEMM1
+(gate/up, the dominant kernel) FP8 FLOPs of the routed (unpadded) pairs over its
+event-timed duration against the measured FP8 dense peak, and under ``layer`` the
+layer's FP8 / NVLink / HBM terms of the most-loaded rank.  ``comm`` (N > 1):
+exposed communication and the hidden fraction.  ``parity``: every rank's output of
+a forward after the timed runs against the fp32 golden (the reference worker's
+gates plus a calibrated max-abs bound).  ``cpu_baseline``: the reference
+algorithm (``oracle.golden``, the numpy restatement of ``moe_bench/verify.py:14-47``)
+on the whole layer on this host's cores.  ``--impl reference`` times only that CPU
+path (rank 0; other ranks exit 0), the same whole-layer run at every N.
 """
 from __future__ import annotations
 
@@ -153,27 +157,46 @@ def gemm1_flops(topk_ids, expert_map, inter_local: int, hidden: int) -> float:
     return 2.0 * pairs * 2 * inter_local * hidden
 
 
-def layer_flops(cfg, topk_ids, expert_map, world: int, parallel: str) -> float:
-    """Per-rank algorithmic FLOPs of the layer (routed + shared), unpadded."""
-    s = cfg.shape
-    ids = topk_ids.reshape(-1)
-    if parallel == "TP":
-        f = 6.0 * s.K * s.intermediate * ids.numel() / world
+def rank_work(layer, topk_ids, inter: int, shared_inter: int) -> dict:
+    """This rank's algorithmic work in one forward: FP8 FLOPs (routed pairs, unpadded, plus the
+    shared expert), the expert weight bytes it must stream from HBM, and its NVLink bytes
+    (all-gather received + reduce-scatter sent, bf16 partials) -- the three roofline terms.
+    ``inter`` / ``shared_inter``: this rank's unpadded intermediate widths."""
+    ids = topk_ids.reshape(-1).long()
+    H, I, P = layer.H, inter, layer.P
+    if layer.expert_map is None:
+        pairs = ids.numel()
+        hit = int(torch_unique_count(ids))
     else:
-        pairs = ids.numel() if expert_map is None else int((expert_map[ids.long()] >= 0).sum().item())
-        f = 6.0 * s.K * s.intermediate * pairs
-    if s.shared_experts:
-        tok = s.M_aligned(world) if parallel == "TP" else s.M_aligned(world) // world
-        f += 6.0 * s.K * s.shared_intermediate * tok / (world if parallel == "TP" else 1)
-    return f
+        local = layer.expert_map[ids] >= 0
+        pairs = int(local.sum().item())
+        hit = int(torch_unique_count(ids[local]))
+    flops = 6.0 * H * I * pairs
+    wbytes = hit * 3.0 * H * I * (1 + 4.0 / (128 * 128))
+    if layer.shared is not None:
+        Is = shared_inter
+        flops += 6.0 * H * Is * layer.shared.rows
+        wbytes += 3.0 * H * Is * (1 + 4.0 / (128 * 128))
+    ag = (P - 1) * layer.T_local * (H + 4 * H // 128)
+    rs = (P - 1) * layer.T_local * 2 * H
+    return {"flops": flops, "weight_bytes": wbytes, "nvlink_bytes": float(ag + rs), "ag_bytes": ag, "rs_bytes": rs,
+            "pairs": pairs, "experts_hit": hit}
+
+
+def torch_unique_count(t) -> int:
+    import torch
+    return int(torch.unique(t).numel()) if t.numel() else 0
 
 
 class CpuGolden:
     """The numpy restatement of the reference golden (``moe_bench/verify.py:14-47``) on this host.
 
-    Weights are held as bf16 bit patterns and widened per expert inside the loop,
-    as the reference golden does (``w1_bf16[expert].float()``); the sample is the
-    first ``n`` tokens of the same layer (every expert they route to is computed).
+    Weights are held as bf16 bit patterns and widened per expert inside the loop, as the
+    reference golden does (``w1_bf16[expert].float()``).  One run is the whole layer: all
+    T tokens of the workload.  The expert loop runs on every host core the process may use
+    (``golden_moe_threads``: whole experts per thread, BLAS single-threaded per thread when
+    there are enough experts to go round, else BLAS threads split the cores), whatever
+    thread limit the launcher set in the environment (torchrun sets OMP_NUM_THREADS=1).
     """
 
     def __init__(self, bundle):
@@ -193,28 +216,28 @@ class CpuGolden:
         self.ids = bundle.routing.topk_ids_full.cpu().numpy()
         self.wts = bundle.routing.topk_weights_full.cpu().numpy()
         self.cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+        hit = len(set(self.ids.reshape(-1).tolist()))
+        self.workers = max(1, min(self.cores, hit))
+        self.blas_threads = max(1, self.cores // self.workers)
 
-    def run(self, n: int) -> float:
+    def run(self) -> float:
+        from threadpoolctl import threadpool_limits
+
         from oracle import golden as ogolden
 
-        t0 = time.perf_counter()
-        ogolden.golden_moe(self.hid[:n], self.ids[:n], self.wts[:n], self.w1, self.w2, self.sw1, self.sw2)
-        return time.perf_counter() - t0
+        with threadpool_limits(limits=self.blas_threads, user_api="blas"):
+            t0 = time.perf_counter()
+            ogolden.golden_moe_threads(self.hid, self.ids, self.wts, self.w1, self.w2, self.sw1, self.sw2,
+                                       workers=self.workers)
+            return time.perf_counter() - t0
 
-    def calibrate(self, budget_s: float) -> int:
-        """Largest power-of-two token sample (>= 16) whose run fits the budget."""
-        n = min(16, self.hid.shape[0])
-        t = self.run(n)
-        while 2 * t < budget_s and n < self.hid.shape[0]:
-            n = min(self.hid.shape[0], n * 2)
-            t = self.run(n)
-        return n
-
-    def describe(self, n: int, runs: int, mean_t: float) -> dict:
+    def describe(self, runs: int, mean_t: float) -> dict:
+        n = self.hid.shape[0]
         return {"value": n / mean_t, "unit": "tokens/s", "cores": self.cores, "kind": "port",
-                "sample": f"first {n} of {self.hid.shape[0]} tokens through the full layer (numpy fp32 golden of "
-                          f"moe_bench/verify.py:14-47, BLAS threads = host cores); mean of {runs} run(s), "
-                          f"{mean_t:.2f} s each"}
+                "sample": f"the whole layer: all {n} tokens of the workload per run (numpy fp32 golden of "
+                          f"moe_bench/verify.py:14-47, per-expert bf16 widening inside the loop); {self.workers} "
+                          f"expert threads x {self.blas_threads} BLAS thread(s) on {self.cores} host cores; "
+                          f"mean of {runs} run(s), {mean_t:.2f} s each"}
 
 
 def run_reference(args) -> int:
@@ -229,12 +252,11 @@ def run_reference(args) -> int:
     cfg = configs.preset(preset, **over)
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     gold = CpuGolden(data.build_bundle(cfg, device=dev))
-    n = gold.calibrate(budget_s=min(15.0, 150.0 / max(1, args.steps + args.warmup)))
     for _ in range(args.warmup):
-        gold.run(n)
-    times = [gold.run(n) for _ in range(args.steps)]
+        gold.run()
+    times = [gold.run() for _ in range(args.steps)]
     mean_t = sum(times) / len(times)
-    cb = gold.describe(n, len(times), mean_t)
+    cb = gold.describe(len(times), mean_t)
     s = cfg.shape
     line = {"impl": "reference", "metric": "moe_layer_tokens_per_s", "value": cb["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean_t * 1e3,
@@ -273,11 +295,113 @@ def _max_over_ranks(d: dict, world: int, dev) -> dict:
     return dict(zip(d.keys(), v.tolist()))
 
 
-def _before_gemm1(starts, evs) -> float:
-    """Mean time (ms) from each step's start to its gate/up GEMM launch point."""
-    g = [ev for name, ev in evs if name == "gemm1_start"]
-    t = [a.elapsed_time(b) for a, b in zip(starts, g)]
-    return sum(t) / max(1, len(t))
+def _timed(fn, steps: int, warmup: int, flush, barrier, events=None):
+    """Per-step CUDA-event times (ms) of ``fn`` on the current stream: warm-up steps run
+    exactly what a timed step runs, the L2 flush sits between steps outside the events."""
+    import torch
+
+    for _ in range(warmup):
+        flush.zero_()
+        fn()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    s = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        s[i].record()
+        fn()
+        e[i].record()
+    torch.cuda.synchronize()
+    barrier()
+    return [a.elapsed_time(b) for a, b in zip(s, e)]
+
+
+def _mean_max_over_ranks(times: list[float], world: int, dev) -> float:
+    """Mean over steps of the per-step maximum over ranks (ms)."""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(times, dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.mean().item())
+
+
+def exchange_split(layer, bundle, x, ids, wts, args, flush, barrier, world, dev, fused_ms: float) -> dict | None:
+    """Exposed communication of the fused exchange and the fraction of it that is hidden.
+
+    * compute: this rank's shard of the layer run as a one-GPU layer (every token local,
+      no exchange: align, quant + dispatch, GEMM1, GEMM2, combine), plus its shared expert;
+    * comm: the exchange kernels of one step with no GEMM between them
+      (``P2PExchange.exchange_alone``: quantise + push + dispatch, combine + push + owner reduce);
+    * exposed = fused - compute; hidden fraction = 1 - exposed / comm.
+    All per-step maxima over ranks, means over steps."""
+    import torch
+
+    from td_benchmark_b200.layer import MoELayer, NullExchange
+
+    ex = layer.exchange
+    if getattr(ex, "name", "") != "p2p" or world == 1:
+        return None
+    solo = MoELayer(layer.w, layer.T, layer.top_k, layer.E, expert_map=layer.expert_map, shared=None,
+                    exchange=NullExchange(), device=layer.device)
+    x_all = bundle.hidden_full.to(dev).contiguous()
+    t_solo = _timed(lambda: solo.forward(x_all, ids, wts), args.steps, args.warmup, flush, barrier)
+    solo.check()
+    del solo
+    t_shared = [0.0] * args.steps
+    if layer.shared is not None:
+        t_shared = _timed(lambda: layer.shared.run(layer.status), args.steps, args.warmup, flush, barrier)
+    compute_ms = _mean_max_over_ranks([a + b for a, b in zip(t_solo, t_shared)], world, dev)
+    comm_ms = None
+    if ex.exchange_alone(layer, x, ids):
+        t_comm = _timed(lambda: ex.exchange_alone(layer, x, ids), args.steps, args.warmup, flush, barrier)
+        comm_ms = _mean_max_over_ranks(t_comm, world, dev)
+    layer.check()
+    exposed = fused_ms - compute_ms
+    out = {"fused_us": fused_ms * 1e3, "compute_us": compute_ms * 1e3, "exposed_comm_us": exposed * 1e3,
+           "comm_alone_us": None if comm_ms is None else comm_ms * 1e3,
+           "hidden_frac": None if not comm_ms else 1.0 - exposed / comm_ms,
+           "how": "compute = this rank's shard run as a one-GPU layer (no exchange) + its shared expert; comm = "
+                  "the exchange kernels of a step alone (P2PExchange.exchange_alone); exposed = fused - compute; "
+                  "hidden = 1 - exposed/comm; per-step max over ranks, mean over steps"}
+    return out
+
+
+def check_parity(layer, bundle, x, ids, wts, world, rank, dev) -> dict:
+    """One more regular forward, every rank's rows against the fp32 golden of the same tokens
+    (the reference worker's gates + max-abs <= 1.5 x calibrated activation-quant error)."""
+    import torch
+    import torch.distributed as dist
+
+    from td_benchmark_b200 import verify
+
+    out = layer.forward(x, ids, wts)
+    torch.cuda.synchronize()
+    layer.check()
+    r0, n = rank * layer.T_local, layer.T_local
+    hid = bundle.hidden_full[r0:r0 + n].to(dev)
+    rep = verify.check_layer(out, hid, ids[r0:r0 + n], wts[r0:r0 + n], bundle.ckpt)
+    v = torch.tensor([1.0 if rep["pass"] else 0.0, rep["cos_sim"], rep["rel_p99"], rep["max_abs"], rep["calib"],
+                      abs(rep["scale"] - 1.0), rep["max_abs"] / max(rep["max_abs_bound"], 1e-30)],
+                     dtype=torch.float64, device=dev)
+    if world > 1:
+        parts = [torch.empty_like(v) for _ in range(world)]
+        dist.all_gather(parts, v)
+        allv = torch.stack(parts)
+    else:
+        allv = v[None]
+    a = allv.cpu().tolist()
+    return {"pass": all(r[0] == 1.0 for r in a), "ranks": world, "cos_min": min(r[1] for r in a),
+            "rel_p99_max": max(r[2] for r in a), "max_abs_max": max(r[3] for r in a),
+            "calib_min": min(r[4] for r in a), "scale_dev_max": max(r[5] for r in a),
+            "max_abs_over_bound_max": max(r[6] for r in a),
+            "gates": "cos >= 0.995, masked rel_p99 <= 5, |scale-1| <= 0.05 (moe_bench/worker.py:108-110) and max_abs "
+                     "<= 1.5 x calib (calib = max |golden - golden without activation quant| on the same rows)",
+            "how": "after the timed runs: one regular forward; each rank's output rows vs the fp32 golden of its "
+                   "tokens computed on the device (td_benchmark_b200.verify)"}
 
 
 def main() -> int:
@@ -285,7 +409,7 @@ def main() -> int:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="mixtral", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="dsv3", choices=sorted(WORKLOADS))
     ap.add_argument("--tokens", type=int, default=None, help="override the workload's token count")
     ap.add_argument("--impl", default="b2m", choices=["b2m", "reference"])
     ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"],
@@ -298,6 +422,7 @@ def main() -> int:
     ap.add_argument("--chunks", type=int, default=4, help="down-GEMM column chunks of the copy-engine push")
     ap.add_argument("--ce-streams", type=int, default=2, help="side streams carrying the copy-engine push")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the post-run check against the fp32 golden")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -367,7 +492,6 @@ def main() -> int:
     layer.check()
     local = torch.tensor([s.elapsed_time(e) for s, e in zip(starts, ends)], dtype=torch.float64, device=dev)
     evs = layer.events
-    pre_g1 = _before_gemm1(starts, evs)
     stages = _max_over_ranks(_stages(starts, ends, evs), world, dev)
     g1 = []
     layer.events = None
@@ -388,46 +512,12 @@ def main() -> int:
         dist.all_gather_object(parts, clocks)
         clocks = ClockSampler.merge(parts)
 
-    # ---- exposed communication (fused exchange, N > 1): the same kernels on local data
-    # with every peer flag already satisfied and nothing sent; exposed = fused - that.
-    comm = None
-    if world > 1 and getattr(layer.exchange, "name", "") == "p2p":
-        layer.exchange.compute_only = True
-        for _ in range(args.warmup):
-            flush.zero_()
-            layer.forward(x, ids, wts)
-        torch.cuda.synchronize()
+    # ---- exposed communication and hidden fraction (fused exchange, N > 1)
+    comm = exchange_split(layer, bundle, x, ids, wts, args, flush, barrier, world, dev, ms)
+    if comm is not None:
+        comm["stages_us_max_over_ranks"] = {k: round(v, 1) for k, v in stages.items()}
         barrier()
-        c_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        c_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        layer.events = []
-        for i in range(args.steps):
-            flush.zero_()
-            c_s[i].record()
-            layer.forward(x, ids, wts)
-            c_e[i].record()
-        torch.cuda.synchronize()
-        c_pre_g1 = _before_gemm1(c_s, layer.events)
-        c_stages = _max_over_ranks(_stages(c_s, c_e, layer.events), world, dev)
-        layer.events = None
-        layer.exchange.compute_only = False
-        pre = torch.tensor([pre_g1, c_pre_g1], dtype=torch.float64, device=dev)
-        dist.all_reduce(pre, op=dist.ReduceOp.MAX)
-        pre_f, pre_c = (float(v) * 1e3 for v in pre.tolist())
-        c_local = torch.tensor([a.elapsed_time(b) for a, b in zip(c_s, c_e)], dtype=torch.float64, device=dev)
-        dist.all_reduce(c_local, op=dist.ReduceOp.MAX)
-        c_ms = float(c_local.mean().item())
-        H_ = cfg.shape.K
-        ag_bytes = (world - 1) * layer.T_local * (H_ + 4 * H_ // 128)
-        rs_bytes = (world - 1) * layer.T_local * H_ * 2
-        comm = {"compute_only_us": c_ms * 1e3, "fused_us": ms * 1e3, "exposed_comm_us": (ms - c_ms) * 1e3,
-                "exposed_all_gather_us": pre_f - pre_c, "exposed_reduce_scatter_us": (ms - c_ms) * 1e3 - (pre_f - pre_c),
-                "stages_us_max_over_ranks": {"fused": {k: round(v, 1) for k, v in stages.items()},
-                                             "compute_only": {k: round(v, 1) for k, v in c_stages.items()}},
-                "nvlink_bytes_per_rank": {"all_gather_in": ag_bytes, "reduce_scatter_out": rs_bytes},
-                "how": "same kernels with peer flags pre-satisfied and local data (no traffic); per-step max over ranks"}
-        barrier()
-        layer.forward(x, ids, wts)   # one regular step so every rank's epoch and buffers are in step again
+        layer.forward(x, ids, wts)   # one regular step so every rank's buffers are in step again
         torch.cuda.synchronize()
         barrier()
 
@@ -476,35 +566,22 @@ def main() -> int:
         out = layer.forward(x_d, ids_d, wts_d)
         out_h.copy_(out, non_blocking=True)
 
-    for _ in range(args.warmup):
-        flush.zero_()
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    for i in range(args.steps):
-        flush.zero_()
-        e_s[i].record()
-        e2e_step()
-        e_e[i].record()
-    torch.cuda.synchronize()
-    barrier()
-    e_local = torch.tensor([s.elapsed_time(e) for s, e in zip(e_s, e_e)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e_local, op=dist.ReduceOp.MAX)
-    e_serial_ms = float(e_local.mean().item())
+    e_serial_ms = _mean_max_over_ranks(_timed(e2e_step, args.steps, args.warmup, flush, barrier), world, dev)
     h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * 4 + wts_h.numel() * 4
     d2h = out_h.numel() * out_h.element_size()
 
-    # ---- roofline of GEMM1 on this rank
+    # ---- roofline: the dominant kernel (GEMM1) and the layer
     peaks = _peaks()
     fp8_peak = peaks.get("fp8_tflops")
-    peak_src = "measured (profiles/peaks.json)"
+    peak_src = "measured cuBLASLt FP8 8192^3 (profiles/peaks.json)"
     if not fp8_peak:
         fp8_peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
-        peak_src = "2 x measured bf16 (MEASURED_PEAKS.json); no FP8 measurement yet"
+        peak_src = "2 x measured bf16 (MEASURED_PEAKS.json); no FP8 measurement"
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    nvl_peak = peaks.get("nvlink_gbs")
+    nvl_src = peaks.get("nvlink_how", "profiles/peaks.json")
+    if not nvl_peak:
+        nvl_peak, nvl_src = 770.0, "peer copy per direction measured on this pool (profiling recipe figure)"
     g1_ms = sum(g1) / len(g1)
     f1 = gemm1_flops(ids, layer.expert_map, layer.w.inter, layer.H)
     achieved = f1 / (g1_ms * 1e-3) / 1e12
@@ -512,16 +589,38 @@ def main() -> int:
     tp = ROOT / "profiles" / "traffic.json"
     if tp.exists():
         traffic = json.loads(tp.read_text()).get(f"gemm1/{args.workload}/{world}")
-    lf = layer_flops(cfg, ids, layer.expert_map, world, spec.parallel)
+    s = cfg.shape
+    inter_alg = s.intermediate // world if spec.parallel == "TP" else s.intermediate
+    sh_alg = s.shared_intermediate // world if spec.parallel == "TP" else s.shared_intermediate
+    work = rank_work(layer, ids, inter_alg, sh_alg)
+    t_fp8 = work["flops"] / (fp8_peak * 1e12)
+    t_nvl = work["nvlink_bytes"] / (nvl_peak * 1e9)
+    t_hbm = work["weight_bytes"] / (hbm_peak * 1e9)
+    terms = torch.tensor([t_fp8, t_nvl, t_hbm, work["flops"]], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(terms, op=dist.ReduceOp.MAX)   # the most-loaded rank sets the layer time
+    t_fp8, t_nvl, t_hbm, fl_max = terms.tolist()
+    bound = max(t_fp8, t_nvl)
+    layer_roof = {"t_fp8_us": t_fp8 * 1e6, "t_nvlink_us": t_nvl * 1e6, "t_hbm_weights_us": t_hbm * 1e6,
+                  "bound_us": bound * 1e6, "bound_term": "fp8" if t_fp8 >= t_nvl else "nvlink",
+                  "frac": bound / (ms * 1e-3), "frac_incl_hbm": max(bound, t_hbm) / (ms * 1e-3),
+                  "flops_most_loaded_rank": fl_max, "nvlink_bytes_per_rank": work["nvlink_bytes"],
+                  "weight_bytes_per_rank": work["weight_bytes"], "fp8_peak_tflops": fp8_peak,
+                  "nvlink_peak_gbs": nvl_peak, "nvlink_peak_source": nvl_src, "hbm_peak_gbs": hbm_peak,
+                  "how": "per rank: FP8 FLOPs of routed (unpadded) pairs + shared expert / FP8 peak; all-gather "
+                         "received + reduce-scatter sent bytes / NVLink per-direction bandwidth; expert weight "
+                         "bytes / HBM; max over ranks; bound = max(fp8, nvlink) (BASELINE definition); frac = "
+                         "bound / measured layer time"}
+
+    # ---- parity of the benchmarked layer on every rank
+    parity = None if args.no_parity else check_parity(layer, bundle, x, ids, wts, world, rank, dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gold = CpuGolden(bundle)
-        n = gold.calibrate(budget_s=15.0)
-        cpu = gold.describe(n, 1, gold.run(n))
+        cpu = gold.describe(1, gold.run())
 
     if rank == 0:
-        s = cfg.shape
         line = {
             "metric": "moe_layer_tokens_per_s", "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3,
@@ -530,8 +629,9 @@ def main() -> int:
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp8-e4m3 (fp32 accum)",
             "data": "synthetic (seeded, BASELINE value distributions)",
             "config": {"workload": label, "tokens": T, "hidden": s.K, "intermediate": s.intermediate,
-                       "experts": s.E, "top_k": s.top_k, "parallelism": f"{spec.parallel.lower()}{world}",
-                       "scheme": code, "shard_level": level, "routing": cfg.routing.imbalance_kind,
+                       "experts": s.E, "top_k": s.top_k, "shared_experts": s.shared_experts,
+                       "parallelism": f"{spec.parallel.lower()}{world}", "scheme": code, "shard_level": level,
+                       "routing": cfg.routing.imbalance_kind,
                        "exchange": (f"p2p ag={layer.exchange.ag_mode} rs={args.rs_mode} "
                                     f"chunks={len(layer.exchange.chunk_cols)}"
                                     if getattr(layer.exchange, "name", "") == "p2p" else
@@ -546,8 +646,8 @@ def main() -> int:
             "roofline": {"bound": "tensor", "kernel": "gemm1 (gate/up, tcgen05 kind::f8f6f4)",
                          "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s", "frac": achieved / fp8_peak,
                          "peak_source": peak_src, "traffic": traffic, "gemm1_ms": g1_ms,
-                         "layer_tflops": lf / (ms * 1e-3) / 1e12,
-                         "layer_frac_of_fp8_peak": lf / (ms * 1e-3) / 1e12 / fp8_peak},
+                         "gemm1_flops_per_launch": f1, "layer": layer_roof},
+            "parity": parity,
             "clocks": clocks,
             "comm": comm,
             "cpu_baseline": cpu,

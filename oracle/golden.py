@@ -63,6 +63,38 @@ def golden_moe(hidden: np.ndarray, topk_ids: np.ndarray, topk_weights: np.ndarra
     return out
 
 
+def golden_moe_threads(hidden: np.ndarray, topk_ids: np.ndarray, topk_weights: np.ndarray,
+                       w1: np.ndarray, w2: np.ndarray,
+                       shared_w1: np.ndarray | None = None, shared_w2: np.ndarray | None = None,
+                       workers: int = 1) -> np.ndarray:
+    """``golden_moe`` with the per-expert work spread over ``workers`` host threads.
+
+    Same steps as ``golden_moe`` (the expert loop of ``moe_bench/verify.py:29-41``,
+    including the per-expert widening of bf16 weights); each worker computes whole
+    experts and the results are added into the output in ascending expert order, as
+    the serial loop does.  numpy releases the GIL inside its array kernels and BLAS,
+    so the threads run in parallel.  Used to time the reference algorithm on all host
+    cores (with BLAS itself single-threaded per worker by the caller)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    hidden = np.asarray(hidden, dtype=np.float32)
+    ids = np.asarray(topk_ids)
+    wts = np.asarray(topk_weights, dtype=np.float32)
+    experts = [e for e in range(w1.shape[0]) if np.any(ids == e)]
+
+    def one(e: int):
+        rows, slots = np.nonzero(ids == e)
+        return rows, _ffn(hidden[rows], w1[e], w2[e], True) * wts[rows, slots][:, None]
+
+    out = np.zeros((hidden.shape[0], w2.shape[1]), dtype=np.float32)
+    with ThreadPoolExecutor(max_workers=max(1, workers)) as pool:
+        for rows, y in pool.map(one, experts):
+            np.add.at(out, rows, y)
+    if shared_w1 is not None and shared_w2 is not None:
+        out = out + _ffn(hidden, shared_w1[0], shared_w2[0], True)
+    return out
+
+
 def compare_outputs(actual: np.ndarray, expected: np.ndarray, atol: float = 0.2, rtol: float = 0.0,
                     cos_threshold: float | None = None, rel_p99_threshold: float | None = None,
                     scale_tolerance: float | None = None) -> dict:

@@ -20,6 +20,10 @@ uint64_t timeout_ns();
 // B2M_OK when the current device is sm_100 (cached per device).
 int require_sm100(int* num_sms);
 
+// Driver API entry point by name, resolved once per process (thread-safe).  The CUDA
+// runtime is linked statically, so driver calls it does not wrap are reached this way.
+int driver_entry(const char* name, void** fn);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace b2m

@@ -3,7 +3,9 @@
 #include <stdio.h>
 
 #include <atomic>
+#include <map>
 #include <mutex>
+#include <string>
 
 #include "b2m_host.h"
 
@@ -45,6 +47,24 @@ int require_sm100(int* num_sms) {
     return fail(B2M_ERR_UNSUPPORTED, "b2m kernels need an sm_100 GPU (B200); device %d is sm_%d", dev,
                 cached_major[dev]);
   if (num_sms) *num_sms = cached_sms[dev];
+  return B2M_OK;
+}
+
+int driver_entry(const char* name, void** fn) {
+  static std::mutex mu;
+  static std::map<std::string, void*> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(name);
+  if (it != cache.end()) {
+    *fn = it->second;
+    return B2M_OK;
+  }
+  cudaDriverEntryPointQueryResult q;
+  void* p = nullptr;
+  B2M_TRY(check_cuda(cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q), "cudaGetDriverEntryPoint"));
+  if (q != cudaDriverEntryPointSuccess || !p) return fail(B2M_ERR_UNSUPPORTED, "%s not available from the driver", name);
+  cache.emplace(name, p);
+  *fn = p;
   return B2M_OK;
 }
 

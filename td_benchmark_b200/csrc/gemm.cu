@@ -45,6 +45,8 @@
 // site in dev_status, drains its own copies and MMAs and frees TMEM before returning.
 #include <cudaTypedefs.h>
 
+#include <atomic>
+
 #include "b2m_common.cuh"
 #include "b2m_host.h"
 
@@ -191,7 +193,7 @@ __device__ __forceinline__ bool wait_block_sources(const GemmParams& p, int mb, 
   int ok = 1;
   if (lane == 0) {
     for (int src = lo; src <= hi && ok; ++src) {
-      if (src < 0 || src >= 32 || (ready >> src) & 1u) continue;
+      if (src < 0 || src >= 32 || (ready >> src) & 1u) continue;  // the host bounds sources to 8
       if (!wait_flag_geq(p.src_flags + src, p.src_epoch, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_PEER)) {
         ok = 0;
         *abort = 1;
@@ -926,16 +928,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 // ------------------------------------------------------------------ host side
 int encode_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
                   uint32_t box_inner, uint32_t box_outer) {
-  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-  if (!encode) {
-    cudaDriverEntryPointQueryResult q;
-    void* fn = nullptr;
-    B2M_TRY(check_cuda(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q),
-                       "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)"));
-    if (q != cudaDriverEntryPointSuccess || !fn)
-      return fail(B2M_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled not available from the driver");
-    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  }
+  void* fn = nullptr;
+  B2M_TRY(driver_entry("cuTensorMapEncodeTiled", &fn));
+  const auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {row_bytes};
   const cuuint32_t box[2] = {box_inner, box_outer};
@@ -949,21 +944,44 @@ int encode_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t o
   return B2M_OK;
 }
 
+// Per-device "dynamic shared memory attribute set" flags (the call is idempotent; the
+// atomics only make concurrent first calls well defined).
+template <typename Kernel>
+int ensure_smem_attr(std::atomic<bool> (&done)[64], Kernel kernel, size_t bytes, const char* what) {
+  int dev = 0;
+  B2M_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  if (dev >= 0 && dev < 64 && done[dev].load(std::memory_order_acquire)) return B2M_OK;
+  B2M_TRY(check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)),
+                     what));
+  if (dev >= 0 && dev < 64) done[dev].store(true, std::memory_order_release);
+  return B2M_OK;
+}
+
 template <bool kGateUp>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int num_sms, cudaStream_t s) {
   // num_sms here is the CTA budget (all SMs, or fewer when the caller keeps SMs for comm kernels)
-  static int attr_done[64] = {0};
-  int dev = 0;
-  B2M_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    B2M_TRY(check_cuda(cudaFuncSetAttribute(moe_gemm_kernel<kGateUp>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(SMEM_BYTES)),
-                       "gemm: cudaFuncSetAttribute"));
-    attr_done[dev] = 1;
-  }
+  static std::atomic<bool> attr_done[64];
+  B2M_TRY(ensure_smem_attr(attr_done, moe_gemm_kernel<kGateUp>, SMEM_BYTES, "gemm: cudaFuncSetAttribute"));
   int64_t upper = static_cast<int64_t>(p.max_blocks) * p.num_nt;
   int grid = static_cast<int>(upper < num_sms ? upper : num_sms);
   if (grid < 1) grid = 1;
+  if (p.push_world > 1) {
+    // The grid both waits for the peers' flags (producer) and publishes this rank's flags
+    // once every CTA's pusher warps are done: all CTAs must be resident together, or
+    // resident CTAs could wait on peers whose flags need this rank's unscheduled CTAs.
+    // A cooperative launch guarantees co-residency (one CTA per SM, grid <= SMs).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, moe_gemm_kernel<kGateUp>, ma, mb, p), "gemm1 push (cooperative) launch");
+  }
   moe_gemm_kernel<kGateUp><<<grid, NUM_THREADS, SMEM_BYTES, s>>>(ma, mb, p);
   return check_cuda(cudaGetLastError(), kGateUp ? "gemm1 launch" : "gemm2 launch");
 }
@@ -971,16 +989,8 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& 
 template <bool kGateUp>
 int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, const int32_t* block_pairs,
                      int num_sms, cudaStream_t s) {
-  static int attr_done[64] = {0};
-  int dev = 0;
-  B2M_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    B2M_TRY(check_cuda(cudaFuncSetAttribute(moe_gemm_pair_kernel<kGateUp>,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(PSMEM_BYTES)),
-                       "gemm pair: cudaFuncSetAttribute"));
-    attr_done[dev] = 1;
-  }
+  static std::atomic<bool> attr_done[64];
+  B2M_TRY(ensure_smem_attr(attr_done, moe_gemm_pair_kernel<kGateUp>, PSMEM_BYTES, "gemm pair: cudaFuncSetAttribute"));
   int64_t upper = static_cast<int64_t>(p.max_blocks) * p.num_nt;  // pairs <= blocks
   int64_t clusters = num_sms / 2;
   if (upper < clusters) clusters = upper;
@@ -1057,6 +1067,11 @@ int gemm1_impl(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, i
     if (!sw->block_order || !sw->sorted_ids || !sw->flags || sw->top_k < 1 || sw->tokens_per_src < 1 ||
         sw->numel < 0 || sw->numel >= INT32_MAX)
       return fail(B2M_ERR_ARG, "gemm1_wait: block_order, sorted_ids and flags are required; top_k, tokens_per_src >= 1");
+    // Every source rank of a row must have a flag the producer waits on (at most 8 ranks).
+    const int64_t tokens = (sw->numel + sw->top_k - 1) / sw->top_k;
+    if ((tokens + sw->tokens_per_src - 1) / sw->tokens_per_src > 8)
+      return fail(B2M_ERR_ARG, "gemm1_wait: %lld tokens / %lld per source is more than 8 source ranks",
+                  (long long)tokens, (long long)sw->tokens_per_src);
     p.block_order = sw->block_order;
     p.sorted_ids = sw->sorted_ids;
     p.numel = static_cast<int32_t>(sw->numel);

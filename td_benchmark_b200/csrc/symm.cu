@@ -359,17 +359,9 @@ static __device__ __align__(256) int32_t g_push_scratch[kPushScratchInts];
 // work on the stream, preceded by a fence with the effect of __threadfence_system, and
 // executed by the GPU front end rather than by an SM.
 int stream_write_fn(PFN_cuStreamWriteValue32_v11070* out) {
-  static PFN_cuStreamWriteValue32_v11070 fn = nullptr;
-  if (!fn) {
-    cudaDriverEntryPointQueryResult q;
-    void* p = nullptr;
-    B2M_TRY(check_cuda(cudaGetDriverEntryPoint("cuStreamWriteValue32", &p, cudaEnableDefault, &q),
-                       "cudaGetDriverEntryPoint(cuStreamWriteValue32)"));
-    if (q != cudaDriverEntryPointSuccess || !p)
-      return fail(B2M_ERR_UNSUPPORTED, "cuStreamWriteValue32 not available from the driver");
-    fn = reinterpret_cast<PFN_cuStreamWriteValue32_v11070>(p);
-  }
-  *out = fn;
+  void* p = nullptr;
+  B2M_TRY(driver_entry("cuStreamWriteValue32", &p));
+  *out = reinterpret_cast<PFN_cuStreamWriteValue32_v11070>(p);
   return B2M_OK;
 }
 
@@ -452,20 +444,37 @@ int b2m_copy2d_async(void* dst, int64_t dpitch, const void* src, int64_t spitch,
                     "copy2d_async: cudaMemcpy2DAsync");
 }
 
+}  // extern "C"
+
+namespace b2m {
+namespace {
+// Argument checks of b2m_quant_push other than the counter (shared with the no-alloc variant).
+int check_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world, void* const* q_dst,
+                     void* const* s_dst, uint32_t* const* flag_dst, const char* who) {
+  if (world < 1 || world > kMaxWorld) return fail(B2M_ERR_ARG, "%s: world=%d outside [1, 8]", who, world);
+  if (rows <= 0 || hidden <= 0 || hidden % 128 || ldx < hidden || ldx % 8 || !x || !aligned16(x) || !q_dst ||
+      !s_dst || !flag_dst)
+    return fail(B2M_ERR_ARG, "%s: bad shape/pointers (hidden %% 128 == 0, 16-byte rows)", who);
+  for (int r = 0; r < world; ++r)
+    if (!q_dst[r] || !s_dst[r] || !flag_dst[r]) return fail(B2M_ERR_ARG, "%s: null peer pointer %d", who, r);
+  return B2M_OK;
+}
+}  // namespace
+}  // namespace b2m
+
+extern "C" {
+
 int b2m_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world, void* const* q_dst,
                    void* const* s_dst, int64_t row0, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
                    void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
-  if (world < 1 || world > kMaxWorld) return fail(B2M_ERR_ARG, "quant_push: world=%d outside [1, 8]", world);
-  if (rows <= 0 || hidden <= 0 || hidden % 128 || ldx < hidden || ldx % 8 || !x || !aligned16(x) || !counter ||
-      !q_dst || !s_dst || !flag_dst)
-    return fail(B2M_ERR_ARG, "quant_push: bad shape/pointers (hidden %% 128 == 0, 16-byte rows)");
+  B2M_TRY(check_quant_push(x, rows, hidden, ldx, world, q_dst, s_dst, flag_dst, "quant_push"));
+  if (!counter) return fail(B2M_ERR_ARG, "quant_push: null counter");
   PeerPtrs q{}, s{};
   FlagPtrs f{};
   for (int r = 0; r < world; ++r) {
-    if (!q_dst[r] || !s_dst[r] || !flag_dst[r]) return fail(B2M_ERR_ARG, "quant_push: null peer pointer %d", r);
     q.p[r] = q_dst[r];
     s.p[r] = s_dst[r];
     f.p[r] = flag_dst[r];
@@ -484,7 +493,10 @@ int b2m_quant_push_noalloc(const void* x, int64_t rows, int64_t hidden, int64_t 
   if (world < 1 || world > kMaxWorld)
     return fail(B2M_ERR_ARG, "quant_push_noalloc: world=%d outside [1, %d]", world, kMaxWorld);
   // The scratch need is one counter whatever rows/hidden are, so no problem size can
-  // outgrow the static array; the peer table bounds world (checked above).
+  // outgrow the static array; the peer table bounds world (checked above).  Every other
+  // argument is checked before anything is enqueued, so a rejected call leaves the
+  // caller's stream untouched.
+  B2M_TRY(check_quant_push(x, rows, hidden, ldx, world, q_dst, s_dst, flag_dst, "quant_push_noalloc"));
   int32_t* counter = nullptr;
   B2M_TRY(require_sm100(nullptr));
   B2M_TRY(push_scratch_ptr(&counter));

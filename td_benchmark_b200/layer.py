@@ -268,9 +268,6 @@ class P2PExchange:
         self.chunks_req = chunks if rs_mode == "ce" else 1
         self.rs_mode = rs_mode
         self.ce_streams = max(1, ce_streams)
-        # Diagnostic only (bench's exposed-communication split): run the same kernels on
-        # local data with every peer flag treated as already set and nothing sent.
-        self.compute_only = False
 
     def setup(self, layer: "MoELayer") -> None:
         from .symm import SymmetricWorkspace, ptr_array
@@ -356,8 +353,6 @@ class P2PExchange:
     def gather_dispatch(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
         from . import _lib
 
-        if self.compute_only:
-            return self._gather_dispatch_local(layer, x_local)
         self.epoch += 1
         st = ops._stream(layer.device)
         Tl, H = layer.T_local, layer.H
@@ -428,28 +423,14 @@ class P2PExchange:
         if self.ag_mode != "push":
             return False
         r, Tl, k, P = layer.route, layer.T_local, layer.top_k, self.world_size
-        push = not self.compute_only        # compute-only: same GEMM, nothing sent, waits satisfied
         _lib.call("b2m_gemm1_wait", layer.a_sorted.data_ptr(), layer.as_t.data_ptr(), r.rows_cap, layer.H,
                   layer.w.w1i.data_ptr(), layer.w.w1i_scale.data_ptr(), layer.w.num_experts, layer.w.inter,
                   r.expert_ids.data_ptr(), r.ntpp.data_ptr(), self.block_order.data_ptr(), r.sorted_ids.data_ptr(),
-                  layer.numel, k, Tl, self.ag_flags, self.epoch if push else 0,
-                  r.pair_pos.data_ptr() + 4 * self.rank * Tl * k if push else None, Tl * k,
-                  self._a_dst if push else None, self._as_dst if push else None, self._ag_dst if push else None,
-                  self.push_counters if push else None, P, self.rank, layer.inter_q.data_ptr(),
-                  layer.inter_st.data_ptr(), layer.status.data_ptr(), ops._stream(layer.device))
+                  layer.numel, k, Tl, self.ag_flags, self.epoch, r.pair_pos.data_ptr() + 4 * self.rank * Tl * k,
+                  Tl * k, self._a_dst, self._as_dst, self._ag_dst, self.push_counters, P, self.rank,
+                  layer.inter_q.data_ptr(), layer.inter_st.data_ptr(), layer.status.data_ptr(),
+                  ops._stream(layer.device))
         return True
-
-    def _gather_dispatch_local(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
-        if self.ag_mode == "push":
-            self._push_own(layer, x_local, 0)
-            return
-        r0 = self.rank * layer.T_local
-        ops.quant_g128(x_local, layer.xq[r0:r0 + layer.T_local], layer.xs[r0:r0 + layer.T_local])
-        if layer.shared is not None and layer.ep:
-            layer.shared.load_rows(layer.xq[r0:r0 + layer.T_local], layer.xs[r0:r0 + layer.T_local])
-        ops.dispatch_rows(layer.xq, layer.xs, layer.route.pair_pos, layer.top_k, layer.a_sorted, layer.as_t)
-        if layer.shared is not None and not layer.ep:
-            layer.shared.load_rows(layer.xq, layer.xs)
 
     def _gemm2_scatter(self, layer: "MoELayer", topk_weights, dst) -> None:
         from . import _lib
@@ -470,37 +451,9 @@ class P2PExchange:
                   self.rs_flags, self.world_size, epoch, None if add is None else add.data_ptr(),
                   layer.out_local.data_ptr(), layer.status.data_ptr(), ops._stream(layer.device))
 
-    def _down_and_scatter_local(self, layer: "MoELayer", topk_weights, ids, shared_out) -> torch.Tensor:
-        from . import _lib
-
-        if self.rs_mode == "gemm":
-            # every owner pointer is the own receive buffer: rows of other owners land in
-            # (and overwrite) own rows -- a timing stand-in that sends nothing
-            self._gemm2_scatter(layer, topk_weights, self._local_recv_dst())
-            layer._event("gemm2_end")
-            layer._event("combine_end")
-            add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
-            layer._event("shared_end")
-            self._rs_combine(layer, add, 0)
-            return layer.out_local
-
-        layer.gemm2(topk_weights)
-        layer._event("gemm2_end")
-        st = ops._stream(layer.device)
-        ops.combine(layer.staged, layer.top_k, ids, layer.expert_map, shared_out, self.slots)
-        layer._event("combine_end")
-        add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
-        layer._event("shared_end")
-        _lib.call("b2m_rs_reduce", self.slots.data_ptr(), layer.T_local, layer.H, self.world_size, 1,
-                  self.rs_flags, 0, None if add is None else add.data_ptr(), layer.out_local.data_ptr(),
-                  layer.status.data_ptr(), st)
-        return layer.out_local
-
     def down_and_scatter(self, layer: "MoELayer", topk_weights, ids, shared_out) -> torch.Tensor:
         from . import _lib
 
-        if self.compute_only:
-            return self._down_and_scatter_local(layer, topk_weights, ids, shared_out)
         compute = torch.cuda.current_stream(layer.device)
         P, Tl, H = self.world_size, layer.T_local, layer.H
         idsp = None if ids is None else ids.data_ptr()
@@ -548,12 +501,30 @@ class P2PExchange:
                   compute.cuda_stream)
         return layer.out_local
 
-    def _local_recv_dst(self):
-        from .symm import ptr_array
+    def exchange_alone(self, layer: "MoELayer", x_local: torch.Tensor, topk_ids: torch.Tensor) -> bool:
+        """The all-gather and the reduce-scatter of one forward with no GEMM between them.
 
-        if getattr(self, "_local_dst", None) is None:
-            self._local_dst = ptr_array([self.ws.local("recv")] * self.world_size)
-        return self._local_dst
+        Runs exactly the exchange kernels of ``forward`` -- quantise + push to every peer +
+        dispatch as each source arrives, then combine + push of the staged rows to their
+        owners + the owner reduce -- so a caller can time the communication of a step by
+        itself (the reference's T_comm).  The staged rows are those of the last forward;
+        the result lands in the layer's output buffer and is not meaningful.  Only for the
+        SM / copy-engine all-gather with the SM reduce-scatter; returns False otherwise."""
+        from . import _lib
+
+        if self.ag_mode not in ("sm", "ce") or self.rs_mode != "sm":
+            return False
+        self.gather_dispatch(layer, x_local)
+        compute = torch.cuda.current_stream(layer.device)
+        emap = None if layer.expert_map is None else layer.expert_map.data_ptr()
+        idsp = topk_ids.data_ptr() if layer.ep else None
+        _lib.call("b2m_combine_push", layer.staged.data_ptr(), layer.T, layer.top_k, layer.H, 0, layer.H, idsp, emap,
+                  None, self.world_size, self.rank, self._slot_dst, self._rs_dst, self.epoch, self.counters + 4, 0,
+                  compute.cuda_stream)
+        self._join_side(compute)
+        _lib.call("b2m_rs_reduce", self.slots.data_ptr(), layer.T_local, layer.H, self.world_size, 1, self.rs_flags,
+                  self.epoch, None, layer.out_local.data_ptr(), layer.status.data_ptr(), compute.cuda_stream)
+        return True
 
     def extra_launches(self) -> int:
         """Kernels per forward beyond align, quant(+push), dispatch, GEMM1, GEMM2, combine(+push)."""

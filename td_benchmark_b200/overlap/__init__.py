@@ -23,17 +23,29 @@ from typing import Any, Optional
 
 import torch
 
-from ..layer import ExpertWeights, MoELayer, NcclExchange, NullExchange
+from ..layer import ExpertWeights, MoELayer, NcclExchange, NullExchange, P2PExchange
 
 __all__ = ["MoEOverlapState", "moe_forward_overlap_fp8ag"]
 
 
 @dataclass
 class MoEOverlapState:
+    """Per-model state of the overlap entry points (``overlap_forward.py:61-97``).
+
+    ``exchange`` picks how the ranks of ``tp_group`` exchange tokens and partials:
+    ``"p2p"`` (default) the fused all-gather / reduce-scatter through NVLink peer memory
+    (``P2PExchange``), ``"nccl"`` NCCL collectives (the unfused comparison).  With one
+    rank there is no exchange.  ``n_chunks_*`` are kept for interface parity: the b2m
+    path does not split the GEMMs into stream-level chunks."""
     n_chunks_gateup: int = 4
     n_chunks_down: int = 4
     tp_group: Any = field(default=None, repr=False)
+    exchange: str = "p2p"
     _layers: dict = field(default_factory=dict, repr=False, init=False)
+
+    def __post_init__(self) -> None:
+        if self.exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange={self.exchange!r} must be 'p2p' or 'nccl'")
 
     @property
     def tp_size(self) -> int:
@@ -47,7 +59,15 @@ class MoEOverlapState:
         """Kept for interface parity; the b2m path orders all work on the caller's stream."""
 
     def release(self) -> None:
+        """Free every prepared layer (collective with P2P exchanges: all ranks call it)."""
+        for layer in self._layers.values():
+            layer.close()
         self._layers.clear()
+
+    def make_exchange(self):
+        if self.tp_size == 1:
+            return NullExchange()
+        return P2PExchange(self.tp_group) if self.exchange == "p2p" else NcclExchange(self.tp_group)
 
 
 def _as_expert_weights(shared_mlp: Any) -> Optional[ExpertWeights]:
@@ -83,9 +103,9 @@ def moe_forward_overlap_fp8ag(state: MoEOverlapState, hidden_states: torch.Tenso
     layer = state._layers.get(key)
     if layer is None:
         weights = ExpertWeights.prepare(w1, w1_scale, w2, w2_scale)
-        exchange = NcclExchange(state.tp_group) if P > 1 else NullExchange()
         layer = MoELayer(weights, tokens, top_k, global_num_experts, expert_map=expert_map,
-                         shared=_as_expert_weights(shared_mlp), exchange=exchange, device=hidden_states.device)
+                         shared=_as_expert_weights(shared_mlp), exchange=state.make_exchange(),
+                         device=hidden_states.device)
         state._layers[key] = layer
     ids = topk_ids[:tokens].to(torch.int32).contiguous()
     wts = topk_weights[:tokens].to(torch.float32).contiguous()

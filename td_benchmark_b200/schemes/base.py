@@ -64,40 +64,63 @@ class SchemeInstance:
 BuilderFn = Callable[[Any, Any, Any, Any], SchemeInstance]
 
 
+def _conforms(expected: type, value: Any) -> bool:
+    """Type rule of a tunable: a bool tunable takes only True/False, and no other type
+    takes a bool (``True`` is not a chunk count, although ``bool`` subclasses ``int``)."""
+    is_bool = isinstance(value, bool)
+    if expected is bool:
+        return is_bool
+    return not is_bool and isinstance(value, expected)
+
+
 def validate_tunables(spec: SchemeSpec, provided: dict[str, Any]) -> dict[str, Any]:
-    unknown = sorted(set(provided) - set(spec.tunables_schema))
-    if unknown:
-        raise SchemeConfigError(f"{spec.code} tunables {unknown} violate schema: allowed keys are "
-                                f"{sorted(spec.tunables_schema)}")
-    values = {name: item.default for name, item in spec.tunables_schema.items()}
-    values.update(provided)
-    for name, value in values.items():
-        expected = spec.tunables_schema[name].typ
-        ok = isinstance(value, bool) if expected is bool else (isinstance(value, expected) and
-                                                                not isinstance(value, bool))
-        if not ok:
-            raise SchemeConfigError(f"{spec.code}.{name}={value!r} violates schema: expected {expected.__name__}")
-    return values
+    """Schema defaults overlaid with ``provided``, checked key by key in schema order.
+
+    Unknown keys, then the first value of the wrong type, raise ``SchemeConfigError``
+    with the message texts of the reference contract (``moe_bench/schemes/base.py:48-62``).
+    """
+    schema = spec.tunables_schema
+    extra = [key for key in provided if key not in schema]
+    if extra:
+        raise SchemeConfigError(f"{spec.code} tunables {sorted(extra)} violate schema: allowed keys are "
+                                f"{sorted(schema)}")
+    resolved: dict[str, Any] = {}
+    for key, item in schema.items():
+        value = provided[key] if key in provided else item.default
+        if not _conforms(item.typ, value):
+            raise SchemeConfigError(f"{spec.code}.{key}={value!r} violates schema: expected {item.typ.__name__}")
+        resolved[key] = value
+    return resolved
+
+
+# SchemeSpec fields copied into every instance's diagnostics (the results row reads them).
+_DIAGNOSTIC_FIELDS = ("name", "family", "parallel", "weight_dtype", "act_quant", "requires_nvshmem")
+
+
+def _no_op() -> None:
+    return None
 
 
 def make_lazy_instance(spec: SchemeSpec, tunables: dict[str, Any], run_impl: Callable[[], Any],
                        diagnostics: dict[str, Any] | None = None,
                        close_impl: Callable[[], None] | None = None,
                        staged_impl: Callable[[], StageResult] | None = None) -> SchemeInstance:
-    diag = {
-        "scheme": spec.code, "name": spec.name, "family": spec.family, "parallel": spec.parallel,
-        "weight_dtype": spec.weight_dtype, "act_quant": spec.act_quant,
-        "requires_nvshmem": spec.requires_nvshmem, "tunables": tunables,
-    }
-    if diagnostics:
-        diag.update(diagnostics)
+    """Wrap a prepared forward as a ``SchemeInstance``.
 
-    def run_staged() -> StageResult:
-        return StageResult(output=run_impl(), stage_ms={})
-
-    return SchemeInstance(run=run_impl, run_staged=staged_impl or run_staged, diagnostics=diag,
-                          close=close_impl or (lambda: None))
+    The diagnostics dict carries the scheme code, the spec's descriptive fields and the
+    resolved tunables, then any scheme-specific entries (which may override them).
+    Without ``staged_impl`` the staged run is the plain run with no stage times.
+    """
+    diag: dict[str, Any] = {"scheme": spec.code}
+    diag.update((f, getattr(spec, f)) for f in _DIAGNOSTIC_FIELDS)
+    diag["tunables"] = tunables
+    diag.update(diagnostics or {})
+    if staged_impl is None:
+        def staged_impl() -> StageResult:
+            return StageResult(output=run_impl(), stage_ms={})
+    return SchemeInstance(run=run_impl, run_staged=staged_impl, diagnostics=diag, close=close_impl or _no_op)
 
 
 def missing_dependency(message: str) -> None:
+    """A scheme whose runtime dependency is absent fails with RuntimeError (the reference's rule)."""
     raise RuntimeError(message)

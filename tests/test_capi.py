@@ -51,3 +51,14 @@ def test_argument_validation_message():
         pytest.skip("libb2m.so not built")
     with pytest.raises(_lib.B2MError, match="timeout"):
         _lib.call("b2m_set_timeout_ns", 10)
+
+
+def test_noalloc_push_validates_before_touching_the_device():
+    """Argument errors of the allocation-free push come back without a GPU (nothing is enqueued)."""
+    if not _lib.LIB_PATH.exists():
+        pytest.skip("libb2m.so not built")
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("has a GPU")
+    with pytest.raises(_lib.B2MError, match="quant_push_noalloc: bad shape"):
+        _lib.call("b2m_quant_push_noalloc", 16, 8, 100, 128, 1, None, None, 0, None, 1, None)

@@ -134,3 +134,17 @@ def test_host_pipeline_matches_direct_forward():
     assert layer.forward(xs[2], ids, wts, out=out_dev) is out_dev and torch.equal(out_dev, want[2])
     with pytest.raises(ValueError):
         layer.forward(xs[0], ids, wts, out=torch.empty(3, dtype=torch.bfloat16, device=DEV))
+
+
+@pytest.mark.parametrize("name", ["mixtral", "dsv3"])
+def test_benchmarked_full_shapes_vs_golden(name):
+    """The shapes bench.py times at N=1: Mixtral T=4096 (TP1) and DeepSeek-V3 T=8192 with Zipf
+    routing and the shared expert (EP1), against the device fp32 golden of the package's
+    verification step (the worker's gates + max-abs <= 1.5 x calibrated act-quant error)."""
+    from td_benchmark_b200 import verify
+
+    cfg = configs.preset(name)
+    bundle, out = _run_scheme(cfg, "d2" if cfg.parallel == "EP" else "d1")
+    rep = verify.check_layer(out, bundle.hidden_full, bundle.routing.topk_ids_full, bundle.routing.topk_weights_full,
+                             bundle.ckpt)
+    assert rep["pass"], rep

@@ -149,3 +149,18 @@ def test_align_expert_map_marks_non_local():
     s2, e2, n2 = _align_loop(ids, 8, E, emap)
     assert np.array_equal(e, e2) and np.array_equal(s, s2)
     assert set(e[e >= 0].tolist()) <= {0, 1, 2, 3}
+
+
+def test_threaded_golden_equals_serial_golden():
+    """The threaded expert loop (used to time the CPU baseline) computes the same layer."""
+    from oracle import golden as og
+    rng = np.random.default_rng(5)
+    T, H, I, E, k = 48, 256, 256, 6, 2
+    h = rng.standard_normal((T, H)).astype(np.float32)
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    w = rng.random((T, k)).astype(np.float32)
+    w1 = (0.05 * rng.standard_normal((E, 2 * I, H))).astype(np.float32)
+    w2 = (0.05 * rng.standard_normal((E, H, I))).astype(np.float32)
+    a = og.golden_moe(h, ids, w, w1, w2)
+    b = og.golden_moe_threads(h, ids, w, w1, w2, workers=4)
+    np.testing.assert_allclose(b, a, rtol=1e-5, atol=1e-6)

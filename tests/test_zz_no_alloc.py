@@ -59,3 +59,15 @@ def test_noalloc_push_rejects_world_beyond_limit():
     with pytest.raises(_lib.B2MError, match="world=9"):
         _lib.call("b2m_quant_push_noalloc", x.data_ptr(), 8, 128, 128, 9, ptrs, ptrs, 0, ptrs, 1,
                   torch.cuda.current_stream(DEV).cuda_stream)
+
+
+def test_noalloc_push_rejects_bad_shape_before_enqueueing():
+    """A bad shape is refused by the argument checks, before the scratch counter is cleared."""
+    x = torch.zeros((8, 128), dtype=torch.bfloat16, device=DEV)
+    ptrs = ptr_array([x.data_ptr()])
+    with pytest.raises(_lib.B2MError, match="quant_push_noalloc: bad shape"):
+        _lib.call("b2m_quant_push_noalloc", x.data_ptr(), 8, 100, 128, 1, ptrs, ptrs, 0, ptrs, 1,
+                  torch.cuda.current_stream(DEV).cuda_stream)
+    with pytest.raises(_lib.B2MError, match="null peer pointer"):
+        _lib.call("b2m_quant_push_noalloc", x.data_ptr(), 8, 128, 128, 1, ptrs, ptr_array([0]), 0, ptrs, 1,
+                  torch.cuda.current_stream(DEV).cuda_stream)
