@@ -188,12 +188,16 @@ def torch_unique_count(t) -> int:
     return int(torch.unique(t).numel()) if t.numel() else 0
 
 
+SAMPLE = 2048   # tokens per CPU run: a whole-layer DeepSeek-V3 run takes ~15 s on 16 host cores
+
+
 class CpuGolden:
     """The numpy restatement of the reference golden (``moe_bench/verify.py:14-47``) on this host.
 
     Weights are held as bf16 bit patterns and widened per expert inside the loop, as the
-    reference golden does (``w1_bf16[expert].float()``).  One run is the whole layer: all
-    T tokens of the workload.  The expert loop runs on every host core the process may use
+    reference golden does (``w1_bf16[expert].float()``).  One run is a fixed sample of the
+    layer: its first ``SAMPLE`` tokens (all of them when T is smaller), every expert they
+    route to computed -- the same sample at every N and in the main arm's cpu_baseline.  The expert loop runs on every host core the process may use
     (``golden_moe_threads``: whole experts per thread, BLAS single-threaded per thread when
     there are enough experts to go round, else BLAS threads split the cores), whatever
     thread limit the launcher set in the environment (torchrun sets OMP_NUM_THREADS=1).
@@ -212,9 +216,11 @@ class CpuGolden:
                 np.uint16)
 
         self.w1, self.w2, self.sw1, self.sw2 = bits(ck.w1), bits(ck.w2), bits(ck.shared_w1), bits(ck.shared_w2)
-        self.hid = bundle.hidden_full.float().cpu().numpy()
-        self.ids = bundle.routing.topk_ids_full.cpu().numpy()
-        self.wts = bundle.routing.topk_weights_full.cpu().numpy()
+        self.total = bundle.hidden_full.shape[0]
+        n = min(SAMPLE, self.total)
+        self.hid = bundle.hidden_full[:n].float().cpu().numpy()
+        self.ids = bundle.routing.topk_ids_full[:n].cpu().numpy()
+        self.wts = bundle.routing.topk_weights_full[:n].cpu().numpy()
         self.cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
         hit = len(set(self.ids.reshape(-1).tolist()))
         self.workers = max(1, min(self.cores, hit))
@@ -234,8 +240,9 @@ class CpuGolden:
     def describe(self, runs: int, mean_t: float) -> dict:
         n = self.hid.shape[0]
         return {"value": n / mean_t, "unit": "tokens/s", "cores": self.cores, "kind": "port",
-                "sample": f"the whole layer: all {n} tokens of the workload per run (numpy fp32 golden of "
-                          f"moe_bench/verify.py:14-47, per-expert bf16 widening inside the loop); {self.workers} "
+                "sample": f"the first {n} of the layer's {self.total} tokens per run, every expert they route to "
+                          f"(numpy fp32 golden of moe_bench/verify.py:14-47, per-expert bf16 widening inside the "
+                          f"loop; the same sample at every N); {self.workers} "
                           f"expert threads x {self.blas_threads} BLAS thread(s) on {self.cores} host cores; "
                           f"mean of {runs} run(s), {mean_t:.2f} s each"}
 
@@ -370,9 +377,10 @@ def exchange_split(layer, bundle, x, ids, wts, args, flush, barrier, world, dev,
     return out
 
 
-def check_parity(layer, bundle, x, ids, wts, world, rank, dev) -> dict:
+def check_parity(layer, bundle, x, ids, wts, world, rank, dev, parallel: str, rs_fp8: bool) -> dict:
     """One more regular forward, every rank's rows against the fp32 golden of the same tokens
-    (the reference worker's gates + max-abs <= 1.5 x calibrated activation-quant error)."""
+    (the reference worker's gates + max-abs <= 1.5 x calibrated activation-quant error, plus
+    the quantisation error of the ranks' partials when the reduce-scatter payload is FP8)."""
     import torch
     import torch.distributed as dist
 
@@ -383,7 +391,11 @@ def check_parity(layer, bundle, x, ids, wts, world, rank, dev) -> dict:
     layer.check()
     r0, n = rank * layer.T_local, layer.T_local
     hid = bundle.hidden_full[r0:r0 + n].to(dev)
-    rep = verify.check_layer(out, hid, ids[r0:r0 + n], wts[r0:r0 + n], bundle.ckpt)
+    extra = 0.0
+    if rs_fp8 and world > 1:
+        extra = verify.rs_fp8_error(verify.rank_partials(hid, ids[r0:r0 + n], wts[r0:r0 + n], bundle.ckpt, world,
+                                                         parallel))
+    rep = verify.check_layer(out, hid, ids[r0:r0 + n], wts[r0:r0 + n], bundle.ckpt, extra_calib=extra)
     v = torch.tensor([1.0 if rep["pass"] else 0.0, rep["cos_sim"], rep["rel_p99"], rep["max_abs"], rep["calib"],
                       abs(rep["scale"] - 1.0), rep["max_abs"] / max(rep["max_abs_bound"], 1e-30)],
                      dtype=torch.float64, device=dev)
@@ -419,6 +431,8 @@ def main() -> int:
                          "or copy-engine push")
     ap.add_argument("--ag-mode", default="auto", choices=["auto", "sm", "ce", "push"],
                     help="fused all-gather: SM stores from the quant kernel, copy-engine copies, or by block size")
+    ap.add_argument("--rs-dtype", default="bf16", choices=["bf16", "fp8"],
+                    help="reduce-scatter payload: bf16 partials, or 1x128 e4m3 codes + scales (the b3 variant)")
     ap.add_argument("--chunks", type=int, default=4, help="down-GEMM column chunks of the copy-engine push")
     ap.add_argument("--ce-streams", type=int, default=2, help="side streams carrying the copy-engine push")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -449,8 +463,14 @@ def main() -> int:
     exchange = None
     if world > 1 and args.comm == "p2p":
         from td_benchmark_b200.layer import P2PExchange
-        exchange = P2PExchange(ctx.group, chunks=args.chunks, rs_mode=args.rs_mode, ce_streams=args.ce_streams,
+        if args.rs_dtype == "fp8" and args.rs_mode != "sm":
+            raise SystemExit("--rs-dtype fp8 needs --rs-mode sm")
+        exchange = P2PExchange(ctx.group, chunks=args.chunks,
+                               rs_mode="fp8" if args.rs_dtype == "fp8" else args.rs_mode, ce_streams=args.ce_streams,
                                ag_mode=args.ag_mode)
+    elif world > 1:
+        from td_benchmark_b200.layer import NcclExchange
+        exchange = NcclExchange(ctx.group, rs_dtype=args.rs_dtype)
     layer, level = build_layer(spec, cfg, ctx, bundle, exchange=exchange)
     T = layer.T
     x = bundle.hidden_local.contiguous()
@@ -613,7 +633,8 @@ def main() -> int:
                          "bound / measured layer time"}
 
     # ---- parity of the benchmarked layer on every rank
-    parity = None if args.no_parity else check_parity(layer, bundle, x, ids, wts, world, rank, dev)
+    parity = None if args.no_parity else check_parity(layer, bundle, x, ids, wts, world, rank, dev, spec.parallel,
+                                                      args.rs_dtype == "fp8")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -632,7 +653,8 @@ def main() -> int:
                        "experts": s.E, "top_k": s.top_k, "shared_experts": s.shared_experts,
                        "parallelism": f"{spec.parallel.lower()}{world}", "scheme": code, "shard_level": level,
                        "routing": cfg.routing.imbalance_kind,
-                       "exchange": (f"p2p ag={layer.exchange.ag_mode} rs={args.rs_mode} "
+                       "rs_payload": args.rs_dtype if world > 1 else None,
+                       "exchange": (f"p2p ag={layer.exchange.ag_mode} rs={layer.exchange.rs_mode} "
                                     f"chunks={len(layer.exchange.chunk_cols)}"
                                     if getattr(layer.exchange, "name", "") == "p2p" else
                                     getattr(layer.exchange, "name", "none")),

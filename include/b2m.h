@@ -330,6 +330,28 @@ int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world
                   const uint32_t* flags, uint32_t epoch, const void* add, void* out, int32_t* dev_status,
                   void* stream);
 
+/* FP8 reduce-scatter push (replaces the b3 path's per-chunk rs_input quantisation +
+ * all_to_all_single of codes and scales, moe_bench/overlap/overlap_forward.py:900-928).
+ * Token t's partial -- its local top-k rows (+ shared row) summed in fp32, rounded to bf16 --
+ * is quantised per 128 columns (scale = max(amax/448, 1e-12), IEEE division, clamp, RNE
+ * e4m3) and stored at row rank*(T/world) + t - q*(T/world) of owner q = t / (T/world):
+ * codes into code_dst[q] (u8 [T, hidden]), scales into scale_dst[q] (fp32 [T, hidden/128]).
+ * Then *flag_dst[q] = epoch for every owner (counter == NULL: nothing published, e.g. when
+ * a collective moves the slots afterwards).  hidden % 128 == 0. */
+int b2m_combine_push_fp8(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, const int32_t* topk_ids,
+                         const int32_t* expert_map, const void* shared, int32_t world, int32_t rank,
+                         void* const* code_dst, void* const* scale_dst, uint32_t* const* flag_dst, uint32_t epoch,
+                         int32_t* counter, void* stream);
+
+/* Owner side of the FP8 reduce-scatter (replaces the dequant-sum of overlap_forward.py:933-946):
+ * once flags[0..world) are all >= epoch (flags == NULL: no wait),
+ *   out[t, :] = bf16( sum_{r=0..world-1} e4m3(codes[r*rows + t, :]) * scales[r*rows + t, group] + add[t, :] )
+ * in fp32, rank order, one rounding.  codes u8 [world*rows, hidden], scales fp32
+ * [world*rows, hidden/128]; add (bf16 [rows, hidden]) may be NULL. */
+int b2m_rs_reduce_fp8(const void* codes, const float* scales, int64_t rows, int64_t hidden, int32_t world,
+                      const uint32_t* flags, uint32_t epoch, const void* add, void* out, int32_t* dev_status,
+                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

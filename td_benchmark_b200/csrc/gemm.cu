@@ -43,6 +43,8 @@
 //
 // All waits are bounded (b2m_set_timeout_ns); on a timeout the kernel records the
 // site in dev_status, drains its own copies and MMAs and frees TMEM before returning.
+// Waits on another rank's flag use the set bound, waits on the CTA's own pipeline twice
+// that, so a pipeline stalled behind a missing peer records TIMEOUT_PEER (the cause).
 #include <cudaTypedefs.h>
 
 #include <atomic>
@@ -108,7 +110,9 @@ struct GemmParams {
   const float* topk_weights;
   int64_t hidden;
   int32_t* status;
-  uint64_t timeout_ns;
+  uint64_t timeout_ns;       // bound of a wait on another rank's flag
+  uint64_t pipe_timeout_ns;  // bound of a wait on this CTA's own pipeline (2 x timeout_ns): a
+                             // stalled pipeline behind a missing peer reports the peer, not itself
   // Down GEMM scatter (rs_world > 0): the row of pair p goes to owner q = p / rs_pairs_per_owner,
   // row rs_row0 + p - q * rs_pairs_per_owner of rs_dst[q] (another rank's receive buffer),
   // instead of row p of out_bf16.
@@ -294,8 +298,8 @@ __device__ __forceinline__ void stage_producer(const CUtensorMap* map_a, const C
       const uint32_t rph = (kbg / SRING) & 1;
       int ok = 1;
       if (lane == 0)
-        ok = mbar_wait(&C->sempty[r], rph ^ 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort) &&
-             mbar_wait(&C->empty[s], ph ^ 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort);
+        ok = mbar_wait(&C->sempty[r], rph ^ 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort) &&
+             mbar_wait(&C->empty[s], ph ^ 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         alive = false;
@@ -320,10 +324,10 @@ __device__ __forceinline__ void stage_producer(const CUtensorMap* map_a, const C
   if (lane == 0) {
     const uint32_t first = kbg > STAGES ? kbg - STAGES : 0;
     for (uint32_t i = first; i < kbg; ++i)
-      mbar_wait(&C->full[i % STAGES], (i / STAGES) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
+      mbar_wait(&C->full[i % STAGES], (i / STAGES) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
     const uint32_t rfirst = kbg > SRING ? kbg - SRING : 0;
     for (uint32_t i = rfirst; i < kbg; ++i)
-      mbar_wait(&C->sfull[i % SRING], (i / SRING) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
+      mbar_wait(&C->sfull[i % SRING], (i / SRING) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
   }
   __syncwarp();
 }
@@ -343,8 +347,8 @@ __device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, C
       const uint32_t ph = (kbg / STAGES) & 1;
       const int b = kbg & 1;
       const uint32_t tph = (kbg >> 1) & 1;
-      if (!mbar_wait(&C->tempty[b], tph ^ 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_MMA, abort) ||
-          !mbar_wait(&C->full[s], ph, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_MMA, abort)) {
+      if (!mbar_wait(&C->tempty[b], tph ^ 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_MMA, abort) ||
+          !mbar_wait(&C->full[s], ph, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_MMA, abort)) {
         alive = false;
         break;
       }
@@ -362,7 +366,7 @@ __device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, C
   // completed (on the normal path they all have; after an abort some may not).
   if (kbg > 0) {
     mma_commit(&C->mma_done);
-    mbar_wait(&C->mma_done, 0, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
+    mbar_wait(&C->mma_done, 0, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
   }
 }
 
@@ -388,7 +392,7 @@ __device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)
     const int par = tiles_done & 1;
     amax_x[par][h][r] = amax;
     mbar_arrive(&amax_bar[par]);
-    int ok = mbar_wait(&amax_bar[par], (tiles_done >> 1) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
+    int ok = mbar_wait(&amax_bar[par], (tiles_done >> 1) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
                        abort);
     if (!__all_sync(0xffffffffu, ok)) return false;
     amax = fmaxf(amax_x[par][0][r], amax_x[par][1][r]);
@@ -484,8 +488,8 @@ __device__ __forceinline__ void epilogue_warps(const GemmParams& p, Control* C, 
     for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
       const int rs = kbg % SRING;
       const int b = kbg & 1;
-      int ok = mbar_wait(&C->tfull[b], (kbg >> 1) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE, abort);
-      ok = ok && mbar_wait(&C->sfull[rs], (kbg / SRING) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
+      int ok = mbar_wait(&C->tfull[b], (kbg >> 1) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE, abort);
+      ok = ok && mbar_wait(&C->sfull[rs], (kbg / SRING) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
                            abort);
       if (!__all_sync(0xffffffffu, ok)) {
         alive = false;
@@ -696,8 +700,8 @@ __device__ __forceinline__ void pair_producer(const CUtensorMap* map_a, const CU
       const uint32_t rph = (kbg / SRING) & 1;
       int ok = 1;
       if (lane == 0)
-        ok = mbar_wait(&C->sempty[r], rph ^ 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort) &&
-             mbar_wait(&C->empty[s], ph ^ 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort);
+        ok = mbar_wait(&C->sempty[r], rph ^ 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort) &&
+             mbar_wait(&C->empty[s], ph ^ 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_PRODUCER, abort);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         alive = false;
@@ -723,12 +727,12 @@ __device__ __forceinline__ void pair_producer(const CUtensorMap* map_a, const CU
     if (cr == 0) {
       const uint32_t first = kbg > PSTAGES ? kbg - PSTAGES : 0;
       for (uint32_t i = first; i < kbg; ++i)
-        mbar_wait(&C->full[i % PSTAGES], (i / PSTAGES) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN,
+        mbar_wait(&C->full[i % PSTAGES], (i / PSTAGES) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN,
                   nullptr);
     }
     const uint32_t rfirst = kbg > SRING ? kbg - SRING : 0;
     for (uint32_t i = rfirst; i < kbg; ++i)
-      mbar_wait(&C->sfull[i % SRING], (i / SRING) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
+      mbar_wait(&C->sfull[i % SRING], (i / SRING) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
   }
   __syncwarp();
 }
@@ -746,8 +750,8 @@ __device__ __forceinline__ void pair_mma_thread(const GemmParams& p, uint8_t* sm
       const uint32_t ph = (kbg / PSTAGES) & 1;
       const int b = kbg & 1;
       const uint32_t tph = (kbg >> 1) & 1;
-      if (!mbar_wait(&C->tempty[b], tph ^ 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_MMA, abort) ||
-          !mbar_wait(&C->full[s], ph, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_MMA, abort)) {
+      if (!mbar_wait(&C->tempty[b], tph ^ 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_MMA, abort) ||
+          !mbar_wait(&C->full[s], ph, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_MMA, abort)) {
         alive = false;
         break;
       }
@@ -763,7 +767,7 @@ __device__ __forceinline__ void pair_mma_thread(const GemmParams& p, uint8_t* sm
   }
   if (kbg > 0) {
     mma_commit_pair(&C->mma_done, 0x1);
-    mbar_wait(&C->mma_done, 0, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
+    mbar_wait(&C->mma_done, 0, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
   }
 }
 
@@ -806,8 +810,8 @@ __device__ __forceinline__ void pair_epilogue(const GemmParams& p, PairControl* 
     for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
       const int rs = kbg % SRING;
       const int b = kbg & 1;
-      int ok = mbar_wait(&C->tfull[b], (kbg >> 1) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE, abort);
-      ok = ok && mbar_wait(&C->sfull[rs], (kbg / SRING) & 1, p.timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
+      int ok = mbar_wait(&C->tfull[b], (kbg >> 1) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE, abort);
+      ok = ok && mbar_wait(&C->sfull[rs], (kbg / SRING) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
                            abort);
       if (!__all_sync(0xffffffffu, ok)) {
         alive = false;
@@ -1062,6 +1066,7 @@ int gemm1_impl(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, i
   p.hidden = hidden;
   p.status = dev_status;
   p.timeout_ns = timeout_ns();
+  p.pipe_timeout_ns = 2 * p.timeout_ns;
   if (sw) {
     if (block_pairs) return fail(B2M_ERR_UNSUPPORTED, "gemm1_wait: no paired-CTA variant");
     if (!sw->block_order || !sw->sorted_ids || !sw->flags || sw->top_k < 1 || sw->tokens_per_src < 1 ||
@@ -1187,6 +1192,7 @@ int gemm2_impl(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int3
   p.hidden = hidden;
   p.status = dev_status;
   p.timeout_ns = timeout_ns();
+  p.pipe_timeout_ns = 2 * p.timeout_ns;
   if (sc) {
     if (sc->world < 1 || sc->world > 8 || !sc->dst || sc->pairs_per_owner <= 0 || sc->row0 < 0 ||
         sc->pairs_per_owner * sc->world != numel)

@@ -330,6 +330,95 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// ---------------------------------------------------------------- reduce-scatter push, FP8 payload
+// The b3 variant of the reduce-scatter (moe_bench/overlap/overlap_forward.py:900-946): each
+// token's combined partial row -- its local top-k rows (+ shared expert) summed in fp32 and
+// rounded to bf16, which is what the reference quantises -- is quantised per 128 columns by the
+// activation rule (amax / 448 floored at 1e-12, IEEE division, clamp, RNE e4m3), and the codes
+// (hidden bytes) and fp32 scales (hidden / 128) go to the owner's FP8 slot for this source:
+// H + H/32 bytes per row instead of 2H.  One warp per token; in each 256-column step lanes
+// 0-15 hold one 128-group (8 values each) and lanes 16-31 the next.
+__global__ void __launch_bounds__(kThreads)
+    combine_push_fp8_kernel(const __nv_bfloat16* __restrict__ staged, int64_t tokens, int top_k, int64_t hidden,
+                            const int32_t* __restrict__ topk_ids, const int32_t* __restrict__ expert_map,
+                            const __nv_bfloat16* __restrict__ shared, int world, int rank,
+                            const __grid_constant__ PeerPtrs codes, const __grid_constant__ PeerPtrs scales,
+                            const __grid_constant__ FlagPtrs flags, uint32_t epoch, int32_t* counter) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
+  const int64_t per_rank = tokens / world;
+  const int64_t gpr = hidden / 128;
+  for (int64_t t = warp; t < tokens; t += nwarps) {
+    const uint32_t mask = local_pair_mask(topk_ids, expert_map, t, top_k, lane);
+    const int owner = static_cast<int>(t / per_rank);
+    const int64_t slot_row = static_cast<int64_t>(rank) * per_rank + (t - owner * per_rank);
+    uint8_t* qrow = static_cast<uint8_t*>(codes.p[owner]) + slot_row * hidden;
+    float* srow = static_cast<float*>(scales.p[owner]) + slot_row * gpr;
+    for (int64_t c0 = 0; c0 < hidden; c0 += 256) {
+      const int64_t c = c0 + lane * 8;
+      const bool in = c < hidden;  // hidden % 128 == 0: a half-warp is all in or all out
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (in) v = combine_vec(staged, t, top_k, hidden, c, mask, topk_ids, expert_map, shared);
+      float f[8];
+      bf16x8_to_f32(v, f);
+      const float scale = fmaxf(halfwarp_amax(f) / 448.0f, 1e-12f);
+      if (in) {
+        *reinterpret_cast<uint2*>(qrow + c) = quant8(f, scale);
+        if ((lane & 15) == 0) srow[c / 128] = scale;
+      }
+    }
+  }
+  if (counter) publish_when_grid_done(counter, flags, world, epoch);
+}
+
+// Owner side of the FP8 reduce-scatter: out[t] = bf16(sum over sources r in rank order of
+// e4m3(codes[r][t]) * scale[r][t][group], + add[t]) in fp32 with one rounding, after every
+// source's flag reached epoch (flags == nullptr: the slots were filled by a collective that
+// has already completed on this stream).
+__global__ void __launch_bounds__(kThreads)
+    rs_reduce_fp8_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ scales, int64_t rows,
+                         int64_t hidden, int world, const uint32_t* flags, uint32_t epoch,
+                         const __nv_bfloat16* __restrict__ add, __nv_bfloat16* __restrict__ out, int32_t* status,
+                         uint64_t timeout_ns) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if (flags && threadIdx.x < world && !wait_flag_geq(flags + threadIdx.x, epoch, timeout_ns, status,
+                                                     B2M_STATUS_TIMEOUT_PEER))
+    s_ok = 0;
+  __syncthreads();
+  if (!s_ok) return;  // status already records the timeout
+  const int64_t vec = hidden / 8;
+  const int64_t gpr = hidden / 128;
+  const int64_t total = rows * vec;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t t = v / vec;
+    const int64_t c = (v - t * vec) * 8;
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int r = 0; r < world; ++r) {
+      const int64_t row = static_cast<int64_t>(r) * rows + t;
+      const uint2 q = __ldcg(reinterpret_cast<const uint2*>(codes + row * hidden + c));
+      const float sc = __ldcg(scales + row * gpr + c / 128);
+      const uint32_t w[2] = {q.x, q.y};
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(
+              static_cast<__nv_fp8x2_storage_t>((w[i] >> (16 * j)) & 0xFFFFu), __NV_E4M3);
+          const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&h));
+          a[4 * i + 2 * j] += d.x * sc;
+          a[4 * i + 2 * j + 1] += d.y * sc;
+        }
+      }
+    }
+    if (add) acc_bf16x8(*reinterpret_cast<const uint4*>(add + t * hidden + c), a);
+    *reinterpret_cast<uint4*>(out + t * hidden + c) = pack_bf16x8(a);
+  }
+}
+
 int grid_for(int64_t work, int num_sms, int per_sm) {
   int64_t b = (work + kThreads - 1) / kThreads;
   if (b > int64_t(num_sms) * per_sm) b = int64_t(num_sms) * per_sm;
@@ -628,6 +717,50 @@ int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world
       static_cast<const __nv_bfloat16*>(slots), rows, hidden, world, nchunks * world, flags, epoch,
       static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out), dev_status, timeout_ns());
   return check_cuda(cudaGetLastError(), "rs_reduce launch");
+}
+
+int b2m_combine_push_fp8(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, const int32_t* topk_ids,
+                         const int32_t* expert_map, const void* shared, int32_t world, int32_t rank,
+                         void* const* code_dst, void* const* scale_dst, uint32_t* const* flag_dst, uint32_t epoch,
+                         int32_t* counter, void* stream) {
+  using namespace b2m;
+  int num_sms = 0;
+  B2M_TRY(require_sm100(&num_sms));
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || tokens <= 0 || tokens % world ||
+      hidden <= 0 || hidden % 128 || top_k <= 0)
+    return fail(B2M_ERR_ARG, "combine_push_fp8: bad shape (tokens %% world == 0, hidden %% 128 == 0)");
+  if (!staged || !code_dst || !scale_dst || (counter && !flag_dst) || (expert_map && !topk_ids) ||
+      !aligned16(staged) || (shared && !aligned16(shared)))
+    return fail(B2M_ERR_ARG, "combine_push_fp8: bad pointers");
+  PeerPtrs q{}, sc{};
+  FlagPtrs f{};
+  for (int r = 0; r < world; ++r) {
+    if (!code_dst[r] || !scale_dst[r] || (counter && !flag_dst[r]) ||
+        (reinterpret_cast<uintptr_t>(code_dst[r]) & 7u) || (reinterpret_cast<uintptr_t>(scale_dst[r]) & 3u))
+      return fail(B2M_ERR_ARG, "combine_push_fp8: bad peer pointer %d (codes 8-byte, scales 4-byte aligned)", r);
+    q.p[r] = code_dst[r];
+    sc.p[r] = scale_dst[r];
+    f.p[r] = counter ? flag_dst[r] : nullptr;
+  }
+  combine_push_fp8_kernel<<<grid_for(tokens * 32, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, topk_ids, expert_map,
+      static_cast<const __nv_bfloat16*>(shared), world, rank, q, sc, f, epoch, counter);
+  return check_cuda(cudaGetLastError(), "combine_push_fp8 launch");
+}
+
+int b2m_rs_reduce_fp8(const void* codes, const float* scales, int64_t rows, int64_t hidden, int32_t world,
+                      const uint32_t* flags, uint32_t epoch, const void* add, void* out, int32_t* dev_status,
+                      void* stream) {
+  using namespace b2m;
+  int num_sms = 0;
+  B2M_TRY(require_sm100(&num_sms));
+  if (world < 1 || world > kMaxWorld || rows <= 0 || hidden <= 0 || hidden % 128 || !codes || !scales || !out ||
+      (reinterpret_cast<uintptr_t>(codes) & 7u) || !aligned16(out) || (add && !aligned16(add)))
+    return fail(B2M_ERR_ARG, "rs_reduce_fp8: bad shape/pointers (hidden %% 128 == 0, 16-byte rows)");
+  rs_reduce_fp8_kernel<<<grid_for(rows * (hidden / 8), num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(codes), scales, rows, hidden, world, flags, epoch,
+      static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out), dev_status, timeout_ns());
+  return check_cuda(cudaGetLastError(), "rs_reduce_fp8 launch");
 }
 
 }  // extern "C"

@@ -152,25 +152,47 @@ class NullExchange:
 
 
 class NcclExchange:
-    """Unfused comparison: NCCL all-gather of FP8 bytes + fp32 scales, NCCL bf16 reduce-scatter.
+    """Unfused comparison: NCCL all-gather of FP8 bytes + fp32 scales, NCCL reduce-scatter.
 
     Same collectives as the reference's b2 (``overlap_forward.py:494-505``, ``:603-608``),
-    issued as one call each instead of per chunk.
+    issued as one call each instead of per chunk.  ``rs_dtype="fp8"`` is the b3 variant
+    (``overlap_forward.py:900-946``): every token's partial is quantised per 128 columns
+    into a send buffer ordered by owner (``b2m_combine_push_fp8`` with local destinations),
+    codes and scales cross with ``all_to_all_single``, and ``b2m_rs_reduce_fp8``
+    dequant-sums the received slots in rank order.
     """
     name = "nccl"
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, rs_dtype: str = "bf16"):
         import torch.distributed as dist
+        if rs_dtype not in ("bf16", "fp8"):
+            raise ValueError(f"rs_dtype must be 'bf16' or 'fp8', got {rs_dtype!r}")
         self.dist = dist
         self.group = group
         self.world_size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.rs_dtype = rs_dtype
 
     def setup(self, layer: "MoELayer") -> None:
+        from .symm import ptr_array
+
         dev = layer.device
         layer.xq = torch.empty((layer.T, layer.H), dtype=ops.FP8, device=dev)
         layer.xs = torch.empty((layer.T, layer.H // 128), dtype=torch.float32, device=dev)
-        self.partial = torch.empty((layer.T, layer.H), dtype=torch.bfloat16, device=dev)
+        if self.rs_dtype == "bf16":
+            self.partial = torch.empty((layer.T, layer.H), dtype=torch.bfloat16, device=dev)
+            return
+        T, H, Tl, P = layer.T, layer.H, layer.T_local, self.world_size
+        self.send_q = torch.empty((T, H), dtype=torch.uint8, device=dev)
+        self.send_s = torch.empty((T, H // 128), dtype=torch.float32, device=dev)
+        self.recv_q = torch.empty((T, H), dtype=torch.uint8, device=dev)
+        self.recv_s = torch.empty((T, H // 128), dtype=torch.float32, device=dev)
+        # destination r's rows start at row r*Tl of the send buffer: the push kernel stores
+        # owner r's token i at row rank*Tl + i of destination r, so shift each base back
+        # by (r - rank)*Tl rows (the addresses written all fall inside the buffer)
+        qb, sb = self.send_q.data_ptr(), self.send_s.data_ptr()
+        self._q_dst = ptr_array([qb + (r - self.rank) * Tl * H for r in range(P)])
+        self._s_dst = ptr_array([sb + (r - self.rank) * Tl * (H // 128) * 4 for r in range(P)])
 
     def gather_dispatch(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
         r0 = self.rank * layer.T_local
@@ -185,7 +207,23 @@ class NcclExchange:
             layer.shared.load_rows(layer.xq, layer.xs)
 
     def down_and_scatter(self, layer: "MoELayer", topk_weights, ids, shared_out) -> torch.Tensor:
+        from . import _lib
+
         layer.gemm2(topk_weights)
+        if self.rs_dtype == "fp8":
+            st = ops._stream(layer.device)
+            _lib.call("b2m_combine_push_fp8", layer.staged.data_ptr(), layer.T, layer.top_k, layer.H,
+                      None if ids is None else ids.data_ptr(),
+                      None if layer.expert_map is None else layer.expert_map.data_ptr(),
+                      None if shared_out is None else shared_out.data_ptr(), self.world_size, self.rank, self._q_dst,
+                      self._s_dst, None, 0, None, st)
+            self.dist.all_to_all_single(self.recv_q, self.send_q, group=self.group)
+            self.dist.all_to_all_single(self.recv_s, self.send_s, group=self.group)
+            add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
+            _lib.call("b2m_rs_reduce_fp8", self.recv_q.data_ptr(), self.recv_s.data_ptr(), layer.T_local, layer.H,
+                      self.world_size, None, 0, None if add is None else add.data_ptr(), layer.out_local.data_ptr(),
+                      layer.status.data_ptr(), st)
+            return layer.out_local
         ops.combine(layer.staged, layer.top_k, ids, layer.expert_map, shared_out, self.partial)
         self.dist.reduce_scatter_tensor(layer.out_local, self.partial, group=self.group)
         if layer.shared is not None and layer.ep:
@@ -247,6 +285,10 @@ class P2PExchange:
            "sm" on 2 and 8 B200s for the Mixtral and DeepSeek-V3 shapes (the strided
            copy-engine pushes ran below the SM stores' NVLink rate and the column chunks
            cost the down GEMM time), kept as the alternative.
+      "fp8" -- the b3 payload (``overlap_forward.py:900-946``): as "sm", but each token's
+           partial is quantised per 128 columns and its e4m3 codes + fp32 scales are stored in
+           the owner's FP8 slot (``b2m_combine_push_fp8``, H + H/32 bytes per row instead of
+           2H); the owner dequantises and sums in rank order (``b2m_rs_reduce_fp8``).
     ``b2m_rs_reduce`` then sums the slots in rank order.  Flags are epochs.
     """
     name = "p2p"
@@ -255,9 +297,9 @@ class P2PExchange:
 
     def __init__(self, group=None, chunks: int = 4, rs_mode: str = "sm", ce_streams: int = 2, ag_mode: str = "auto"):
         import torch.distributed as dist
-        if rs_mode not in ("ce", "sm", "gemm") or ag_mode not in ("ce", "sm", "auto", "push"):
-            raise ValueError(f"rs_mode must be 'gemm', 'ce' or 'sm' and ag_mode 'push', 'ce', 'sm' or 'auto', got "
-                             f"{rs_mode!r}, {ag_mode!r}")
+        if rs_mode not in ("ce", "sm", "gemm", "fp8") or ag_mode not in ("ce", "sm", "auto", "push"):
+            raise ValueError(f"rs_mode must be 'gemm', 'ce', 'sm' or 'fp8' and ag_mode 'push', 'ce', 'sm' or 'auto', "
+                             f"got {rs_mode!r}, {ag_mode!r}")
         self.ag_mode = ag_mode
         self.dist = dist
         self.group = group
@@ -265,6 +307,7 @@ class P2PExchange:
         self.rank = dist.get_rank(group)
         self.epoch = 0
         self.ws = None
+        self._shared_out = None   # shared expert output of this forward (expert parallel), run early
         self.chunks_req = chunks if rs_mode == "ce" else 1
         self.rs_mode = rs_mode
         self.ce_streams = max(1, ce_streams)
@@ -286,6 +329,9 @@ class P2PExchange:
                   "counters": 16}
         if self.rs_mode == "gemm":
             layout["recv"] = self.rs_nsrc * Tl * layer.top_k * H * 2
+        elif self.rs_mode == "fp8":
+            layout["slots_q"] = T * H                    # [P source blocks of T/P rows, H] e4m3
+            layout["slots_s"] = T * (H // 128) * 4       # their fp32 group scales
         else:
             layout["slots"] = T * H * 2
         rows_cap = layer.route.rows_cap
@@ -308,6 +354,9 @@ class P2PExchange:
         layer.xs = ws.tensor("xs", (T, H // 128), torch.float32)
         if self.rs_mode == "gemm":
             self._recv_dst = ptr_array([ws.peer("recv", r) for r in range(P)])
+        elif self.rs_mode == "fp8":
+            self._slotq_dst = ptr_array([ws.peer("slots_q", r) for r in range(P)])
+            self._slots_dst = ptr_array([ws.peer("slots_s", r) for r in range(P)])
         else:
             self.slots = ws.tensor("slots", (T, H), torch.bfloat16)   # [P source blocks of T/P rows, H]
         self.ag_flags = ws.local("ag_flags")
@@ -317,7 +366,7 @@ class P2PExchange:
         self._s_dst = ptr_array([ws.peer("xs", r) for r in range(P)])
         self._ag_dst = ptr_array([ws.peer("ag_flags", r) + 4 * self.rank for r in range(P)])
         self._ag_own = ptr_array([self.ag_flags + 4 * self.rank])
-        if self.rs_mode != "gemm":
+        if self.rs_mode in ("sm", "ce"):
             self._slot_dst = ptr_array([ws.peer("slots", r) for r in range(P)])
         self._rs_dst = ptr_array([ws.peer("rs_flags", r) + 4 * self.rank for r in range(P)])
         # column chunks of the down GEMM (multiples of its 256-column tile)
@@ -350,7 +399,7 @@ class P2PExchange:
             self.chunk_ev = [torch.cuda.Event() for _ in self.chunk_cols]
         self.dist.barrier(group=self.group)
 
-    def gather_dispatch(self, layer: "MoELayer", x_local: torch.Tensor) -> None:
+    def gather_dispatch(self, layer: "MoELayer", x_local: torch.Tensor, with_shared: bool = True) -> None:
         from . import _lib
 
         self.epoch += 1
@@ -364,9 +413,16 @@ class P2PExchange:
                       self._s_dst, self.rank * Tl, self._ag_dst, self.epoch, self.counters, st)
         else:
             self._gather_ce(layer, x_local)
-        if layer.shared is not None and layer.ep:
+        self._shared_out = None
+        if layer.shared is not None and layer.ep and with_shared:
+            # Expert parallel: the shared expert works on this rank's own tokens, which are
+            # already quantised here, so its GEMMs run now -- while the peers' rows are still
+            # crossing NVLink -- instead of after the reduce-scatter (the overlap of the
+            # reference's shared stream, overlap_forward.py:513-525).
             r0 = self.rank * Tl
             layer.shared.load_rows(layer.xq[r0:r0 + Tl], layer.xs[r0:r0 + Tl])
+            self._shared_out = layer.shared.run(layer.status)
+            layer._event("shared_end")
         r = layer.route
         _lib.call("b2m_dispatch_rows_wait", layer.xq.data_ptr(), layer.xs.data_ptr(), layer.T, H, r.pair_pos.data_ptr(),
                   layer.top_k, layer.a_sorted.data_ptr(), layer.as_t.data_ptr(), r.rows_cap, self.ag_flags,
@@ -464,9 +520,12 @@ class P2PExchange:
             layer._event("gemm2_end")
             _lib.call("b2m_signal", self._rs_dst, P, self.epoch, compute.cuda_stream)
             layer._event("combine_end")
-            add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
-            layer._event("shared_end")
-            self._rs_combine(layer, add, self.epoch)
+            self._rs_combine(layer, self._shared_out, self.epoch)
+            return layer.out_local
+        if self.rs_mode == "fp8":
+            layer.gemm2(topk_weights)
+            layer._event("gemm2_end")
+            self._fp8_push_reduce(layer, idsp, emap, shp, self._shared_out, compute)
             return layer.out_local
         if self.rs_mode == "sm":
             layer.gemm2(topk_weights)
@@ -492,14 +551,25 @@ class P2PExchange:
             _lib.call("b2m_signal", self._rs_dst, P, self.epoch, self.ce[0].cuda_stream)
             self._pending_side = True
         layer._event("combine_end")
-        add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
-        layer._event("shared_end")
+        add = self._shared_out
         if self.rs_mode == "ce":
             self._join_side(compute)   # staging buffer reuse by the next call
         _lib.call("b2m_rs_reduce", self.slots.data_ptr(), Tl, H, P, 1, self.rs_flags, self.epoch,
                   None if add is None else add.data_ptr(), layer.out_local.data_ptr(), layer.status.data_ptr(),
                   compute.cuda_stream)
         return layer.out_local
+
+    def _fp8_push_reduce(self, layer: "MoELayer", idsp, emap, shp, add, compute) -> None:
+        """FP8 reduce-scatter: quantised partials to the owners' slots, then the owner dequant-sum."""
+        from . import _lib
+
+        _lib.call("b2m_combine_push_fp8", layer.staged.data_ptr(), layer.T, layer.top_k, layer.H, idsp, emap, shp,
+                  self.world_size, self.rank, self._slotq_dst, self._slots_dst, self._rs_dst, self.epoch,
+                  self.counters + 4, compute.cuda_stream)
+        layer._event("combine_end")
+        _lib.call("b2m_rs_reduce_fp8", self.ws.local("slots_q"), self.ws.local("slots_s"), layer.T_local, layer.H,
+                  self.world_size, self.rs_flags, self.epoch, None if add is None else add.data_ptr(),
+                  layer.out_local.data_ptr(), layer.status.data_ptr(), compute.cuda_stream)
 
     def exchange_alone(self, layer: "MoELayer", x_local: torch.Tensor, topk_ids: torch.Tensor) -> bool:
         """The all-gather and the reduce-scatter of one forward with no GEMM between them.
@@ -512,12 +582,15 @@ class P2PExchange:
         SM / copy-engine all-gather with the SM reduce-scatter; returns False otherwise."""
         from . import _lib
 
-        if self.ag_mode not in ("sm", "ce") or self.rs_mode != "sm":
+        if self.ag_mode not in ("sm", "ce") or self.rs_mode not in ("sm", "fp8"):
             return False
-        self.gather_dispatch(layer, x_local)
+        self.gather_dispatch(layer, x_local, with_shared=False)
         compute = torch.cuda.current_stream(layer.device)
         emap = None if layer.expert_map is None else layer.expert_map.data_ptr()
         idsp = topk_ids.data_ptr() if layer.ep else None
+        if self.rs_mode == "fp8":
+            self._fp8_push_reduce(layer, idsp, emap, None, None, compute)
+            return True
         _lib.call("b2m_combine_push", layer.staged.data_ptr(), layer.T, layer.top_k, layer.H, 0, layer.H, idsp, emap,
                   None, self.world_size, self.rank, self._slot_dst, self._rs_dst, self.epoch, self.counters + 4, 0,
                   compute.cuda_stream)

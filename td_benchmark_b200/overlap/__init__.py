@@ -25,7 +25,7 @@ import torch
 
 from ..layer import ExpertWeights, MoELayer, NcclExchange, NullExchange, P2PExchange
 
-__all__ = ["MoEOverlapState", "moe_forward_overlap_fp8ag"]
+__all__ = ["MoEOverlapState", "moe_forward_overlap_fp8ag", "moe_forward_overlap_fp8ag_fp8rs"]
 
 
 @dataclass
@@ -64,10 +64,12 @@ class MoEOverlapState:
             layer.close()
         self._layers.clear()
 
-    def make_exchange(self):
+    def make_exchange(self, rs_fp8: bool = False):
         if self.tp_size == 1:
             return NullExchange()
-        return P2PExchange(self.tp_group) if self.exchange == "p2p" else NcclExchange(self.tp_group)
+        if self.exchange == "p2p":
+            return P2PExchange(self.tp_group, rs_mode="fp8" if rs_fp8 else "sm")
+        return NcclExchange(self.tp_group, rs_dtype="fp8" if rs_fp8 else "bf16")
 
 
 def _as_expert_weights(shared_mlp: Any) -> Optional[ExpertWeights]:
@@ -79,14 +81,12 @@ def _as_expert_weights(shared_mlp: Any) -> Optional[ExpertWeights]:
         raise TypeError("shared_mlp must be ExpertWeights or expose w1_fp8/w1_scale/w2_fp8/w2_scale") from exc
 
 
-def moe_forward_overlap_fp8ag(state: MoEOverlapState, hidden_states: torch.Tensor, w1: torch.Tensor,
-                              w2: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor, top_k: int,
-                              global_num_experts: int, expert_map: Optional[torch.Tensor] = None,
-                              shared_mlp: Any = None, M_valid: Optional[int] = None,
-                              w1_scale: Optional[torch.Tensor] = None, w2_scale: Optional[torch.Tensor] = None,
-                              w2_zp: Optional[torch.Tensor] = None, a1_scale: Optional[torch.Tensor] = None,
-                              a2_scale: Optional[torch.Tensor] = None,
-                              block_shape: Optional[list[int]] = None) -> torch.Tensor:
+def _forward(state: MoEOverlapState, rs_fp8: bool, hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+             topk_weights: torch.Tensor, topk_ids: torch.Tensor, top_k: int, global_num_experts: int,
+             expert_map: Optional[torch.Tensor], shared_mlp: Any, M_valid: Optional[int],
+             w1_scale: Optional[torch.Tensor], w2_scale: Optional[torch.Tensor], w2_zp: Optional[torch.Tensor],
+             a1_scale: Optional[torch.Tensor], a2_scale: Optional[torch.Tensor],
+             block_shape: Optional[list[int]]) -> torch.Tensor:
     if w1_scale is None or w2_scale is None:
         raise ValueError("moe_forward_overlap_fp8ag needs w1_scale and w2_scale (block FP8 weights)")
     if block_shape is not None and list(block_shape) != [128, 128]:
@@ -99,14 +99,44 @@ def moe_forward_overlap_fp8ag(state: MoEOverlapState, hidden_states: torch.Tenso
     if M_valid is not None and M_valid < tokens:
         raise ValueError("M_valid < gathered tokens is not supported: pad routing to the full token count")
     key = (w1.data_ptr(), w2.data_ptr(), tokens, top_k, global_num_experts,
-           None if expert_map is None else expert_map.data_ptr(), id(shared_mlp))
+           None if expert_map is None else expert_map.data_ptr(), id(shared_mlp), rs_fp8)
     layer = state._layers.get(key)
     if layer is None:
         weights = ExpertWeights.prepare(w1, w1_scale, w2, w2_scale)
         layer = MoELayer(weights, tokens, top_k, global_num_experts, expert_map=expert_map,
-                         shared=_as_expert_weights(shared_mlp), exchange=state.make_exchange(),
+                         shared=_as_expert_weights(shared_mlp), exchange=state.make_exchange(rs_fp8),
                          device=hidden_states.device)
         state._layers[key] = layer
     ids = topk_ids[:tokens].to(torch.int32).contiguous()
     wts = topk_weights[:tokens].to(torch.float32).contiguous()
     return layer.forward(hidden_states.contiguous(), ids, wts)
+
+
+def moe_forward_overlap_fp8ag(state: MoEOverlapState, hidden_states: torch.Tensor, w1: torch.Tensor,
+                              w2: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor, top_k: int,
+                              global_num_experts: int, expert_map: Optional[torch.Tensor] = None,
+                              shared_mlp: Any = None, M_valid: Optional[int] = None,
+                              w1_scale: Optional[torch.Tensor] = None, w2_scale: Optional[torch.Tensor] = None,
+                              w2_zp: Optional[torch.Tensor] = None, a1_scale: Optional[torch.Tensor] = None,
+                              a2_scale: Optional[torch.Tensor] = None,
+                              block_shape: Optional[list[int]] = None) -> torch.Tensor:
+    """FP8 all-gather, bf16 reduce-scatter (the reference's b2, ``overlap_forward.py:348-622``)."""
+    return _forward(state, False, hidden_states, w1, w2, topk_weights, topk_ids, top_k, global_num_experts,
+                    expert_map, shared_mlp, M_valid, w1_scale, w2_scale, w2_zp, a1_scale, a2_scale, block_shape)
+
+
+def moe_forward_overlap_fp8ag_fp8rs(state: MoEOverlapState, hidden_states: torch.Tensor, w1: torch.Tensor,
+                                    w2: torch.Tensor, topk_weights: torch.Tensor, topk_ids: torch.Tensor,
+                                    top_k: int, global_num_experts: int, expert_map: Optional[torch.Tensor] = None,
+                                    shared_mlp: Any = None, M_valid: Optional[int] = None,
+                                    w1_scale: Optional[torch.Tensor] = None,
+                                    w2_scale: Optional[torch.Tensor] = None,
+                                    w2_zp: Optional[torch.Tensor] = None, a1_scale: Optional[torch.Tensor] = None,
+                                    a2_scale: Optional[torch.Tensor] = None,
+                                    block_shape: Optional[list[int]] = None) -> torch.Tensor:
+    """FP8 all-gather and FP8 reduce-scatter payload (the reference's b3,
+    ``overlap_forward.py:625-953``): each rank's partials cross as 1x128 e4m3 codes +
+    fp32 scales and the owner dequant-sums them in rank order.  With one rank it is the
+    same computation as ``moe_forward_overlap_fp8ag`` (nothing is exchanged)."""
+    return _forward(state, True, hidden_states, w1, w2, topk_weights, topk_ids, top_k, global_num_experts,
+                    expert_map, shared_mlp, M_valid, w1_scale, w2_scale, w2_zp, a1_scale, a2_scale, block_shape)

@@ -25,6 +25,8 @@ EXCHANGE = {"d1": "nccl", "d2": "nccl", "d3": "p2p", "d4": "p2p"}
 
 B200_TUNABLES = {
     "check_status": TunableSpec(bool, False, "synchronise after every run() and raise on a device status code"),
+    "rs_dtype": TunableSpec(str, "bf16", "reduce-scatter payload: bf16 partials ('bf16') or 1x128-quantised e4m3 "
+                                         "codes + fp32 scales dequant-summed by the owner ('fp8', the b3 variant)"),
 }
 # peer-memory exchange knobs of d3 / d4 (P2PExchange)
 P2P_TUNABLES = {
@@ -35,7 +37,7 @@ P2P_TUNABLES = {
                                       "epilogue ('gemm') or copy engines ('ce')"),
     "rs_chunks": TunableSpec(int, 4, "down-GEMM column chunks of the copy-engine reduce-scatter (1..8)"),
 }
-_CHOICES = {"ag_mode": ("sm", "ce", "auto", "push"), "rs_mode": ("sm", "ce", "gemm")}
+_CHOICES = {"ag_mode": ("sm", "ce", "auto", "push"), "rs_mode": ("sm", "ce", "gemm"), "rs_dtype": ("bf16", "fp8")}
 
 
 def _spec(code: str, name: str, parallel: str, comm: str) -> SchemeSpec:
@@ -81,13 +83,19 @@ def build_layer(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, exchange: Any =
                  ckpt.shared_w2.scale.to(device))
         sv = tp_views(*sargs, ctx.rank, ctx.world_size) if spec.parallel == "TP" else tp_views(*sargs, 0, 1)
         shared = ExpertWeights.prepare(sv["w1"], sv["w1_scale"], sv["w2"], sv["w2_scale"])
+    rs_dtype = (tunables or {}).get("rs_dtype", "bf16")
     if exchange is None and ctx.world_size > 1:
         if EXCHANGE.get(spec.code) == "p2p":
             t = {k: v.default for k, v in P2P_TUNABLES.items()}
             t.update({k: v for k, v in (tunables or {}).items() if k in P2P_TUNABLES})
-            exchange = P2PExchange(ctx.group, chunks=t["rs_chunks"], rs_mode=t["rs_mode"], ag_mode=t["ag_mode"])
+            rs_mode = t["rs_mode"]
+            if rs_dtype == "fp8":
+                if rs_mode != "sm":
+                    raise SchemeConfigError(f"{spec.code}.rs_dtype='fp8' needs rs_mode='sm', got {rs_mode!r}")
+                rs_mode = "fp8"
+            exchange = P2PExchange(ctx.group, chunks=t["rs_chunks"], rs_mode=rs_mode, ag_mode=t["ag_mode"])
         else:
-            exchange = NcclExchange(ctx.group)
+            exchange = NcclExchange(ctx.group, rs_dtype=rs_dtype)
     expert_map = views.get("expert_map")
     layer = MoELayer(weights, T, s.top_k, s.E, expert_map=expert_map, shared=shared, exchange=exchange,
                      device=device)
@@ -101,6 +109,9 @@ def build_instance(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, scheme_cfg: 
     for name, allowed in _CHOICES.items():
         if name in tunables and tunables[name] not in allowed:
             raise SchemeConfigError(f"{spec.code}.{name}={tunables[name]!r} violates schema: expected one of {allowed}")
+    if tunables.get("rs_dtype") == "fp8" and tunables.get("rs_mode", "sm") != "sm":
+        raise SchemeConfigError(f"{spec.code}.rs_dtype='fp8' violates schema: needs rs_mode='sm', got "
+                                f"{tunables['rs_mode']!r}")
     if "rs_chunks" in tunables and not 1 <= tunables["rs_chunks"] <= 8:
         raise SchemeConfigError(f"{spec.code}.rs_chunks={tunables['rs_chunks']} violates schema: expected 1..8")
     bundle = require_data(data)

@@ -15,7 +15,11 @@ torch on the GPU, for shapes where a host restatement would take minutes:
   the calibration measure of ``tests/calibrate_tolerance.py:17-25``.
 * ``compare_outputs`` -- the gate metrics.
 * ``check_layer`` -- the gates plus max-abs <= 1.5 x calibration (the calibration
-  script's tight-atol rule), as one report.
+  script's tight-atol rule), as one report;
+* ``rank_partials`` / ``rs_fp8_error`` -- the golden split into each rank's partial sum
+  (its experts under EP, its intermediate slice under TP) and the extra error of the FP8
+  reduce-scatter payload (``overlap_forward.py:900-946``): max |sum_r p_r - sum_r QDQ(bf16(p_r))|,
+  the calibration term added to the bound when the partials cross as FP8.
 
 It is a checker: nothing on the layer's forward path calls it.
 """
@@ -82,6 +86,55 @@ def golden_rows(hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torc
 
 
 @torch.no_grad()
+def rank_partials(hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, ckpt: Any, world: int,
+                  parallel: str) -> torch.Tensor:
+    """fp32 [world, rows, H]: rank r's share of the golden of these rows before the reduce-scatter.
+
+    EP: the routed pairs of experts [r*E/world, (r+1)*E/world) (the shared expert is added after
+    the reduce-scatter and is not part of any partial).  TP: every routed pair restricted to
+    intermediate columns [r*I/world, (r+1)*I/world) (and the same slice of the shared expert);
+    needs I/world to be a multiple of 128 so the slices align with the quantisation groups."""
+    x = hidden.float()
+    E, H, I = ckpt.w1.fp8.shape[0], ckpt.w2.fp8.shape[1], ckpt.w2.fp8.shape[2]
+    out = torch.zeros((world, x.shape[0], H), dtype=torch.float32, device=x.device)
+    ids = topk_ids.long()
+
+    def tp_split(xr: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, scale: torch.Tensor | None, rows):
+        inter = w2.shape[1]
+        if inter % world or (inter // world) % 128:
+            raise ValueError(f"TP slices of I={inter} over {world} ranks are not 128-aligned")
+        gu = qdq128(xr) @ w1.T
+        h = qdq128(F.silu(gu[:, :inter]) * gu[:, inter:])
+        for r in range(world):
+            sl = slice(r * inter // world, (r + 1) * inter // world)
+            y = h[:, sl] @ w2[:, sl].T
+            out[r].index_add_(0, rows, y if scale is None else y * scale)
+
+    for e in torch.unique(ids).tolist():
+        rows, slots = torch.nonzero(ids == e, as_tuple=True)
+        w1 = dequant_bf16(ckpt.w1.fp8[e].to(x.device), ckpt.w1.scale[e].to(x.device))
+        w2 = dequant_bf16(ckpt.w2.fp8[e].to(x.device), ckpt.w2.scale[e].to(x.device))
+        wt = topk_weights[rows, slots].float()[:, None]
+        if parallel == "EP":
+            out[e // (E // world)].index_add_(0, rows, _ffn(x[rows], w1, w2, True) * wt)
+        else:
+            tp_split(x[rows], w1, w2, wt, rows)
+    if parallel != "EP" and getattr(ckpt, "shared_w1", None) is not None:
+        sw1 = dequant_bf16(ckpt.shared_w1.fp8[0].to(x.device), ckpt.shared_w1.scale[0].to(x.device))
+        sw2 = dequant_bf16(ckpt.shared_w2.fp8[0].to(x.device), ckpt.shared_w2.scale[0].to(x.device))
+        tp_split(x, sw1, sw2, None, torch.arange(x.shape[0], device=x.device))
+    return out
+
+
+@torch.no_grad()
+def rs_fp8_error(partials: torch.Tensor) -> float:
+    """max |sum_r p_r - sum_r QDQ128(bf16(p_r))| over the rows: the error the FP8 payload adds."""
+    exact = partials.sum(0)
+    q = torch.stack([qdq128(p.to(torch.bfloat16).float()) for p in partials]).sum(0)
+    return float((exact - q).abs().max())
+
+
+@torch.no_grad()
 def compare_outputs(actual: torch.Tensor, expected: torch.Tensor, cos_threshold: float = 0.995,
                     rel_p99_threshold: float = 5.0, scale_tolerance: float = 0.05) -> dict:
     """Gate metrics of ``moe_bench/verify.py:50-105`` (float64 on the device)."""
@@ -107,12 +160,13 @@ def compare_outputs(actual: torch.Tensor, expected: torch.Tensor, cos_threshold:
 
 @torch.no_grad()
 def check_layer(out: torch.Tensor, hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
-                ckpt: Any) -> dict:
+                ckpt: Any, extra_calib: float = 0.0) -> dict:
     """Layer output rows vs the fp32 golden of the same tokens: the worker's gates plus
-    max-abs <= 1.5 x the activation-quantisation error calibrated on these rows."""
+    max-abs <= 1.5 x (the activation-quantisation error calibrated on these rows +
+    ``extra_calib``, e.g. ``rs_fp8_error`` when the partials crossed as FP8)."""
     g = golden_rows(hidden, topk_ids, topk_weights, ckpt, act_quant=True)
     g_plain = golden_rows(hidden, topk_ids, topk_weights, ckpt, act_quant=False)
-    calib = float((g - g_plain).abs().max())
+    calib = float((g - g_plain).abs().max()) + extra_calib
     rep = compare_outputs(out.float(), g, **GATES)
     rep["calib"] = calib
     rep["max_abs_bound"] = MAX_ABS_FACTOR * calib

@@ -549,3 +549,67 @@ def test_gemm1_pushes_own_rows_to_peers(world, rank):
         assert torch.equal(peers_a[d].cpu()[mask], a_sorted.view(torch.uint8).cpu()[mask])
         assert not peers_a[d].cpu()[~mask].any()
         assert torch.equal(peers_s[d].cpu()[:, mask], a_st.cpu()[:, mask])
+
+
+# ---------------------------------------------------------------- FP8 reduce-scatter (b3 payload)
+@pytest.mark.parametrize("world,k,H,shared,ep", [(2, 2, 256, False, False), (4, 8, 384, True, False),
+                                                 (4, 2, 1024, False, True), (8, 1, 128, False, False)])
+def test_fp8_reduce_scatter_bit_exact(world, k, H, shared, ep):
+    """Every source rank pushes its FP8-quantised partials (codes + scales) to the owners, then
+    every owner dequant-sums its slots in rank order: all ranks emulated on one GPU, each with
+    its own buffers; codes, scales, flags and outputs bit-exact against the oracle."""
+    from oracle import rs as ors
+    from td_benchmark_b200 import _lib
+    from td_benchmark_b200.symm import ptr_array
+
+    Tl = 24
+    T = world * Tl
+    E = 16
+    st = [_bf16((T * k, H), 50 + r, 0.5) for r in range(world)]
+    sh = [_bf16((T, H), 70 + r) if shared else None for r in range(world)]
+    ids = torch.stack([torch.randperm(E, generator=torch.Generator().manual_seed(900 + t))[:k] for t in range(T)])
+    ids = ids.to(torch.int32).contiguous()
+    emaps = []
+    for r in range(world):
+        m = torch.full((E,), -1, dtype=torch.int32)
+        lo = r * E // world
+        m[lo:lo + E // world] = torch.arange(E // world, dtype=torch.int32)
+        emaps.append(m)
+    codes = [torch.zeros((T, H), dtype=torch.uint8, device=DEV) for _ in range(world)]
+    scales = [torch.zeros((T, H // 128), dtype=torch.float32, device=DEV) for _ in range(world)]
+    flags = [torch.zeros(world, dtype=torch.int32, device=DEV) for _ in range(world)]
+    counter = torch.zeros(1, dtype=torch.int32, device=DEV)
+    stream = torch.cuda.current_stream(DEV).cuda_stream
+    ids_d = ids.to(DEV)
+    for r in range(world):
+        sd, shd, em = st[r].to(DEV), None if sh[r] is None else sh[r].to(DEV), emaps[r].to(DEV)
+        _lib.call("b2m_combine_push_fp8", sd.data_ptr(), T, k, H, ids_d.data_ptr() if ep else None,
+                  em.data_ptr() if ep else None, None if shd is None else shd.data_ptr(), world, r,
+                  ptr_array([c.data_ptr() for c in codes]), ptr_array([s.data_ptr() for s in scales]),
+                  ptr_array([f.data_ptr() + 4 * r for f in flags]), 7, counter.data_ptr(), stream)
+        torch.cuda.synchronize(DEV)
+    outs = []
+    status = ops.new_status(DEV)
+    for o in range(world):
+        out = torch.empty((Tl, H), dtype=torch.bfloat16, device=DEV)
+        _lib.call("b2m_rs_reduce_fp8", codes[o].data_ptr(), scales[o].data_ptr(), Tl, H, world, flags[o].data_ptr(),
+                  7, None, out.data_ptr(), status.data_ptr(), stream)
+        outs.append(out)
+    torch.cuda.synchronize(DEV)
+    assert int(status.item()) == 0 and int(counter.item()) == 0
+    assert all(torch.equal(f.cpu(), torch.full((world,), 7, dtype=torch.int32)) for f in flags)
+    # oracle: each source's partials, quantised, land in the owners' slots
+    exp_codes = np.zeros((world, T, H), np.uint8)
+    exp_scales = np.zeros((world, T, H // 128), np.float32)
+    for r in range(world):
+        mask = (emaps[r][ids.long()] >= 0).numpy() if ep else None
+        part = ors.combine_rows(st[r].float().numpy(), k, None if sh[r] is None else sh[r].float().numpy(), mask)
+        q, s = ors.rs_fp8_push(part)
+        for o in range(world):
+            exp_codes[o, r * Tl:(r + 1) * Tl] = q[o * Tl:(o + 1) * Tl]
+            exp_scales[o, r * Tl:(r + 1) * Tl] = s[o * Tl:(o + 1) * Tl]
+    for o in range(world):
+        assert np.array_equal(codes[o].cpu().numpy(), exp_codes[o])
+        assert np.array_equal(scales[o].cpu().numpy(), exp_scales[o])
+        exp = ors.rs_fp8_reduce(exp_codes[o].reshape(world, Tl, H), exp_scales[o].reshape(world, Tl, H // 128))
+        assert np.array_equal(outs[o].view(torch.int16).cpu().numpy().astype(np.uint16), exp)

@@ -42,6 +42,11 @@ def _port() -> int:
     ("d3", "mixtral", 512, ["--ag-mode", "push"]),
     ("d3", "mixtral", 1024, ["--ag-mode", "push", "--rs-mode", "gemm"]),
     ("d3", "qwen3", 256, ["--ag-mode", "push"]),
+    # FP8 reduce-scatter payload (the b3 variant): peer memory and NCCL all-to-all
+    ("d3", "mixtral", 512, ["--rs-dtype", "fp8"]),
+    ("d4", "dsv3", 1024, ["--zipf", "--rs-dtype", "fp8"]),
+    ("d1", "mixtral", 512, ["--rs-dtype", "fp8"]),
+    ("d2", "dsv3", 512, ["--rs-dtype", "fp8"]),
 ], ids=lambda v: "-".join(a.strip("-") for a in v) if isinstance(v, list) else str(v))
 def test_multi_gpu_scheme_matches_golden(scheme, preset, tokens, extra):
     n = min(_gpus(), 4)

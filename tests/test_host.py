@@ -97,7 +97,7 @@ def test_scheme_registry_and_tunables():
     assert {"d1", "d2"} <= set(REGISTRY)
     spec, _ = REGISTRY["d1"]
     assert spec.weight_dtype == "fp8" and spec.act_quant == "group128" and not spec.requires_nvshmem
-    assert validate_tunables(spec, {}) == {"check_status": False}
+    assert validate_tunables(spec, {}) == {"check_status": False, "rs_dtype": "bf16"}
     with pytest.raises(SchemeConfigError, match="violate schema"):
         validate_tunables(spec, {"nope": 1})
     with pytest.raises(SchemeConfigError, match="expected bool"):
@@ -110,14 +110,20 @@ def test_scheme_registry_and_tunables():
 
 def test_p2p_exchange_tunables():
     spec, _ = REGISTRY["d3"]
-    assert validate_tunables(spec, {}) == {"check_status": False, "ag_mode": "auto", "rs_mode": "sm", "rs_chunks": 4}
+    assert validate_tunables(spec, {}) == {"check_status": False, "rs_dtype": "bf16", "ag_mode": "auto", "rs_mode": "sm",
+                                           "rs_chunks": 4}
     with pytest.raises(SchemeConfigError, match="violate schema"):
         validate_tunables(REGISTRY["d1"][0], {"ag_mode": "ce"})   # NCCL schemes have no exchange knobs
     with pytest.raises(SchemeConfigError, match="one of"):
         build_scheme(configs.preset("tiny"), None, None, SchemeCfg("d4", {"ag_mode": "dma"}))
     with pytest.raises(SchemeConfigError, match="1..8"):
         build_scheme(configs.preset("tiny"), None, None, SchemeCfg("d3", {"rs_chunks": 9}))
-    for ok in ({"ag_mode": "push"}, {"ag_mode": "ce", "rs_mode": "gemm"}, {"rs_mode": "ce", "rs_chunks": 8}):
+    with pytest.raises(SchemeConfigError, match="rs_dtype"):
+        build_scheme(configs.preset("tiny"), None, None, SchemeCfg("d3", {"rs_dtype": "fp8", "rs_mode": "gemm"}))
+    with pytest.raises(SchemeConfigError, match="one of"):
+        build_scheme(configs.preset("tiny"), None, None, SchemeCfg("d1", {"rs_dtype": "fp16"}))
+    for ok in ({"ag_mode": "push"}, {"ag_mode": "ce", "rs_mode": "gemm"}, {"rs_mode": "ce", "rs_chunks": 8},
+               {"rs_dtype": "fp8"}):
         with pytest.raises(RuntimeError, match="requires a DataBundle"):   # accepted; fails later for lack of data
             build_scheme(configs.preset("tiny"), None, None, SchemeCfg("d3", ok))
 

@@ -54,3 +54,16 @@ def test_check_layer_rejects_a_zero_output_and_accepts_the_golden():
     assert verify.check_layer(g.to(torch.bfloat16), h, ids, wts, b.ckpt)["pass"]
     bad = verify.check_layer(torch.zeros_like(g), h, ids, wts, b.ckpt)
     assert not bad["pass"] and bad["cos_sim"] == 0.0
+
+
+def test_rank_partials_sum_to_the_golden_ep_and_tp():
+    cfg = configs.preset("tiny", M=64)
+    b = data.build_bundle(cfg, device="cpu")
+    ids, wts, h = b.routing.topk_ids_full, b.routing.topk_weights_full, b.hidden_full
+    g = verify.golden_rows(h, ids, wts, b.ckpt)
+    for world, par in ((2, "EP"), (4, "EP"), (2, "TP"), (4, "TP")):
+        parts = verify.rank_partials(h, ids, wts, b.ckpt, world, par)
+        assert parts.shape == (world, 64, 256)
+        assert torch.allclose(parts.sum(0), g, rtol=1e-4, atol=1e-5), (world, par)
+        err = verify.rs_fp8_error(parts)
+        assert 0.0 < err < 0.1 * float(g.abs().max())
