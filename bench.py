@@ -157,7 +157,7 @@ def gemm1_flops(topk_ids, expert_map, inter_local: int, hidden: int) -> float:
     return 2.0 * pairs * 2 * inter_local * hidden
 
 
-def rank_work(layer, topk_ids, inter: int, shared_inter: int) -> dict:
+def rank_work(layer, topk_ids, inter: int, shared_inter: int, rs_fp8: bool = False) -> dict:
     """This rank's algorithmic work in one forward: FP8 FLOPs (routed pairs, unpadded, plus the
     shared expert), the expert weight bytes it must stream from HBM, and its NVLink bytes
     (all-gather received + reduce-scatter sent, bf16 partials) -- the three roofline terms.
@@ -177,8 +177,20 @@ def rank_work(layer, topk_ids, inter: int, shared_inter: int) -> dict:
         Is = shared_inter
         flops += 6.0 * H * Is * layer.shared.rows
         wbytes += 3.0 * H * Is * (1 + 4.0 / (128 * 128))
-    ag = (P - 1) * layer.T_local * (H + 4 * H // 128)
-    rs = (P - 1) * layer.T_local * 2 * H
+    row_fp8 = H + 4 * H // 128
+    rows = (P - 1) * layer.T_local          # dense: every other rank's tokens in, every partial out
+    ex = layer.exchange
+    if getattr(ex, "sparse", False):
+        # only the tokens of other ranks that route to one of this rank's experts cross in
+        # (all-gather) and their partials out (reduce-scatter)
+        r = ex.rank
+        tl = layer.T_local
+        rk = (topk_ids.long() // (layer.E // P))
+        hit = (rk == r).any(dim=1)
+        hit[r * tl:(r + 1) * tl] = False
+        rows = int(hit.sum().item())
+    ag = rows * row_fp8
+    rs = rows * (row_fp8 if rs_fp8 else 2 * H)
     return {"flops": flops, "weight_bytes": wbytes, "nvlink_bytes": float(ag + rs), "ag_bytes": ag, "rs_bytes": rs,
             "pairs": pairs, "experts_hit": hit}
 
@@ -433,6 +445,8 @@ def main() -> int:
                     help="fused all-gather: SM stores from the quant kernel, copy-engine copies, or by block size")
     ap.add_argument("--rs-dtype", default="bf16", choices=["bf16", "fp8"],
                     help="reduce-scatter payload: bf16 partials, or 1x128 e4m3 codes + scales (the b3 variant)")
+    ap.add_argument("--sparse", action="store_true",
+                    help="expert parallel: send tokens / partials only to / from the ranks holding their experts")
     ap.add_argument("--chunks", type=int, default=4, help="down-GEMM column chunks of the copy-engine push")
     ap.add_argument("--ce-streams", type=int, default=2, help="side streams carrying the copy-engine push")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -467,7 +481,7 @@ def main() -> int:
             raise SystemExit("--rs-dtype fp8 needs --rs-mode sm")
         exchange = P2PExchange(ctx.group, chunks=args.chunks,
                                rs_mode="fp8" if args.rs_dtype == "fp8" else args.rs_mode, ce_streams=args.ce_streams,
-                               ag_mode=args.ag_mode)
+                               ag_mode=args.ag_mode, sparse=args.sparse and cfg.parallel == "EP")
     elif world > 1:
         from td_benchmark_b200.layer import NcclExchange
         exchange = NcclExchange(ctx.group, rs_dtype=args.rs_dtype)
@@ -612,7 +626,7 @@ def main() -> int:
     s = cfg.shape
     inter_alg = s.intermediate // world if spec.parallel == "TP" else s.intermediate
     sh_alg = s.shared_intermediate // world if spec.parallel == "TP" else s.shared_intermediate
-    work = rank_work(layer, ids, inter_alg, sh_alg)
+    work = rank_work(layer, ids, inter_alg, sh_alg, rs_fp8=args.rs_dtype == "fp8")
     t_fp8 = work["flops"] / (fp8_peak * 1e12)
     t_nvl = work["nvlink_bytes"] / (nvl_peak * 1e9)
     t_hbm = work["weight_bytes"] / (hbm_peak * 1e9)
@@ -655,6 +669,7 @@ def main() -> int:
                        "routing": cfg.routing.imbalance_kind,
                        "rs_payload": args.rs_dtype if world > 1 else None,
                        "exchange": (f"p2p ag={layer.exchange.ag_mode} rs={layer.exchange.rs_mode} "
+                                    f"sparse={int(layer.exchange.sparse)} "
                                     f"chunks={len(layer.exchange.chunk_cols)}"
                                     if getattr(layer.exchange, "name", "") == "p2p" else
                                     getattr(layer.exchange, "name", "none")),

@@ -260,6 +260,17 @@ int b2m_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int
                    void* const* s_dst, int64_t row0, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
                    void* stream);
 
+/* Sparse expert-parallel all-gather (the dispatch of moe_bench/tdx/function/ep_moe_fused.py:375-517:
+ * a token goes only to the ranks that hold one of its experts): b2m_quant_push, except that
+ * token row0 + i is stored on rank d only when one of topk_ids[row0 + i, 0..top_k) lies in
+ * [d*experts_per_rank, (d+1)*experts_per_rank), and always on this rank (row0 / rows).
+ * topk_ids int32 [T, top_k] is the routing of all T tokens, the same on every rank; rows
+ * a destination does not receive keep stale contents, which its dispatch never reads
+ * (no pair of that token is local there).  row0 % rows == 0. */
+int b2m_quant_push_sparse(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world, void* const* q_dst,
+                          void* const* s_dst, int64_t row0, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
+                          const int32_t* topk_ids, int32_t top_k, int32_t experts_per_rank, void* stream);
+
 /* b2m_quant_push for callers that cannot allocate device memory (a runtime that
  * owns every device byte through its own arena, or code that may not call
  * cudaMalloc): no counter argument; the completion counter lives in a static
@@ -301,11 +312,14 @@ int b2m_dispatch_rows_wait(const void* xq, const float* xs, int64_t tokens, int6
  * (bf16 [world*T/world, hidden] on rank q); then *flag_dst[q] = epoch.  max_ctas > 0
  * caps the grid (the push shares the GPU with the next chunk's down GEMM).  With
  * counter == NULL nothing is published (flag_dst may be NULL): the partials are only
- * stored, e.g. into a local staging buffer that copy engines push afterwards. */
+ * stored, e.g. into a local staging buffer that copy engines push afterwards.
+ * sparse != 0 (expert parallel, needs expert_map): a token with no pair on this rank's
+ * experts is not sent at all; the owner's sparse reduce does not read that slot (the
+ * send-only-routed-rows combine of moe_bench/tdx/function/ep_moe_fused.py:375-517). */
 int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, int64_t col_begin,
                      int64_t col_end, const int32_t* topk_ids, const int32_t* expert_map, const void* shared,
                      int32_t world, int32_t rank, void* const* slot_dst, uint32_t* const* flag_dst, uint32_t epoch,
-                     int32_t* counter, int32_t max_ctas, void* stream);
+                     int32_t* counter, int32_t max_ctas, int32_t sparse, void* stream);
 
 /* Publishes epoch to every flag_dst[r] (own, peer or host-mapped memory) as stream
  * memory operations (cuStreamWriteValue32): ordered after all earlier work on
@@ -325,10 +339,14 @@ int b2m_rs_combine(const void* recv, int64_t rows, int32_t top_k, int64_t hidden
 
 /* Owner side of the reduce-scatter: once the nchunks*world flags (chunk-major) are all
  * >= epoch, out[t, :] = bf16( sum_{r=0..world-1} slots[r*rows + t, :] + add[t, :] )
- * (fp32, rank order).  add (bf16 [rows, hidden]) may be NULL. */
+ * (fp32, rank order).  add (bf16 [rows, hidden]) may be NULL.  With topk_ids (int32
+ * [rows, top_k], the routing of this owner's tokens; expert parallel, nchunks == 1) only
+ * the sources r holding one of token t's experts (expert / experts_per_rank == r) are
+ * summed -- the slots a sparse b2m_combine_push wrote; the others are zero partials, so
+ * the result is that of the dense sum. */
 int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world, int32_t nchunks,
-                  const uint32_t* flags, uint32_t epoch, const void* add, void* out, int32_t* dev_status,
-                  void* stream);
+                  const uint32_t* flags, uint32_t epoch, const void* add, void* out, const int32_t* topk_ids,
+                  int32_t top_k, int32_t experts_per_rank, int32_t* dev_status, void* stream);
 
 /* FP8 reduce-scatter push (replaces the b3 path's per-chunk rs_input quantisation +
  * all_to_all_single of codes and scales, moe_bench/overlap/overlap_forward.py:900-928).
@@ -337,20 +355,31 @@ int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world
  * e4m3) and stored at row rank*(T/world) + t - q*(T/world) of owner q = t / (T/world):
  * codes into code_dst[q] (u8 [T, hidden]), scales into scale_dst[q] (fp32 [T, hidden/128]).
  * Then *flag_dst[q] = epoch for every owner (counter == NULL: nothing published, e.g. when
- * a collective moves the slots afterwards).  hidden % 128 == 0. */
+ * a collective moves the slots afterwards).  hidden % 128 == 0.  sparse != 0: as for
+ * b2m_combine_push (tokens without a local pair are not sent). */
 int b2m_combine_push_fp8(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, const int32_t* topk_ids,
                          const int32_t* expert_map, const void* shared, int32_t world, int32_t rank,
                          void* const* code_dst, void* const* scale_dst, uint32_t* const* flag_dst, uint32_t epoch,
-                         int32_t* counter, void* stream);
+                         int32_t* counter, int32_t sparse, void* stream);
 
 /* Owner side of the FP8 reduce-scatter (replaces the dequant-sum of overlap_forward.py:933-946):
  * once flags[0..world) are all >= epoch (flags == NULL: no wait),
  *   out[t, :] = bf16( sum_{r=0..world-1} e4m3(codes[r*rows + t, :]) * scales[r*rows + t, group] + add[t, :] )
  * in fp32, rank order, one rounding.  codes u8 [world*rows, hidden], scales fp32
- * [world*rows, hidden/128]; add (bf16 [rows, hidden]) may be NULL. */
+ * [world*rows, hidden/128]; add (bf16 [rows, hidden]) may be NULL.  topk_ids /
+ * top_k / experts_per_rank: the sparse reduce, as for b2m_rs_reduce (NULL: dense). */
 int b2m_rs_reduce_fp8(const void* codes, const float* scales, int64_t rows, int64_t hidden, int32_t world,
-                      const uint32_t* flags, uint32_t epoch, const void* add, void* out, int32_t* dev_status,
-                      void* stream);
+                      const uint32_t* flags, uint32_t epoch, const void* add, void* out, const int32_t* topk_ids,
+                      int32_t top_k, int32_t experts_per_rank, int32_t* dev_status, void* stream);
+
+/* On-device routing (replaces the host-side steps of moe_bench/data/routing.py:58-64 that
+ * follow the gate GEMM): per token t, p = softmax(logits[t, :] + bias) (bias fp32 [E], may
+ * be NULL; the reference adds strength * log(E * target) under imbalanced routing), the k
+ * largest p in descending order (equal p: lower expert first) into topk_ids[t, :] (int32),
+ * and p / sum(selected p) into topk_weights[t, :] (fp32).  logits fp32 [tokens, E],
+ * 1 <= E <= 1024, 1 <= top_k <= min(32, E). */
+int b2m_route_topk(const float* logits, int64_t tokens, int32_t experts, int32_t top_k, const float* bias,
+                   int32_t* topk_ids, float* topk_weights, void* stream);
 
 #ifdef __cplusplus
 }

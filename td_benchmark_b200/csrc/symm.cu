@@ -68,6 +68,18 @@ __device__ __forceinline__ void publish_when_grid_done(int32_t* counter, const F
   }
 }
 
+// Bit r set when token t routes to at least one expert of rank r (experts [r*epr, (r+1)*epr)).
+// Expert parallel only: every rank holds the routing of all tokens, so source and
+// destination agree on this mask without exchanging any index.
+__device__ __forceinline__ uint32_t token_rank_mask(const int32_t* __restrict__ ids, int64_t t, int top_k, int epr) {
+  uint32_t m = 0;
+  for (int j = 0; j < top_k; ++j) {
+    const uint32_t r = static_cast<uint32_t>(__ldg(ids + t * top_k + j)) / static_cast<uint32_t>(epr);
+    m |= r < 32u ? 1u << r : 0u;  // an id outside [0, 32 * epr) names no rank
+  }
+  return m;
+}
+
 // ---------------------------------------------------------------- all-gather push
 // Eight lanes share one 128-group (16 consecutive values each), so a warp covers four
 // consecutive groups of a row and every store to a destination is one coalesced
@@ -78,7 +90,8 @@ __device__ __forceinline__ void publish_when_grid_done(int32_t* counter, const F
 __global__ void __launch_bounds__(kThreads)
     quant_push_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t rows, int64_t gpr, int world,
                       const __grid_constant__ PeerPtrs qdst, const __grid_constant__ PeerPtrs sdst, int64_t row0,
-                      const __grid_constant__ FlagPtrs flags, uint32_t epoch, int32_t* counter) {
+                      const __grid_constant__ FlagPtrs flags, uint32_t epoch, int32_t* counter,
+                      const int32_t* __restrict__ sparse_ids, int top_k, int epr) {
   const int lane = threadIdx.x & 31;
   const int sub = lane >> 3;  // group of the warp's four
   const int gl = lane & 7;    // 16-value slice of that group
@@ -86,7 +99,8 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t groups = rows * gpr;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
-  const int first = static_cast<int>((row0 / rows + 1) % world);
+  const int src = static_cast<int>(row0 / rows);
+  const int first = (src + 1) % world;
   for (int64_t base = warp * 4; base < groups; base += nwarps * 4) {
     const int64_t g = base + sub;
     uint4 raw0 = make_uint4(0, 0, 0, 0), raw1 = raw0;
@@ -112,8 +126,12 @@ __global__ void __launch_bounds__(kThreads)
       const uint2 q1 = quant8(f1, s);
       const uint4 q = make_uint4(q0.x, q0.y, q1.x, q1.y);
       const int64_t dst_row = row0 + row;
+      // sparse (expert parallel): only the ranks that hold one of the token's experts, and
+      // this rank (its own rows also feed its shared expert)
+      const uint32_t need = sparse_ids ? (token_rank_mask(sparse_ids, dst_row, top_k, epr) | (1u << src)) : ~0u;
       for (int i = 0; i < world; ++i) {
         const int r = first + i < world ? first + i : first + i - world;
+        if (!((need >> r) & 1u)) continue;
         *reinterpret_cast<uint4*>(static_cast<uint8_t*>(qdst.p[r]) + dst_row * cols + gi * 128 + gl * 16) = q;
         if (gl == 0) static_cast<float*>(sdst.p[r])[dst_row * gpr + gi] = s;
       }
@@ -247,13 +265,14 @@ __global__ void __launch_bounds__(kThreads)
                         int64_t col0, int64_t col1, const int32_t* __restrict__ topk_ids,
                         const int32_t* __restrict__ expert_map, const __nv_bfloat16* __restrict__ shared, int world,
                         int rank, const __grid_constant__ PeerPtrs slots, const __grid_constant__ FlagPtrs flags,
-                        uint32_t epoch, int32_t* counter) {
+                        uint32_t epoch, int32_t* counter, int sparse) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
   const int64_t per_rank = tokens / world;
   for (int64_t t = warp; t < tokens; t += nwarps) {
     const uint32_t mask = local_pair_mask(topk_ids, expert_map, t, top_k, lane);
+    if (sparse && mask == 0) continue;  // no local pair: the owner does not read this slot
     const int owner = static_cast<int>(t / per_rank);
     const int64_t slot_row = static_cast<int64_t>(rank) * per_rank + (t - owner * per_rank);
     __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(slots.p[owner]) + slot_row * hidden;
@@ -343,7 +362,7 @@ __global__ void __launch_bounds__(kThreads)
                             const int32_t* __restrict__ topk_ids, const int32_t* __restrict__ expert_map,
                             const __nv_bfloat16* __restrict__ shared, int world, int rank,
                             const __grid_constant__ PeerPtrs codes, const __grid_constant__ PeerPtrs scales,
-                            const __grid_constant__ FlagPtrs flags, uint32_t epoch, int32_t* counter) {
+                            const __grid_constant__ FlagPtrs flags, uint32_t epoch, int32_t* counter, int sparse) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
@@ -351,6 +370,7 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t gpr = hidden / 128;
   for (int64_t t = warp; t < tokens; t += nwarps) {
     const uint32_t mask = local_pair_mask(topk_ids, expert_map, t, top_k, lane);
+    if (sparse && mask == 0) continue;  // no local pair: the owner does not read this slot
     const int owner = static_cast<int>(t / per_rank);
     const int64_t slot_row = static_cast<int64_t>(rank) * per_rank + (t - owner * per_rank);
     uint8_t* qrow = static_cast<uint8_t*>(codes.p[owner]) + slot_row * hidden;
@@ -409,13 +429,74 @@ __global__ void __launch_bounds__(kThreads)
           const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(
               static_cast<__nv_fp8x2_storage_t>((w[i] >> (16 * j)) & 0xFFFFu), __NV_E4M3);
           const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&h));
-          a[4 * i + 2 * j] += d.x * sc;
-          a[4 * i + 2 * j + 1] += d.y * sc;
+          // dequantise, then add: two roundings, as the reference's (codes * scales).sum(0)
+          // (no fused multiply-add)
+          a[4 * i + 2 * j] = __fadd_rn(a[4 * i + 2 * j], __fmul_rn(d.x, sc));
+          a[4 * i + 2 * j + 1] = __fadd_rn(a[4 * i + 2 * j + 1], __fmul_rn(d.y, sc));
         }
       }
     }
     if (add) acc_bf16x8(*reinterpret_cast<const uint4*>(add + t * hidden + c), a);
     *reinterpret_cast<uint4*>(out + t * hidden + c) = pack_bf16x8(a);
+  }
+}
+
+// Owner side of the sparse expert-parallel reduce-scatter, either payload: one warp per
+// owned token; the sources summed are exactly the ranks holding one of the token's experts
+// (the same mask the sources used to decide whether to push), in rank order, fp32, plus
+// `add`, one rounding -- so the result equals the dense reduce, in which the other sources'
+// slots hold zero partials.  ids = the routing rows of this owner's tokens.
+template <bool kFp8>
+__global__ void __launch_bounds__(kThreads)
+    rs_reduce_sparse_kernel(const void* __restrict__ slots, const float* __restrict__ scales, int64_t rows,
+                            int64_t hidden, int world, const int32_t* __restrict__ ids, int top_k, int epr,
+                            const uint32_t* flags, uint32_t epoch, const __nv_bfloat16* __restrict__ add,
+                            __nv_bfloat16* __restrict__ out, int32_t* status, uint64_t timeout_ns) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if (flags && threadIdx.x < world && !wait_flag_geq(flags + threadIdx.x, epoch, timeout_ns, status,
+                                                     B2M_STATUS_TIMEOUT_PEER))
+    s_ok = 0;
+  __syncthreads();
+  if (!s_ok) return;  // status already records the timeout
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
+  const int64_t gpr = hidden / 128;
+  for (int64_t t = warp; t < rows; t += nwarps) {
+    const uint32_t rk = lane < top_k ? static_cast<uint32_t>(__ldg(ids + t * top_k + lane)) / static_cast<uint32_t>(epr)
+                                     : 32u;
+    const uint32_t mine = rk < 32u ? 1u << rk : 0u;
+    const uint32_t srcs = __reduce_or_sync(0xffffffffu, mine);
+    for (int64_t c = lane * 8; c < hidden; c += 256) {
+      float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int r = 0; r < world; ++r) {
+        if (!((srcs >> r) & 1u)) continue;
+        const int64_t row = static_cast<int64_t>(r) * rows + t;
+        if (kFp8) {
+          const uint2 q = __ldcg(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(slots) + row * hidden + c));
+          const float sc = __ldcg(scales + row * gpr + c / 128);
+          const uint32_t w[2] = {q.x, q.y};
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(
+                  static_cast<__nv_fp8x2_storage_t>((w[i] >> (16 * j)) & 0xFFFFu), __NV_E4M3);
+              const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&h));
+              a[4 * i + 2 * j] = __fadd_rn(a[4 * i + 2 * j], __fmul_rn(d.x, sc));
+              a[4 * i + 2 * j + 1] = __fadd_rn(a[4 * i + 2 * j + 1], __fmul_rn(d.y, sc));
+            }
+          }
+        } else {
+          acc_bf16x8(__ldcg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(slots) + row * hidden + c)),
+                     a);
+        }
+      }
+      if (add) acc_bf16x8(*reinterpret_cast<const uint4*>(add + t * hidden + c), a);
+      *reinterpret_cast<uint4*>(out + t * hidden + c) = pack_bf16x8(a);
+    }
   }
 }
 
@@ -570,8 +651,33 @@ int b2m_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int
   }
   const int64_t groups = rows * (hidden / 128);
   quant_push_kernel<<<grid_for(groups * 8, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), ldx, rows, hidden / 128, world, q, s, row0, f, epoch, counter);
+      static_cast<const __nv_bfloat16*>(x), ldx, rows, hidden / 128, world, q, s, row0, f, epoch, counter, nullptr, 0,
+      1);
   return check_cuda(cudaGetLastError(), "quant_push launch");
+}
+
+int b2m_quant_push_sparse(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world, void* const* q_dst,
+                          void* const* s_dst, int64_t row0, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
+                          const int32_t* topk_ids, int32_t top_k, int32_t experts_per_rank, void* stream) {
+  using namespace b2m;
+  int num_sms = 0;
+  B2M_TRY(require_sm100(&num_sms));
+  B2M_TRY(check_quant_push(x, rows, hidden, ldx, world, q_dst, s_dst, flag_dst, "quant_push_sparse"));
+  if (!counter || !topk_ids || top_k < 1 || top_k > 32 || experts_per_rank < 1 || row0 % rows)
+    return fail(B2M_ERR_ARG, "quant_push_sparse: need counter, topk_ids, 1 <= top_k <= 32, experts_per_rank >= 1 "
+                             "and row0 a multiple of rows");
+  PeerPtrs q{}, s{};
+  FlagPtrs f{};
+  for (int r = 0; r < world; ++r) {
+    q.p[r] = q_dst[r];
+    s.p[r] = s_dst[r];
+    f.p[r] = flag_dst[r];
+  }
+  const int64_t groups = rows * (hidden / 128);
+  quant_push_kernel<<<grid_for(groups * 8, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, rows, hidden / 128, world, q, s, row0, f, epoch, counter, topk_ids,
+      top_k, experts_per_rank);
+  return check_cuda(cudaGetLastError(), "quant_push_sparse launch");
 }
 
 int b2m_quant_push_noalloc(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world,
@@ -646,15 +752,16 @@ int b2m_dispatch_rows_wait(const void* xq, const float* xs, int64_t tokens, int6
 int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, int64_t col_begin,
                      int64_t col_end, const int32_t* topk_ids, const int32_t* expert_map, const void* shared,
                      int32_t world, int32_t rank, void* const* slot_dst, uint32_t* const* flag_dst, uint32_t epoch,
-                     int32_t* counter, int32_t max_ctas, void* stream) {
+                     int32_t* counter, int32_t max_ctas, int32_t sparse, void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
   if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || tokens <= 0 || tokens % world ||
       hidden % 8 || top_k <= 0)
     return fail(B2M_ERR_ARG, "combine_push: bad shape (tokens %% world == 0, hidden %% 8 == 0)");
-  if (!staged || !slot_dst || (counter && !flag_dst) || (expert_map && !topk_ids) || !aligned16(staged))
-    return fail(B2M_ERR_ARG, "combine_push: bad pointers");
+  if (!staged || !slot_dst || (counter && !flag_dst) || (expert_map && !topk_ids) || !aligned16(staged) ||
+      (sparse && !expert_map))
+    return fail(B2M_ERR_ARG, "combine_push: bad pointers (sparse needs the expert map)");
   if (col_end <= 0) col_end = hidden;
   if (col_begin < 0 || col_begin % 8 || col_end % 8 || col_end > hidden || col_begin >= col_end)
     return fail(B2M_ERR_ARG, "combine_push: column window [%lld, %lld) outside [0, %lld) or not 8-aligned",
@@ -671,7 +778,7 @@ int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t 
   if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
   combine_push_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, col_begin, col_end, topk_ids, expert_map,
-      static_cast<const __nv_bfloat16*>(shared), world, rank, sl, f, epoch, counter);
+      static_cast<const __nv_bfloat16*>(shared), world, rank, sl, f, epoch, counter, sparse);
   return check_cuda(cudaGetLastError(), "combine_push launch");
 }
 
@@ -705,14 +812,22 @@ int b2m_rs_combine(const void* recv, int64_t rows, int32_t top_k, int64_t hidden
 }
 
 int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world, int32_t nchunks,
-                  const uint32_t* flags, uint32_t epoch, const void* add, void* out, int32_t* dev_status,
-                  void* stream) {
+                  const uint32_t* flags, uint32_t epoch, const void* add, void* out, const int32_t* topk_ids,
+                  int32_t top_k, int32_t experts_per_rank, int32_t* dev_status, void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
   if (world < 1 || world > kMaxWorld || rows <= 0 || hidden % 8 || !slots || !flags || !out ||
       !aligned16(slots) || !aligned16(out) || (add && !aligned16(add)) || nchunks < 1 || nchunks * world > kThreads)
     return fail(B2M_ERR_ARG, "rs_reduce: bad shape/pointers/chunks");
+  if (topk_ids) {  // sparse expert-parallel reduce: only the sources holding one of the token's experts
+    if (nchunks != 1 || top_k < 1 || top_k > 32 || experts_per_rank < 1)
+      return fail(B2M_ERR_ARG, "rs_reduce: sparse reduce needs nchunks == 1, 1 <= top_k <= 32, experts_per_rank >= 1");
+    rs_reduce_sparse_kernel<false><<<grid_for(rows * 32, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        slots, nullptr, rows, hidden, world, topk_ids, top_k, experts_per_rank, flags, epoch,
+        static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out), dev_status, timeout_ns());
+    return check_cuda(cudaGetLastError(), "rs_reduce (sparse) launch");
+  }
   rs_reduce_kernel<<<grid_for(rows * (hidden / 8), num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(slots), rows, hidden, world, nchunks * world, flags, epoch,
       static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out), dev_status, timeout_ns());
@@ -722,7 +837,7 @@ int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world
 int b2m_combine_push_fp8(const void* staged, int64_t tokens, int32_t top_k, int64_t hidden, const int32_t* topk_ids,
                          const int32_t* expert_map, const void* shared, int32_t world, int32_t rank,
                          void* const* code_dst, void* const* scale_dst, uint32_t* const* flag_dst, uint32_t epoch,
-                         int32_t* counter, void* stream) {
+                         int32_t* counter, int32_t sparse, void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
@@ -730,8 +845,8 @@ int b2m_combine_push_fp8(const void* staged, int64_t tokens, int32_t top_k, int6
       hidden <= 0 || hidden % 128 || top_k <= 0)
     return fail(B2M_ERR_ARG, "combine_push_fp8: bad shape (tokens %% world == 0, hidden %% 128 == 0)");
   if (!staged || !code_dst || !scale_dst || (counter && !flag_dst) || (expert_map && !topk_ids) ||
-      !aligned16(staged) || (shared && !aligned16(shared)))
-    return fail(B2M_ERR_ARG, "combine_push_fp8: bad pointers");
+      !aligned16(staged) || (shared && !aligned16(shared)) || (sparse && !expert_map))
+    return fail(B2M_ERR_ARG, "combine_push_fp8: bad pointers (sparse needs the expert map)");
   PeerPtrs q{}, sc{};
   FlagPtrs f{};
   for (int r = 0; r < world; ++r) {
@@ -744,19 +859,27 @@ int b2m_combine_push_fp8(const void* staged, int64_t tokens, int32_t top_k, int6
   }
   combine_push_fp8_kernel<<<grid_for(tokens * 32, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, topk_ids, expert_map,
-      static_cast<const __nv_bfloat16*>(shared), world, rank, q, sc, f, epoch, counter);
+      static_cast<const __nv_bfloat16*>(shared), world, rank, q, sc, f, epoch, counter, sparse);
   return check_cuda(cudaGetLastError(), "combine_push_fp8 launch");
 }
 
 int b2m_rs_reduce_fp8(const void* codes, const float* scales, int64_t rows, int64_t hidden, int32_t world,
-                      const uint32_t* flags, uint32_t epoch, const void* add, void* out, int32_t* dev_status,
-                      void* stream) {
+                      const uint32_t* flags, uint32_t epoch, const void* add, void* out, const int32_t* topk_ids,
+                      int32_t top_k, int32_t experts_per_rank, int32_t* dev_status, void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
   if (world < 1 || world > kMaxWorld || rows <= 0 || hidden <= 0 || hidden % 128 || !codes || !scales || !out ||
       (reinterpret_cast<uintptr_t>(codes) & 7u) || !aligned16(out) || (add && !aligned16(add)))
     return fail(B2M_ERR_ARG, "rs_reduce_fp8: bad shape/pointers (hidden %% 128 == 0, 16-byte rows)");
+  if (topk_ids) {
+    if (top_k < 1 || top_k > 32 || experts_per_rank < 1)
+      return fail(B2M_ERR_ARG, "rs_reduce_fp8: sparse reduce needs 1 <= top_k <= 32, experts_per_rank >= 1");
+    rs_reduce_sparse_kernel<true><<<grid_for(rows * 32, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        codes, scales, rows, hidden, world, topk_ids, top_k, experts_per_rank, flags, epoch,
+        static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out), dev_status, timeout_ns());
+    return check_cuda(cudaGetLastError(), "rs_reduce_fp8 (sparse) launch");
+  }
   rs_reduce_fp8_kernel<<<grid_for(rows * (hidden / 8), num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(codes), scales, rows, hidden, world, flags, epoch,
       static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out), dev_status, timeout_ns());

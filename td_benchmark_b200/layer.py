@@ -216,13 +216,13 @@ class NcclExchange:
                       None if ids is None else ids.data_ptr(),
                       None if layer.expert_map is None else layer.expert_map.data_ptr(),
                       None if shared_out is None else shared_out.data_ptr(), self.world_size, self.rank, self._q_dst,
-                      self._s_dst, None, 0, None, st)
+                      self._s_dst, None, 0, None, 0, st)
             self.dist.all_to_all_single(self.recv_q, self.send_q, group=self.group)
             self.dist.all_to_all_single(self.recv_s, self.send_s, group=self.group)
             add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
             _lib.call("b2m_rs_reduce_fp8", self.recv_q.data_ptr(), self.recv_s.data_ptr(), layer.T_local, layer.H,
                       self.world_size, None, 0, None if add is None else add.data_ptr(), layer.out_local.data_ptr(),
-                      layer.status.data_ptr(), st)
+                      None, 0, 0, layer.status.data_ptr(), st)
             return layer.out_local
         ops.combine(layer.staged, layer.top_k, ids, layer.expert_map, shared_out, self.partial)
         self.dist.reduce_scatter_tensor(layer.out_local, self.partial, group=self.group)
@@ -295,12 +295,14 @@ class P2PExchange:
     MAX_CHUNKS = 8
     AG_CE_MIN_BYTES = 6 << 20   # between the measured win (7 MiB blocks) and loss (2 MiB blocks)
 
-    def __init__(self, group=None, chunks: int = 4, rs_mode: str = "sm", ce_streams: int = 2, ag_mode: str = "auto"):
+    def __init__(self, group=None, chunks: int = 4, rs_mode: str = "sm", ce_streams: int = 2, ag_mode: str = "auto",
+                 sparse: bool = False):
         import torch.distributed as dist
         if rs_mode not in ("ce", "sm", "gemm", "fp8") or ag_mode not in ("ce", "sm", "auto", "push"):
             raise ValueError(f"rs_mode must be 'gemm', 'ce', 'sm' or 'fp8' and ag_mode 'push', 'ce', 'sm' or 'auto', "
                              f"got {rs_mode!r}, {ag_mode!r}")
         self.ag_mode = ag_mode
+        self.sparse = sparse
         self.dist = dist
         self.group = group
         self.world_size = dist.get_world_size(group)
@@ -316,6 +318,14 @@ class P2PExchange:
         from .symm import SymmetricWorkspace, ptr_array
 
         P, T, H, Tl = self.world_size, layer.T, layer.H, layer.T_local
+        if self.sparse:
+            # sends decided per (token, rank) by SM stores: no contiguous-block copies
+            if not layer.ep or self.ag_mode in ("ce", "push") or self.rs_mode not in ("sm", "fp8"):
+                raise ValueError("sparse exchange needs expert parallelism, ag_mode 'sm'/'auto' and rs_mode 'sm'/'fp8'")
+            if layer.E % P:
+                raise ValueError(f"sparse exchange needs E={layer.E} divisible by world_size={P}")
+            self.ag_mode = "sm"
+            self.epr = layer.E // P
         if self.ag_mode == "auto":
             self.ag_mode = "ce" if Tl * H >= self.AG_CE_MIN_BYTES else "sm"
         if self.rs_mode == "gemm" and layer.shared is not None and not layer.ep:
@@ -408,7 +418,11 @@ class P2PExchange:
         if self.ag_mode == "push":
             self._push_own(layer, x_local, self.epoch)
             return
-        if self.ag_mode == "sm":
+        if self.ag_mode == "sm" and self.sparse:
+            _lib.call("b2m_quant_push_sparse", x_local.data_ptr(), Tl, H, x_local.stride(0), self.world_size,
+                      self._q_dst, self._s_dst, self.rank * Tl, self._ag_dst, self.epoch, self.counters,
+                      layer.cur_ids.data_ptr(), layer.top_k, self.epr, st)
+        elif self.ag_mode == "sm":
             _lib.call("b2m_quant_push", x_local.data_ptr(), Tl, H, x_local.stride(0), self.world_size, self._q_dst,
                       self._s_dst, self.rank * Tl, self._ag_dst, self.epoch, self.counters, st)
         else:
@@ -531,14 +545,14 @@ class P2PExchange:
             layer.gemm2(topk_weights)
             layer._event("gemm2_end")
             _lib.call("b2m_combine_push", layer.staged.data_ptr(), layer.T, layer.top_k, H, 0, H, idsp, emap, shp,
-                      P, self.rank, self._slot_dst, self._rs_dst, self.epoch, self.counters + 4, 0,
+                      P, self.rank, self._slot_dst, self._rs_dst, self.epoch, self.counters + 4, 0, int(self.sparse),
                       compute.cuda_stream)
         else:
             pb = self.partial.data_ptr()
             for c, (c0, c1) in enumerate(self.chunk_cols):
                 layer.gemm2(topk_weights, cols=(c0, c1))
                 _lib.call("b2m_combine_push", layer.staged.data_ptr(), layer.T, layer.top_k, H, c0, c1, idsp, emap,
-                          shp, P, self.rank, self._stage_dst, None, 0, None, 0, compute.cuda_stream)
+                          shp, P, self.rank, self._stage_dst, None, 0, None, 0, 0, compute.cuda_stream)
                 self.chunk_ev[c].record(compute)
                 for s, peers in zip(self.ce, self._copies):
                     s.wait_event(self.chunk_ev[c])
@@ -555,8 +569,8 @@ class P2PExchange:
         if self.rs_mode == "ce":
             self._join_side(compute)   # staging buffer reuse by the next call
         _lib.call("b2m_rs_reduce", self.slots.data_ptr(), Tl, H, P, 1, self.rs_flags, self.epoch,
-                  None if add is None else add.data_ptr(), layer.out_local.data_ptr(), layer.status.data_ptr(),
-                  compute.cuda_stream)
+                  None if add is None else add.data_ptr(), layer.out_local.data_ptr(), *self._sparse_owner(layer),
+                  layer.status.data_ptr(), compute.cuda_stream)
         return layer.out_local
 
     def _fp8_push_reduce(self, layer: "MoELayer", idsp, emap, shp, add, compute) -> None:
@@ -565,11 +579,18 @@ class P2PExchange:
 
         _lib.call("b2m_combine_push_fp8", layer.staged.data_ptr(), layer.T, layer.top_k, layer.H, idsp, emap, shp,
                   self.world_size, self.rank, self._slotq_dst, self._slots_dst, self._rs_dst, self.epoch,
-                  self.counters + 4, compute.cuda_stream)
+                  self.counters + 4, int(self.sparse), compute.cuda_stream)
         layer._event("combine_end")
         _lib.call("b2m_rs_reduce_fp8", self.ws.local("slots_q"), self.ws.local("slots_s"), layer.T_local, layer.H,
                   self.world_size, self.rs_flags, self.epoch, None if add is None else add.data_ptr(),
-                  layer.out_local.data_ptr(), layer.status.data_ptr(), compute.cuda_stream)
+                  layer.out_local.data_ptr(), *self._sparse_owner(layer), layer.status.data_ptr(), compute.cuda_stream)
+
+    def _sparse_owner(self, layer: "MoELayer") -> tuple:
+        """(routing rows of this rank's tokens, top_k, experts per rank) for the sparse owner
+        reduce, or the dense reduce's (None, 0, 0)."""
+        if not self.sparse:
+            return None, 0, 0
+        return layer.cur_ids.data_ptr() + 4 * self.rank * layer.T_local * layer.top_k, layer.top_k, self.epr
 
     def exchange_alone(self, layer: "MoELayer", x_local: torch.Tensor, topk_ids: torch.Tensor) -> bool:
         """The all-gather and the reduce-scatter of one forward with no GEMM between them.
@@ -584,6 +605,7 @@ class P2PExchange:
 
         if self.ag_mode not in ("sm", "ce") or self.rs_mode not in ("sm", "fp8"):
             return False
+        layer.cur_ids = topk_ids
         self.gather_dispatch(layer, x_local, with_shared=False)
         compute = torch.cuda.current_stream(layer.device)
         emap = None if layer.expert_map is None else layer.expert_map.data_ptr()
@@ -593,10 +615,11 @@ class P2PExchange:
             return True
         _lib.call("b2m_combine_push", layer.staged.data_ptr(), layer.T, layer.top_k, layer.H, 0, layer.H, idsp, emap,
                   None, self.world_size, self.rank, self._slot_dst, self._rs_dst, self.epoch, self.counters + 4, 0,
-                  compute.cuda_stream)
+                  int(self.sparse), compute.cuda_stream)
         self._join_side(compute)
         _lib.call("b2m_rs_reduce", self.slots.data_ptr(), layer.T_local, layer.H, self.world_size, 1, self.rs_flags,
-                  self.epoch, None, layer.out_local.data_ptr(), layer.status.data_ptr(), compute.cuda_stream)
+                  self.epoch, None, layer.out_local.data_ptr(), *self._sparse_owner(layer), layer.status.data_ptr(),
+                  compute.cuda_stream)
         return True
 
     def extra_launches(self) -> int:
@@ -643,6 +666,7 @@ class MoELayer:
         self.route = _Routing(self.numel, global_num_experts, dev)
         H = self.H
         self.xq = self.xs = None   # token-order all-gather target, owned by the exchange
+        self.cur_ids = None        # routing of the current forward
         self.a_sorted = torch.empty((self.route.rows_cap, H), dtype=ops.FP8, device=dev)  # expert order
         self.as_t = torch.empty((H // 128, self.route.rows_cap), dtype=torch.float32, device=dev)
         self.inter_q = torch.empty((self.route.rows_cap, weights.inter), dtype=ops.FP8, device=dev)
@@ -671,6 +695,7 @@ class MoELayer:
     def route_and_dispatch(self, x_local: torch.Tensor, topk_ids: torch.Tensor) -> None:
         """Alignment, then quantisation + (all-gather) + row dispatch into expert order."""
         r = self.route
+        self.cur_ids = topk_ids   # the routing of this forward (the sparse exchange reads it)
         ops.moe_align_block_size(topk_ids, BM, self.E, self.expert_map, out=(r.sorted_ids, r.expert_ids, r.ntpp),
                                  pair_pos=r.pair_pos, block_pairs=r.pairs(self.paired))
         self._event("align_end")

@@ -228,3 +228,26 @@ def combine(staged: torch.Tensor, top_k: int, topk_ids: torch.Tensor | None = No
     _lib.call("b2m_combine", staged.data_ptr(), tokens, top_k, hidden, _ptr(topk_ids), _ptr(expert_map),
               _ptr(shared), out.data_ptr(), out.stride(0), _stream(staged.device))
     return out
+
+
+def route_topk(logits: torch.Tensor, top_k: int, bias: torch.Tensor | None = None,
+               out: tuple[torch.Tensor, torch.Tensor] | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 router logits [T, E] (+ per-expert bias [E]) -> (int32 ids [T, k], fp32 weights [T, k]):
+    softmax, top-k in descending order, renormalised (``moe_bench/data/routing.py:58-64``)."""
+    _cuda(logits, "logits")
+    _need(logits.dtype == torch.float32 and logits.dim() == 2 and logits.is_contiguous(),
+          "logits must be contiguous fp32 [T, E]")
+    tokens, experts = logits.shape
+    if bias is not None:
+        _need(bias.dtype == torch.float32 and bias.numel() == experts and bias.is_contiguous(), "bias must be fp32 [E]")
+    if out is None:
+        ids = torch.empty((tokens, top_k), dtype=torch.int32, device=logits.device)
+        wts = torch.empty((tokens, top_k), dtype=torch.float32, device=logits.device)
+    else:
+        ids, wts = out
+        _need(ids.dtype == torch.int32 and wts.dtype == torch.float32 and ids.is_contiguous() and wts.is_contiguous()
+              and tuple(ids.shape) == (tokens, top_k) and tuple(wts.shape) == (tokens, top_k),
+              "out must be contiguous int32 / fp32 [T, k]")
+    _lib.call("b2m_route_topk", logits.data_ptr(), tokens, experts, top_k, _ptr(bias), ids.data_ptr(), wts.data_ptr(),
+              _stream(logits.device))
+    return ids, wts

@@ -37,6 +37,12 @@ P2P_TUNABLES = {
                                       "epilogue ('gemm') or copy engines ('ce')"),
     "rs_chunks": TunableSpec(int, 4, "down-GEMM column chunks of the copy-engine reduce-scatter (1..8)"),
 }
+# expert-parallel peer-memory scheme only
+EP_SPARSE = {
+    "sparse": TunableSpec(bool, False, "send a token only to the ranks holding one of its experts and its partial only "
+                                       "from those ranks (all-gather and reduce-scatter by SM stores; same output as "
+                                       "the dense exchange, fewer NVLink bytes)"),
+}
 _CHOICES = {"ag_mode": ("sm", "ce", "auto", "push"), "rs_mode": ("sm", "ce", "gemm"), "rs_dtype": ("bf16", "fp8")}
 
 
@@ -44,6 +50,8 @@ def _spec(code: str, name: str, parallel: str, comm: str) -> SchemeSpec:
     schema = dict(B200_TUNABLES)
     if EXCHANGE.get(code) == "p2p":
         schema.update(P2P_TUNABLES)
+        if parallel == "EP":
+            schema.update(EP_SPARSE)
     return SchemeSpec(code=code, name=name, family="b200", parallel=parallel, comm=comm, weight_dtype="fp8",
                       act_quant="group128", requires_nvshmem=False, tunables_schema=schema)
 
@@ -93,7 +101,8 @@ def build_layer(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, exchange: Any =
                 if rs_mode != "sm":
                     raise SchemeConfigError(f"{spec.code}.rs_dtype='fp8' needs rs_mode='sm', got {rs_mode!r}")
                 rs_mode = "fp8"
-            exchange = P2PExchange(ctx.group, chunks=t["rs_chunks"], rs_mode=rs_mode, ag_mode=t["ag_mode"])
+            exchange = P2PExchange(ctx.group, chunks=t["rs_chunks"], rs_mode=rs_mode, ag_mode=t["ag_mode"],
+                                   sparse=bool((tunables or {}).get("sparse", False)))
         else:
             exchange = NcclExchange(ctx.group, rs_dtype=rs_dtype)
     expert_map = views.get("expert_map")

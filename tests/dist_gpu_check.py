@@ -27,6 +27,7 @@ def main() -> int:
     ap.add_argument("--rs-mode", default=None, help="d3/d4 tunable rs_mode")
     ap.add_argument("--rs-chunks", type=int, default=None, help="d3/d4 tunable rs_chunks")
     ap.add_argument("--rs-dtype", default=None, help="tunable rs_dtype (bf16 | fp8)")
+    ap.add_argument("--sparse", action="store_true", help="d4 tunable sparse; also checks it equals the dense exchange")
     args = ap.parse_args()
 
     import torch
@@ -50,11 +51,20 @@ def main() -> int:
                      ("rs_dtype", args.rs_dtype)):
         if val is not None:
             tun[key] = val
+    dense_out = None
+    if args.sparse:
+        dense = build_scheme(cfg, ctx, bundle, SchemeCfg(args.scheme, dict(tun, ag_mode="sm")))
+        dense_out = dense.run().clone()
+        torch.cuda.synchronize()
+        dense.close()
+        tun["sparse"] = True
     inst = build_scheme(cfg, ctx, bundle, SchemeCfg(args.scheme, tun))
     out1 = inst.run().clone()
     out2 = inst.run()
     torch.cuda.synchronize()
     same = bool(torch.equal(out1, out2))
+    if dense_out is not None:
+        same = same and bool(torch.equal(out2, dense_out))   # sparse sends change no bit of the result
     ck = bundle.ckpt
     sw = None
     if ck.shared_w1 is not None:

@@ -551,13 +551,20 @@ def test_gemm1_pushes_own_rows_to_peers(world, rank):
         assert torch.equal(peers_s[d].cpu()[:, mask], a_st.cpu()[:, mask])
 
 
-# ---------------------------------------------------------------- FP8 reduce-scatter (b3 payload)
-@pytest.mark.parametrize("world,k,H,shared,ep", [(2, 2, 256, False, False), (4, 8, 384, True, False),
-                                                 (4, 2, 1024, False, True), (8, 1, 128, False, False)])
-def test_fp8_reduce_scatter_bit_exact(world, k, H, shared, ep):
-    """Every source rank pushes its FP8-quantised partials (codes + scales) to the owners, then
-    every owner dequant-sums its slots in rank order: all ranks emulated on one GPU, each with
-    its own buffers; codes, scales, flags and outputs bit-exact against the oracle."""
+# ---------------------------------------------------------------- reduce-scatter push + owner reduce
+@pytest.mark.parametrize("payload,sparse,world,k,H,shared,ep", [
+    ("fp8", False, 2, 2, 256, False, False), ("fp8", False, 4, 8, 384, True, False),
+    ("fp8", False, 4, 2, 1024, False, True), ("fp8", False, 8, 1, 128, False, False),
+    ("fp8", True, 4, 2, 1024, False, True), ("fp8", True, 8, 8, 256, False, True),
+    ("bf16", False, 4, 8, 384, True, False), ("bf16", True, 4, 2, 512, False, True),
+    ("bf16", True, 8, 8, 256, False, True)])
+def test_reduce_scatter_emulated_bit_exact(payload, sparse, world, k, H, shared, ep):
+    """Every source rank pushes its partials (bf16, or FP8 codes + scales: the b3 payload) to
+    the owners, then every owner sums its slots in rank order: all ranks emulated on one GPU,
+    each with its own buffers; pushed slots, flags and outputs bit-exact against the oracle.
+    Sparse (expert parallel): a token's partial goes only from ranks holding one of its
+    experts, and the owner reads only those slots -- the others are prefilled with NaN here,
+    so reading one would show."""
     from oracle import rs as ors
     from td_benchmark_b200 import _lib
     from td_benchmark_b200.symm import ptr_array
@@ -565,6 +572,7 @@ def test_fp8_reduce_scatter_bit_exact(world, k, H, shared, ep):
     Tl = 24
     T = world * Tl
     E = 16
+    epr = E // world
     st = [_bf16((T * k, H), 50 + r, 0.5) for r in range(world)]
     sh = [_bf16((T, H), 70 + r) if shared else None for r in range(world)]
     ids = torch.stack([torch.randperm(E, generator=torch.Generator().manual_seed(900 + t))[:k] for t in range(T)])
@@ -572,44 +580,73 @@ def test_fp8_reduce_scatter_bit_exact(world, k, H, shared, ep):
     emaps = []
     for r in range(world):
         m = torch.full((E,), -1, dtype=torch.int32)
-        lo = r * E // world
-        m[lo:lo + E // world] = torch.arange(E // world, dtype=torch.int32)
+        m[r * epr:(r + 1) * epr] = torch.arange(epr, dtype=torch.int32)
         emaps.append(m)
-    codes = [torch.zeros((T, H), dtype=torch.uint8, device=DEV) for _ in range(world)]
-    scales = [torch.zeros((T, H // 128), dtype=torch.float32, device=DEV) for _ in range(world)]
+    fp8 = payload == "fp8"
+    if fp8:
+        slots = [torch.full((T, H), 0x7F, dtype=torch.uint8, device=DEV) for _ in range(world)]   # NaN codes
+        scales = [torch.full((T, H // 128), float("nan"), dtype=torch.float32, device=DEV) for _ in range(world)]
+    else:
+        slots = [torch.full((T, H), float("nan"), dtype=torch.bfloat16, device=DEV) for _ in range(world)]
     flags = [torch.zeros(world, dtype=torch.int32, device=DEV) for _ in range(world)]
     counter = torch.zeros(1, dtype=torch.int32, device=DEV)
     stream = torch.cuda.current_stream(DEV).cuda_stream
     ids_d = ids.to(DEV)
     for r in range(world):
         sd, shd, em = st[r].to(DEV), None if sh[r] is None else sh[r].to(DEV), emaps[r].to(DEV)
-        _lib.call("b2m_combine_push_fp8", sd.data_ptr(), T, k, H, ids_d.data_ptr() if ep else None,
-                  em.data_ptr() if ep else None, None if shd is None else shd.data_ptr(), world, r,
-                  ptr_array([c.data_ptr() for c in codes]), ptr_array([s.data_ptr() for s in scales]),
-                  ptr_array([f.data_ptr() + 4 * r for f in flags]), 7, counter.data_ptr(), stream)
+        fl = ptr_array([f.data_ptr() + 4 * r for f in flags])
+        idp, emp, shp = ids_d.data_ptr() if ep else None, em.data_ptr() if ep else None, \
+            None if shd is None else shd.data_ptr()
+        if fp8:
+            _lib.call("b2m_combine_push_fp8", sd.data_ptr(), T, k, H, idp, emp, shp, world, r,
+                      ptr_array([c.data_ptr() for c in slots]), ptr_array([s.data_ptr() for s in scales]), fl, 7,
+                      counter.data_ptr(), int(sparse), stream)
+        else:
+            _lib.call("b2m_combine_push", sd.data_ptr(), T, k, H, 0, H, idp, emp, shp, world, r,
+                      ptr_array([c.data_ptr() for c in slots]), fl, 7, counter.data_ptr(), 0, int(sparse), stream)
         torch.cuda.synchronize(DEV)
     outs = []
     status = ops.new_status(DEV)
     for o in range(world):
         out = torch.empty((Tl, H), dtype=torch.bfloat16, device=DEV)
-        _lib.call("b2m_rs_reduce_fp8", codes[o].data_ptr(), scales[o].data_ptr(), Tl, H, world, flags[o].data_ptr(),
-                  7, None, out.data_ptr(), status.data_ptr(), stream)
+        own_ids = ids_d[o * Tl:(o + 1) * Tl].contiguous()
+        sp = (own_ids.data_ptr(), k, epr) if sparse else (None, 0, 0)
+        if fp8:
+            _lib.call("b2m_rs_reduce_fp8", slots[o].data_ptr(), scales[o].data_ptr(), Tl, H, world,
+                      flags[o].data_ptr(), 7, None, out.data_ptr(), *sp, status.data_ptr(), stream)
+        else:
+            _lib.call("b2m_rs_reduce", slots[o].data_ptr(), Tl, H, world, 1, flags[o].data_ptr(), 7, None,
+                      out.data_ptr(), *sp, status.data_ptr(), stream)
         outs.append(out)
     torch.cuda.synchronize(DEV)
     assert int(status.item()) == 0 and int(counter.item()) == 0
     assert all(torch.equal(f.cpu(), torch.full((world,), 7, dtype=torch.int32)) for f in flags)
-    # oracle: each source's partials, quantised, land in the owners' slots
-    exp_codes = np.zeros((world, T, H), np.uint8)
-    exp_scales = np.zeros((world, T, H // 128), np.float32)
+    # oracle: each source's combined partials; with sparse, only the rows it holds a pair of
+    parts = []
+    sent = []
     for r in range(world):
         mask = (emaps[r][ids.long()] >= 0).numpy() if ep else None
-        part = ors.combine_rows(st[r].float().numpy(), k, None if sh[r] is None else sh[r].float().numpy(), mask)
-        q, s = ors.rs_fp8_push(part)
-        for o in range(world):
-            exp_codes[o, r * Tl:(r + 1) * Tl] = q[o * Tl:(o + 1) * Tl]
-            exp_scales[o, r * Tl:(r + 1) * Tl] = s[o * Tl:(o + 1) * Tl]
+        parts.append(ors.combine_rows(st[r].float().numpy(), k, None if sh[r] is None else sh[r].float().numpy(),
+                                      mask))
+        sent.append(mask.any(1) if (sparse and mask is not None) else np.ones(T, bool))
     for o in range(world):
-        assert np.array_equal(codes[o].cpu().numpy(), exp_codes[o])
-        assert np.array_equal(scales[o].cpu().numpy(), exp_scales[o])
-        exp = ors.rs_fp8_reduce(exp_codes[o].reshape(world, Tl, H), exp_scales[o].reshape(world, Tl, H // 128))
+        rows_o = slice(o * Tl, (o + 1) * Tl)
+        if fp8:
+            qs = [ors.rs_fp8_push(parts[r][rows_o]) for r in range(world)]
+            got_q, got_s = slots[o].cpu().numpy(), scales[o].cpu().numpy()
+            for r in range(world):
+                m = sent[r][rows_o]
+                assert np.array_equal(got_q[r * Tl:(r + 1) * Tl][m], qs[r][0][m])
+                assert np.array_equal(got_s[r * Tl:(r + 1) * Tl][m], qs[r][1][m])
+                assert sparse or m.all()
+            exp = ors.rs_fp8_reduce(np.stack([q[0] for q in qs]), np.stack([q[1] for q in qs]))
+        else:
+            got = slots[o].view(torch.int16).cpu().numpy().astype(np.uint16)
+            for r in range(world):
+                m = sent[r][rows_o]
+                assert np.array_equal(got[r * Tl:(r + 1) * Tl][m], parts[r][rows_o][m])
+            acc = np.zeros((Tl, H), np.float32)
+            for r in range(world):
+                acc = (acc + ofp8.bf16_bits_to_f32(parts[r][rows_o])).astype(np.float32)
+            exp = ofp8.f32_to_bf16_bits(acc)
         assert np.array_equal(outs[o].view(torch.int16).cpu().numpy().astype(np.uint16), exp)

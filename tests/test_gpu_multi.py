@@ -47,6 +47,9 @@ def _port() -> int:
     ("d4", "dsv3", 1024, ["--zipf", "--rs-dtype", "fp8"]),
     ("d1", "mixtral", 512, ["--rs-dtype", "fp8"]),
     ("d2", "dsv3", 512, ["--rs-dtype", "fp8"]),
+    # sparse expert-parallel exchange (bit-identical to the dense one)
+    ("d4", "dsv3", 1024, ["--zipf", "--sparse"]),
+    ("d4", "dsv3", 512, ["--sparse", "--rs-dtype", "fp8"]),
 ], ids=lambda v: "-".join(a.strip("-") for a in v) if isinstance(v, list) else str(v))
 def test_multi_gpu_scheme_matches_golden(scheme, preset, tokens, extra):
     n = min(_gpus(), 4)
