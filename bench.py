@@ -591,6 +591,29 @@ def main() -> int:
         dist.all_reduce(e_tot, op=dist.ReduceOp.MAX)
     e_ms = float(e_tot.item()) / args.steps
 
+    # diagnosis of the pipelined run (not part of the timed number): the same steps traced
+    # per stage, and the host<->device copies of a step alone, all ranks copying at once
+    tpipe = HostPipeline(layer, trace=True)
+    for i in range(args.steps):
+        tpipe.submit(x_h, ids_h, wts_h, outs_h[i % 2])
+    tpipe.drain()
+    spans = tpipe.spans()
+    torch.cuda.synchronize()
+    barrier()
+    x_c, ids_c, wts_c = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(wts)
+
+    def copies_alone():
+        with torch.cuda.stream(pipe.h2d):
+            x_c.copy_(x_h, non_blocking=True)
+            ids_c.copy_(ids_h, non_blocking=True)
+            wts_c.copy_(wts_h, non_blocking=True)
+        with torch.cuda.stream(pipe.d2h):
+            out_h.copy_(layer.out_local, non_blocking=True)
+        cur.wait_stream(pipe.h2d)
+        cur.wait_stream(pipe.d2h)
+
+    copy_ms = _mean_max_over_ranks(_timed(copies_alone, args.steps, args.warmup, flush, barrier), world, dev)
+
     x_d, ids_d, wts_d = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(wts)
 
     def e2e_step():
@@ -678,7 +701,13 @@ def main() -> int:
                     "d2h_bytes_per_step": d2h, "ms_per_step": e_ms,
                     "how": "HostPipeline: pinned-host inputs in and result out every step, double-buffered so the "
                            "copies of steps i+1 / i-1 overlap step i; whole run timed with CUDA events, max over ranks",
-                    "serial_ms_per_step": e_serial_ms},
+                    "serial_ms_per_step": e_serial_ms,
+                    "diag": {"pipeline_rank0": {k: round(v, 4) if isinstance(v, float) else v for k, v in spans.items()},
+                             "copies_alone_ms_per_step": copy_ms,
+                             "copies_alone_gbs": (h2d + d2h) / (copy_ms * 1e-3) / 1e9,
+                             "how": "traced pipelined steps (rank 0; forward_gap = forward waiting for its inputs); "
+                                    "copies alone = one step's h2d and d2h copies on their two streams, no forward, "
+                                    "every rank at once, max over ranks"}},
             "gpu_launches": layer.kernel_launches() * args.steps,
             "roofline": {"bound": "tensor", "kernel": "gemm1 (gate/up, tcgen05 kind::f8f6f4)",
                          "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s", "frac": achieved / fp8_peak,
