@@ -449,6 +449,8 @@ def main() -> int:
                     help="expert parallel: send tokens / partials only to / from the ranks holding their experts")
     ap.add_argument("--chunks", type=int, default=4, help="down-GEMM column chunks of the copy-engine push")
     ap.add_argument("--ce-streams", type=int, default=2, help="side streams carrying the copy-engine push")
+    ap.add_argument("--e2e-chunk-mb", type=float, default=1.0,
+                    help="host<->device copies of the e2e pipeline in pieces of this many MiB (0: whole tensors)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the post-run check against the fp32 golden")
     args = ap.parse_args()
@@ -567,7 +569,8 @@ def main() -> int:
     wts_h = wts.cpu().pin_memory()
     outs_h = [torch.empty(layer.out_local.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     out_h = outs_h[0]
-    pipe = HostPipeline(layer)
+    chunk = int(args.e2e_chunk_mb * (1 << 20))
+    pipe = HostPipeline(layer, chunk_bytes=chunk)
     cur = torch.cuda.current_stream(dev)
     for i in range(args.warmup):
         pipe.submit(x_h, ids_h, wts_h, outs_h[i % 2])
@@ -593,7 +596,7 @@ def main() -> int:
 
     # diagnosis of the pipelined run (not part of the timed number): the same steps traced
     # per stage, and the host<->device copies of a step alone, all ranks copying at once
-    tpipe = HostPipeline(layer, trace=True)
+    tpipe = HostPipeline(layer, trace=True, chunk_bytes=chunk)
     for i in range(args.steps):
         tpipe.submit(x_h, ids_h, wts_h, outs_h[i % 2])
     tpipe.drain()
