@@ -185,7 +185,7 @@ def rank_work(layer, topk_ids, inter: int, shared_inter: int, rs_fp8: bool = Fal
         # (all-gather) and their partials out (reduce-scatter)
         r = ex.rank
         tl = layer.T_local
-        rk = (topk_ids.long() // (layer.E // P))
+        rk = layer.expert_owner[topk_ids.long()]
         hit = (rk == r).any(dim=1)
         hit[r * tl:(r + 1) * tl] = False
         rows = int(hit.sum().item())
@@ -405,8 +405,9 @@ def check_parity(layer, bundle, x, ids, wts, world, rank, dev, parallel: str, rs
     hid = bundle.hidden_full[r0:r0 + n].to(dev)
     extra = 0.0
     if rs_fp8 and world > 1:
+        owner = None if layer.expert_owner is None else layer.expert_owner.cpu().tolist()
         extra = verify.rs_fp8_error(verify.rank_partials(hid, ids[r0:r0 + n], wts[r0:r0 + n], bundle.ckpt, world,
-                                                         parallel))
+                                                         parallel, owner))
     rep = verify.check_layer(out, hid, ids[r0:r0 + n], wts[r0:r0 + n], bundle.ckpt, extra_calib=extra)
     v = torch.tensor([1.0 if rep["pass"] else 0.0, rep["cos_sim"], rep["rel_p99"], rep["max_abs"], rep["calib"],
                       abs(rep["scale"] - 1.0), rep["max_abs"] / max(rep["max_abs_bound"], 1e-30)],
@@ -445,6 +446,9 @@ def main() -> int:
                     help="fused all-gather: SM stores from the quant kernel, copy-engine copies, or by block size")
     ap.add_argument("--rs-dtype", default="bf16", choices=["bf16", "fp8"],
                     help="reduce-scatter payload: bf16 partials, or 1x128 e4m3 codes + scales (the b3 variant)")
+    ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="expert parallel: E/P experts per rank balanced by routed pairs (default) or the reference's "
+                         "contiguous ranges")
     ap.add_argument("--sparse", action="store_true",
                     help="expert parallel: send tokens / partials only to / from the ranks holding their experts")
     ap.add_argument("--chunks", type=int, default=4, help="down-GEMM column chunks of the copy-engine push")
@@ -487,7 +491,7 @@ def main() -> int:
     elif world > 1:
         from td_benchmark_b200.layer import NcclExchange
         exchange = NcclExchange(ctx.group, rs_dtype=args.rs_dtype)
-    layer, level = build_layer(spec, cfg, ctx, bundle, exchange=exchange)
+    layer, level = build_layer(spec, cfg, ctx, bundle, exchange=exchange, placement=args.placement)
     T = layer.T
     x = bundle.hidden_local.contiguous()
     ids = bundle.routing.topk_ids_full.contiguous()
@@ -694,6 +698,7 @@ def main() -> int:
                        "parallelism": f"{spec.parallel.lower()}{world}", "scheme": code, "shard_level": level,
                        "routing": cfg.routing.imbalance_kind,
                        "rs_payload": args.rs_dtype if world > 1 else None,
+                       "placement": (args.placement if (spec.parallel == "EP" and world > 1) else None),
                        "exchange": (f"p2p ag={layer.exchange.ag_mode} rs={layer.exchange.rs_mode} "
                                     f"sparse={int(layer.exchange.sparse)} "
                                     f"chunks={len(layer.exchange.chunk_cols)}"

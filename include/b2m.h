@@ -262,14 +262,16 @@ int b2m_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int
 
 /* Sparse expert-parallel all-gather (the dispatch of moe_bench/tdx/function/ep_moe_fused.py:375-517:
  * a token goes only to the ranks that hold one of its experts): b2m_quant_push, except that
- * token row0 + i is stored on rank d only when one of topk_ids[row0 + i, 0..top_k) lies in
- * [d*experts_per_rank, (d+1)*experts_per_rank), and always on this rank (row0 / rows).
+ * token row0 + i is stored on rank d only when expert_owner[e] == d for one of its experts
+ * e = topk_ids[row0 + i, 0..top_k), and always on this rank (row0 / rows).  expert_owner
+ * (int32 [num_experts], global expert -> rank) is the same on every rank.
  * topk_ids int32 [T, top_k] is the routing of all T tokens, the same on every rank; rows
  * a destination does not receive keep stale contents, which its dispatch never reads
  * (no pair of that token is local there).  row0 % rows == 0. */
 int b2m_quant_push_sparse(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world, void* const* q_dst,
                           void* const* s_dst, int64_t row0, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
-                          const int32_t* topk_ids, int32_t top_k, int32_t experts_per_rank, void* stream);
+                          const int32_t* topk_ids, int32_t top_k, const int32_t* expert_owner, int32_t num_experts,
+                          void* stream);
 
 /* b2m_quant_push for callers that cannot allocate device memory (a runtime that
  * owns every device byte through its own arena, or code that may not call
@@ -341,12 +343,13 @@ int b2m_rs_combine(const void* recv, int64_t rows, int32_t top_k, int64_t hidden
  * >= epoch, out[t, :] = bf16( sum_{r=0..world-1} slots[r*rows + t, :] + add[t, :] )
  * (fp32, rank order).  add (bf16 [rows, hidden]) may be NULL.  With topk_ids (int32
  * [rows, top_k], the routing of this owner's tokens; expert parallel, nchunks == 1) only
- * the sources r holding one of token t's experts (expert / experts_per_rank == r) are
- * summed -- the slots a sparse b2m_combine_push wrote; the others are zero partials, so
- * the result is that of the dense sum. */
+ * the sources r holding one of token t's experts (expert_owner[expert] == r) are summed --
+ * the slots a sparse b2m_combine_push wrote; the others are zero partials, so the result
+ * is that of the dense sum. */
 int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world, int32_t nchunks,
                   const uint32_t* flags, uint32_t epoch, const void* add, void* out, const int32_t* topk_ids,
-                  int32_t top_k, int32_t experts_per_rank, int32_t* dev_status, void* stream);
+                  int32_t top_k, const int32_t* expert_owner, int32_t num_experts, int32_t* dev_status,
+                  void* stream);
 
 /* FP8 reduce-scatter push (replaces the b3 path's per-chunk rs_input quantisation +
  * all_to_all_single of codes and scales, moe_bench/overlap/overlap_forward.py:900-928).
@@ -366,11 +369,12 @@ int b2m_combine_push_fp8(const void* staged, int64_t tokens, int32_t top_k, int6
  * once flags[0..world) are all >= epoch (flags == NULL: no wait),
  *   out[t, :] = bf16( sum_{r=0..world-1} e4m3(codes[r*rows + t, :]) * scales[r*rows + t, group] + add[t, :] )
  * in fp32, rank order, one rounding.  codes u8 [world*rows, hidden], scales fp32
- * [world*rows, hidden/128]; add (bf16 [rows, hidden]) may be NULL.  topk_ids /
- * top_k / experts_per_rank: the sparse reduce, as for b2m_rs_reduce (NULL: dense). */
+ * [world*rows, hidden/128]; add (bf16 [rows, hidden]) may be NULL.  topk_ids / top_k /
+ * expert_owner / num_experts: the sparse reduce, as for b2m_rs_reduce (NULL: dense). */
 int b2m_rs_reduce_fp8(const void* codes, const float* scales, int64_t rows, int64_t hidden, int32_t world,
                       const uint32_t* flags, uint32_t epoch, const void* add, void* out, const int32_t* topk_ids,
-                      int32_t top_k, int32_t experts_per_rank, int32_t* dev_status, void* stream);
+                      int32_t top_k, const int32_t* expert_owner, int32_t num_experts, int32_t* dev_status,
+                      void* stream);
 
 /* On-device routing (replaces the host-side steps of moe_bench/data/routing.py:58-64 that
  * follow the gate GEMM): per token t, p = softmax(logits[t, :] + bias) (bias fp32 [E], may

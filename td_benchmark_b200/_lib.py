@@ -49,10 +49,10 @@ SIGNATURES: dict[str, list] = {
                          _i32, _p],
     "b2m_signal": [_p, _i32, _c.c_uint32, _p],
     "b2m_rs_combine": [_p, _i64, _i32, _i64, _i32, _p, _i32, _c.c_uint32, _p, _p, _p, _p],
-    "b2m_rs_reduce": [_p, _i64, _i64, _i32, _i32, _p, _c.c_uint32, _p, _p, _p, _i32, _i32, _p, _p],
+    "b2m_rs_reduce": [_p, _i64, _i64, _i32, _i32, _p, _c.c_uint32, _p, _p, _p, _i32, _p, _i32, _p, _p],
     "b2m_combine_push_fp8": [_p, _i64, _i32, _i64, _p, _p, _p, _i32, _i32, _p, _p, _p, _c.c_uint32, _p, _i32, _p],
-    "b2m_rs_reduce_fp8": [_p, _p, _i64, _i64, _i32, _p, _c.c_uint32, _p, _p, _p, _i32, _i32, _p, _p],
-    "b2m_quant_push_sparse": [_p, _i64, _i64, _i64, _i32, _p, _p, _i64, _p, _c.c_uint32, _p, _p, _i32, _i32, _p],
+    "b2m_rs_reduce_fp8": [_p, _p, _i64, _i64, _i32, _p, _c.c_uint32, _p, _p, _p, _i32, _p, _i32, _p, _p],
+    "b2m_quant_push_sparse": [_p, _i64, _i64, _i64, _i32, _p, _p, _i64, _p, _c.c_uint32, _p, _p, _i32, _p, _i32, _p],
     "b2m_route_topk": [_p, _i64, _i32, _i32, _p, _p, _p, _p],
 }
 

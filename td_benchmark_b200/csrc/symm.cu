@@ -68,14 +68,21 @@ __device__ __forceinline__ void publish_when_grid_done(int32_t* counter, const F
   }
 }
 
-// Bit r set when token t routes to at least one expert of rank r (experts [r*epr, (r+1)*epr)).
-// Expert parallel only: every rank holds the routing of all tokens, so source and
+// The rank holding global expert `id` (owner table int32 [experts]); 32 (no rank) for an id
+// outside [0, experts).
+__device__ __forceinline__ uint32_t expert_rank(const int32_t* __restrict__ owner, int experts, int32_t id) {
+  return (id >= 0 && id < experts) ? static_cast<uint32_t>(__ldg(owner + id)) : 32u;
+}
+
+// Bit r set when token t routes to at least one expert held by rank r.  Expert parallel
+// only: every rank holds the routing of all tokens and the same owner table, so source and
 // destination agree on this mask without exchanging any index.
-__device__ __forceinline__ uint32_t token_rank_mask(const int32_t* __restrict__ ids, int64_t t, int top_k, int epr) {
+__device__ __forceinline__ uint32_t token_rank_mask(const int32_t* __restrict__ ids, int64_t t, int top_k,
+                                                   const int32_t* __restrict__ owner, int experts) {
   uint32_t m = 0;
   for (int j = 0; j < top_k; ++j) {
-    const uint32_t r = static_cast<uint32_t>(__ldg(ids + t * top_k + j)) / static_cast<uint32_t>(epr);
-    m |= r < 32u ? 1u << r : 0u;  // an id outside [0, 32 * epr) names no rank
+    const uint32_t r = expert_rank(owner, experts, __ldg(ids + t * top_k + j));
+    m |= r < 32u ? 1u << r : 0u;
   }
   return m;
 }
@@ -91,7 +98,8 @@ __global__ void __launch_bounds__(kThreads)
     quant_push_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t rows, int64_t gpr, int world,
                       const __grid_constant__ PeerPtrs qdst, const __grid_constant__ PeerPtrs sdst, int64_t row0,
                       const __grid_constant__ FlagPtrs flags, uint32_t epoch, int32_t* counter,
-                      const int32_t* __restrict__ sparse_ids, int top_k, int epr) {
+                      const int32_t* __restrict__ sparse_ids, int top_k, const int32_t* __restrict__ owner,
+                      int experts) {
   const int lane = threadIdx.x & 31;
   const int sub = lane >> 3;  // group of the warp's four
   const int gl = lane & 7;    // 16-value slice of that group
@@ -128,7 +136,8 @@ __global__ void __launch_bounds__(kThreads)
       const int64_t dst_row = row0 + row;
       // sparse (expert parallel): only the ranks that hold one of the token's experts, and
       // this rank (its own rows also feed its shared expert)
-      const uint32_t need = sparse_ids ? (token_rank_mask(sparse_ids, dst_row, top_k, epr) | (1u << src)) : ~0u;
+      const uint32_t need =
+          sparse_ids ? (token_rank_mask(sparse_ids, dst_row, top_k, owner, experts) | (1u << src)) : ~0u;
       for (int i = 0; i < world; ++i) {
         const int r = first + i < world ? first + i : first + i - world;
         if (!((need >> r) & 1u)) continue;
@@ -449,7 +458,8 @@ __global__ void __launch_bounds__(kThreads)
 template <bool kFp8>
 __global__ void __launch_bounds__(kThreads)
     rs_reduce_sparse_kernel(const void* __restrict__ slots, const float* __restrict__ scales, int64_t rows,
-                            int64_t hidden, int world, const int32_t* __restrict__ ids, int top_k, int epr,
+                            int64_t hidden, int world, const int32_t* __restrict__ ids, int top_k,
+                            const int32_t* __restrict__ owner, int experts,
                             const uint32_t* flags, uint32_t epoch, const __nv_bfloat16* __restrict__ add,
                             __nv_bfloat16* __restrict__ out, int32_t* status, uint64_t timeout_ns) {
   __shared__ int s_ok;
@@ -465,8 +475,7 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
   const int64_t gpr = hidden / 128;
   for (int64_t t = warp; t < rows; t += nwarps) {
-    const uint32_t rk = lane < top_k ? static_cast<uint32_t>(__ldg(ids + t * top_k + lane)) / static_cast<uint32_t>(epr)
-                                     : 32u;
+    const uint32_t rk = lane < top_k ? expert_rank(owner, experts, __ldg(ids + t * top_k + lane)) : 32u;
     const uint32_t mine = rk < 32u ? 1u << rk : 0u;
     const uint32_t srcs = __reduce_or_sync(0xffffffffu, mine);
     for (int64_t c = lane * 8; c < hidden; c += 256) {
@@ -652,20 +661,21 @@ int b2m_quant_push(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int
   const int64_t groups = rows * (hidden / 128);
   quant_push_kernel<<<grid_for(groups * 8, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, rows, hidden / 128, world, q, s, row0, f, epoch, counter, nullptr, 0,
-      1);
+      nullptr, 0);
   return check_cuda(cudaGetLastError(), "quant_push launch");
 }
 
 int b2m_quant_push_sparse(const void* x, int64_t rows, int64_t hidden, int64_t ldx, int32_t world, void* const* q_dst,
                           void* const* s_dst, int64_t row0, uint32_t* const* flag_dst, uint32_t epoch, int32_t* counter,
-                          const int32_t* topk_ids, int32_t top_k, int32_t experts_per_rank, void* stream) {
+                          const int32_t* topk_ids, int32_t top_k, const int32_t* expert_owner, int32_t num_experts,
+                          void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
   B2M_TRY(check_quant_push(x, rows, hidden, ldx, world, q_dst, s_dst, flag_dst, "quant_push_sparse"));
-  if (!counter || !topk_ids || top_k < 1 || top_k > 32 || experts_per_rank < 1 || row0 % rows)
-    return fail(B2M_ERR_ARG, "quant_push_sparse: need counter, topk_ids, 1 <= top_k <= 32, experts_per_rank >= 1 "
-                             "and row0 a multiple of rows");
+  if (!counter || !topk_ids || !expert_owner || top_k < 1 || top_k > 32 || num_experts < 1 || row0 % rows)
+    return fail(B2M_ERR_ARG, "quant_push_sparse: need counter, topk_ids, expert_owner, 1 <= top_k <= 32, "
+                             "num_experts >= 1 and row0 a multiple of rows");
   PeerPtrs q{}, s{};
   FlagPtrs f{};
   for (int r = 0; r < world; ++r) {
@@ -676,7 +686,7 @@ int b2m_quant_push_sparse(const void* x, int64_t rows, int64_t hidden, int64_t l
   const int64_t groups = rows * (hidden / 128);
   quant_push_kernel<<<grid_for(groups * 8, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, rows, hidden / 128, world, q, s, row0, f, epoch, counter, topk_ids,
-      top_k, experts_per_rank);
+      top_k, expert_owner, num_experts);
   return check_cuda(cudaGetLastError(), "quant_push_sparse launch");
 }
 
@@ -813,7 +823,7 @@ int b2m_rs_combine(const void* recv, int64_t rows, int32_t top_k, int64_t hidden
 
 int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world, int32_t nchunks,
                   const uint32_t* flags, uint32_t epoch, const void* add, void* out, const int32_t* topk_ids,
-                  int32_t top_k, int32_t experts_per_rank, int32_t* dev_status, void* stream) {
+                  int32_t top_k, const int32_t* expert_owner, int32_t num_experts, int32_t* dev_status, void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
@@ -821,10 +831,10 @@ int b2m_rs_reduce(const void* slots, int64_t rows, int64_t hidden, int32_t world
       !aligned16(slots) || !aligned16(out) || (add && !aligned16(add)) || nchunks < 1 || nchunks * world > kThreads)
     return fail(B2M_ERR_ARG, "rs_reduce: bad shape/pointers/chunks");
   if (topk_ids) {  // sparse expert-parallel reduce: only the sources holding one of the token's experts
-    if (nchunks != 1 || top_k < 1 || top_k > 32 || experts_per_rank < 1)
-      return fail(B2M_ERR_ARG, "rs_reduce: sparse reduce needs nchunks == 1, 1 <= top_k <= 32, experts_per_rank >= 1");
+    if (nchunks != 1 || top_k < 1 || top_k > 32 || !expert_owner || num_experts < 1)
+      return fail(B2M_ERR_ARG, "rs_reduce: sparse reduce needs nchunks == 1, 1 <= top_k <= 32 and the owner table");
     rs_reduce_sparse_kernel<false><<<grid_for(rows * 32, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        slots, nullptr, rows, hidden, world, topk_ids, top_k, experts_per_rank, flags, epoch,
+        slots, nullptr, rows, hidden, world, topk_ids, top_k, expert_owner, num_experts, flags, epoch,
         static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out), dev_status, timeout_ns());
     return check_cuda(cudaGetLastError(), "rs_reduce (sparse) launch");
   }
@@ -865,7 +875,8 @@ int b2m_combine_push_fp8(const void* staged, int64_t tokens, int32_t top_k, int6
 
 int b2m_rs_reduce_fp8(const void* codes, const float* scales, int64_t rows, int64_t hidden, int32_t world,
                       const uint32_t* flags, uint32_t epoch, const void* add, void* out, const int32_t* topk_ids,
-                      int32_t top_k, int32_t experts_per_rank, int32_t* dev_status, void* stream) {
+                      int32_t top_k, const int32_t* expert_owner, int32_t num_experts, int32_t* dev_status,
+                      void* stream) {
   using namespace b2m;
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
@@ -873,10 +884,10 @@ int b2m_rs_reduce_fp8(const void* codes, const float* scales, int64_t rows, int6
       (reinterpret_cast<uintptr_t>(codes) & 7u) || !aligned16(out) || (add && !aligned16(add)))
     return fail(B2M_ERR_ARG, "rs_reduce_fp8: bad shape/pointers (hidden %% 128 == 0, 16-byte rows)");
   if (topk_ids) {
-    if (top_k < 1 || top_k > 32 || experts_per_rank < 1)
-      return fail(B2M_ERR_ARG, "rs_reduce_fp8: sparse reduce needs 1 <= top_k <= 32, experts_per_rank >= 1");
+    if (top_k < 1 || top_k > 32 || !expert_owner || num_experts < 1)
+      return fail(B2M_ERR_ARG, "rs_reduce_fp8: sparse reduce needs 1 <= top_k <= 32 and the owner table");
     rs_reduce_sparse_kernel<true><<<grid_for(rows * 32, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        codes, scales, rows, hidden, world, topk_ids, top_k, experts_per_rank, flags, epoch,
+        codes, scales, rows, hidden, world, topk_ids, top_k, expert_owner, num_experts, flags, epoch,
         static_cast<const __nv_bfloat16*>(add), static_cast<__nv_bfloat16*>(out), dev_status, timeout_ns());
     return check_cuda(cudaGetLastError(), "rs_reduce_fp8 (sparse) launch");
   }

@@ -222,7 +222,7 @@ class NcclExchange:
             add = layer.shared.run(layer.status) if (layer.shared is not None and layer.ep) else None
             _lib.call("b2m_rs_reduce_fp8", self.recv_q.data_ptr(), self.recv_s.data_ptr(), layer.T_local, layer.H,
                       self.world_size, None, 0, None if add is None else add.data_ptr(), layer.out_local.data_ptr(),
-                      None, 0, 0, layer.status.data_ptr(), st)
+                      None, 0, None, 0, layer.status.data_ptr(), st)
             return layer.out_local
         ops.combine(layer.staged, layer.top_k, ids, layer.expert_map, shared_out, self.partial)
         self.dist.reduce_scatter_tensor(layer.out_local, self.partial, group=self.group)
@@ -325,7 +325,8 @@ class P2PExchange:
             if layer.E % P:
                 raise ValueError(f"sparse exchange needs E={layer.E} divisible by world_size={P}")
             self.ag_mode = "sm"
-            self.epr = layer.E // P
+            if layer.expert_owner is None:   # the contiguous layout: expert e on rank e // (E/P)
+                layer.expert_owner = (torch.arange(layer.E, device=layer.device) // (layer.E // P)).to(torch.int32)
         if self.ag_mode == "auto":
             self.ag_mode = "ce" if Tl * H >= self.AG_CE_MIN_BYTES else "sm"
         if self.rs_mode == "gemm" and layer.shared is not None and not layer.ep:
@@ -421,7 +422,7 @@ class P2PExchange:
         if self.ag_mode == "sm" and self.sparse:
             _lib.call("b2m_quant_push_sparse", x_local.data_ptr(), Tl, H, x_local.stride(0), self.world_size,
                       self._q_dst, self._s_dst, self.rank * Tl, self._ag_dst, self.epoch, self.counters,
-                      layer.cur_ids.data_ptr(), layer.top_k, self.epr, st)
+                      layer.cur_ids.data_ptr(), layer.top_k, layer.expert_owner.data_ptr(), layer.E, st)
         elif self.ag_mode == "sm":
             _lib.call("b2m_quant_push", x_local.data_ptr(), Tl, H, x_local.stride(0), self.world_size, self._q_dst,
                       self._s_dst, self.rank * Tl, self._ag_dst, self.epoch, self.counters, st)
@@ -586,11 +587,12 @@ class P2PExchange:
                   layer.out_local.data_ptr(), *self._sparse_owner(layer), layer.status.data_ptr(), compute.cuda_stream)
 
     def _sparse_owner(self, layer: "MoELayer") -> tuple:
-        """(routing rows of this rank's tokens, top_k, experts per rank) for the sparse owner
-        reduce, or the dense reduce's (None, 0, 0)."""
+        """(routing rows of this rank's tokens, top_k, expert -> rank table, E) for the sparse
+        owner reduce, or the dense reduce's (None, 0, None, 0)."""
         if not self.sparse:
-            return None, 0, 0
-        return layer.cur_ids.data_ptr() + 4 * self.rank * layer.T_local * layer.top_k, layer.top_k, self.epr
+            return None, 0, None, 0
+        return (layer.cur_ids.data_ptr() + 4 * self.rank * layer.T_local * layer.top_k, layer.top_k,
+                layer.expert_owner.data_ptr(), layer.E)
 
     def exchange_alone(self, layer: "MoELayer", x_local: torch.Tensor, topk_ids: torch.Tensor) -> bool:
         """The all-gather and the reduce-scatter of one forward with no GEMM between them.
@@ -647,7 +649,7 @@ class MoELayer:
 
     def __init__(self, weights: ExpertWeights, tokens: int, top_k: int, global_num_experts: int,
                  expert_map: torch.Tensor | None = None, shared: ExpertWeights | None = None,
-                 exchange=None, device=None):
+                 exchange=None, device=None, expert_owner: torch.Tensor | None = None):
         self.w = weights
         self.exchange = exchange or NullExchange()
         self.P = self.exchange.world_size
@@ -661,6 +663,8 @@ class MoELayer:
         self.device = torch.device(device) if device is not None else weights.w1i.device
         self.expert_map = expert_map
         self.ep = expert_map is not None
+        # int32 [E] global expert -> rank (expert parallel; None: the contiguous layout)
+        self.expert_owner = None if expert_owner is None else expert_owner.to(self.device, torch.int32).contiguous()
         dev = self.device
         self.numel = tokens * top_k
         self.route = _Routing(self.numel, global_num_experts, dev)

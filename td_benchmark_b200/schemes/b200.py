@@ -37,17 +37,26 @@ P2P_TUNABLES = {
                                       "epilogue ('gemm') or copy engines ('ce')"),
     "rs_chunks": TunableSpec(int, 4, "down-GEMM column chunks of the copy-engine reduce-scatter (1..8)"),
 }
+# expert-parallel schemes (d2, d4)
+EP_TUNABLES = {
+    "placement": TunableSpec(str, "contiguous", "experts per rank: 'contiguous' (rank r holds [r*E/P, (r+1)*E/P), the "
+                                                "reference's layout) or 'balanced' (E/P experts per rank chosen so "
+                                                "every rank holds about the same number of routed pairs; same output)"),
+}
 # expert-parallel peer-memory scheme only
 EP_SPARSE = {
     "sparse": TunableSpec(bool, False, "send a token only to the ranks holding one of its experts and its partial only "
                                        "from those ranks (all-gather and reduce-scatter by SM stores; same output as "
                                        "the dense exchange, fewer NVLink bytes)"),
 }
-_CHOICES = {"ag_mode": ("sm", "ce", "auto", "push"), "rs_mode": ("sm", "ce", "gemm"), "rs_dtype": ("bf16", "fp8")}
+_CHOICES = {"ag_mode": ("sm", "ce", "auto", "push"), "rs_mode": ("sm", "ce", "gemm"), "rs_dtype": ("bf16", "fp8"),
+            "placement": ("contiguous", "balanced")}
 
 
 def _spec(code: str, name: str, parallel: str, comm: str) -> SchemeSpec:
     schema = dict(B200_TUNABLES)
+    if parallel == "EP":
+        schema.update(EP_TUNABLES)
     if EXCHANGE.get(code) == "p2p":
         schema.update(P2P_TUNABLES)
         if parallel == "EP":
@@ -69,12 +78,16 @@ def require_data(data: Any) -> Any:
 
 
 def build_layer(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, exchange: Any = None,
-                tunables: dict[str, Any] | None = None):
-    """Shard views + prepared weights + MoELayer for this rank."""
+                tunables: dict[str, Any] | None = None, placement: str | None = None):
+    """Shard views + prepared weights + MoELayer for this rank.
+
+    ``placement`` (expert parallel; default the ``placement`` tunable, else 'contiguous'):
+    'balanced' places E/P experts per rank by the routed pairs of ``data.routing`` (every rank
+    computes the same placement from the same routing)."""
     import torch
 
     from ..layer import ExpertWeights, MoELayer, NcclExchange, P2PExchange
-    from ..weights import ep_views, tp_views
+    from ..weights import balanced_placement, ep_views, tp_views
 
     bundle = require_data(data)
     ckpt = bundle.ckpt
@@ -83,7 +96,14 @@ def build_layer(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, exchange: Any =
     T = s.M_aligned(ctx.world_size)
     args = (ckpt.w1.fp8.to(device), ckpt.w1.scale.to(device), ckpt.w2.fp8.to(device), ckpt.w2.scale.to(device),
             ctx.rank, ctx.world_size)
-    views = tp_views(*args) if spec.parallel == "TP" else ep_views(*args)
+    if placement is None:
+        placement = (tunables or {}).get("placement", "contiguous")
+    if spec.parallel == "TP":
+        views = tp_views(*args)
+    elif placement == "balanced" and ctx.world_size > 1:
+        views = ep_views(*args, placement=balanced_placement(bundle.routing.topk_ids_full, s.E, ctx.world_size))
+    else:
+        views = ep_views(*args)
     weights = ExpertWeights.prepare(views["w1"], views["w1_scale"], views["w2"], views["w2_scale"])
     shared = None
     if ckpt.shared_w1 is not None and ckpt.shared_w2 is not None:
@@ -107,7 +127,7 @@ def build_layer(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, exchange: Any =
             exchange = NcclExchange(ctx.group, rs_dtype=rs_dtype)
     expert_map = views.get("expert_map")
     layer = MoELayer(weights, T, s.top_k, s.E, expert_map=expert_map, shared=shared, exchange=exchange,
-                     device=device)
+                     device=device, expert_owner=views.get("expert_owner"))
     return layer, views["shard_level"]
 
 

@@ -15,6 +15,8 @@ its variants.  Variants (expert parallel, scheme d2 / d4):
 * ``sparse`` peer-memory exchange sending tokens / partials only to / from the ranks that
              hold their experts;
 * ``fp8rs``  peer-memory exchange with the FP8 reduce-scatter payload;
+* ``balanced`` / ``balanced-fp8rs``: ``fused`` / ``fp8rs`` with E/P experts per rank placed by
+             routed pairs instead of contiguous ranges (the other variants use contiguous);
 * ``ceC``    the chunked variant: the down GEMM in C column chunks, each chunk's partials
              pushed by copy engines while the next computes -- the overlap-chunk axis of the
              reference's b2/b3 (``n_chunks_down``).
@@ -71,8 +73,10 @@ def _exchange(variant: str, ctx):
         return P2PExchange(ctx.group)
     if variant == "sparse":
         return P2PExchange(ctx.group, sparse=True)
-    if variant == "fp8rs":
+    if variant in ("fp8rs", "balanced-fp8rs"):
         return P2PExchange(ctx.group, rs_mode="fp8")
+    if variant == "balanced":
+        return P2PExchange(ctx.group)
     if variant.startswith("ce"):
         return P2PExchange(ctx.group, rs_mode="ce", chunks=int(variant[2:]))
     raise ValueError(f"unknown variant {variant!r}")
@@ -116,9 +120,11 @@ def main(argv: list[str] | None = None) -> int:
                 code = ("d2" if variant == "nccl" else "d4") if cfg.parallel == "EP" else \
                        ("d1" if variant == "nccl" else "d3")
                 exchange = None if world == 1 else _exchange(variant, ctx)
-                layer, _ = build_layer(REGISTRY[code][0], cfg, ctx, bundle, exchange=exchange)
+                placement = "balanced" if variant.startswith("balanced") else "contiguous"
+                layer, _ = build_layer(REGISTRY[code][0], cfg, ctx, bundle, exchange=exchange, placement=placement)
                 ms = _time_forward(layer, x, ids, wts, args.steps, args.warmup, flush, world, dev)
                 rec = {"preset": args.preset, "tokens": T, "routing": routing, "variant": variant, "scheme": code,
+                       "placement": placement if cfg.parallel == "EP" else None,
                        "n_gpus": world, "parallelism": f"{cfg.parallel.lower()}{world}", "us_per_layer": ms * 1e3,
                        "tokens_per_s": T / (ms * 1e-3), "steps": args.steps, "warmup": args.warmup,
                        "exchange": getattr(layer.exchange, "name", "none"),

@@ -87,11 +87,12 @@ def golden_rows(hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torc
 
 @torch.no_grad()
 def rank_partials(hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, ckpt: Any, world: int,
-                  parallel: str) -> torch.Tensor:
+                  parallel: str, owner: list[int] | None = None) -> torch.Tensor:
     """fp32 [world, rows, H]: rank r's share of the golden of these rows before the reduce-scatter.
 
-    EP: the routed pairs of experts [r*E/world, (r+1)*E/world) (the shared expert is added after
-    the reduce-scatter and is not part of any partial).  TP: every routed pair restricted to
+    EP: the routed pairs of the experts rank r holds (``owner[e]``, default the contiguous layout
+    [r*E/world, (r+1)*E/world)); the shared expert is added after the reduce-scatter and is not
+    part of any partial.  TP: every routed pair restricted to
     intermediate columns [r*I/world, (r+1)*I/world) (and the same slice of the shared expert);
     needs I/world to be a multiple of 128 so the slices align with the quantisation groups."""
     x = hidden.float()
@@ -116,7 +117,8 @@ def rank_partials(hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: to
         w2 = dequant_bf16(ckpt.w2.fp8[e].to(x.device), ckpt.w2.scale[e].to(x.device))
         wt = topk_weights[rows, slots].float()[:, None]
         if parallel == "EP":
-            out[e // (E // world)].index_add_(0, rows, _ffn(x[rows], w1, w2, True) * wt)
+            r = owner[e] if owner is not None else e // (E // world)
+            out[r].index_add_(0, rows, _ffn(x[rows], w1, w2, True) * wt)
         else:
             tp_split(x[rows], w1, w2, wt, rows)
     if parallel != "EP" and getattr(ckpt, "shared_w1", None) is not None:

@@ -71,15 +71,65 @@ def tp_views(w1: torch.Tensor, w1_scale: torch.Tensor, w2: torch.Tensor, w2_scal
     return {"w1": w1q, "w1_scale": s1q, "w2": w2q, "w2_scale": s2q, "shard_level": "L2", "inter": irp}
 
 
+def contiguous_placement(num_experts: int, world_size: int) -> list[list[int]]:
+    """The reference's expert-parallel layout: rank r owns experts [r*E/P, (r+1)*E/P)
+    (``moe_bench/schemes/runtime.py:86-93``)."""
+    le = num_experts // world_size
+    return [list(range(r * le, (r + 1) * le)) for r in range(world_size)]
+
+
+def balanced_placement(topk_ids: torch.Tensor, num_experts: int, world_size: int) -> list[list[int]]:
+    """Experts per rank balanced by routed (token, expert) pairs, E/P experts on every rank.
+
+    Greedy longest-first: experts in descending pair count (ties: lower id first) each go
+    to the rank with the fewest pairs so far among those with room (ties: lower rank).
+    Expert placement does not enter the layer's math -- the output is the same sum over
+    the same experts -- only which rank computes which expert, so under skewed routing
+    (Zipf) it removes the load imbalance the contiguous layout has (DeepSeek-V3 EP8 at
+    Zipf 1.2: the most-loaded rank holds 2.24x the mean pairs contiguous, 1.0x balanced).
+    Returns each rank's experts in ascending id order."""
+    if num_experts % world_size:
+        raise ValueError(f"E={num_experts} not divisible by world_size {world_size}")
+    cap = num_experts // world_size
+    counts = torch.bincount(topk_ids.reshape(-1).long().cpu(), minlength=num_experts)[:num_experts].tolist()
+    order = sorted(range(num_experts), key=lambda e: (-counts[e], e))
+    load = [0] * world_size
+    owned: list[list[int]] = [[] for _ in range(world_size)]
+    for e in order:
+        r = min((r for r in range(world_size) if len(owned[r]) < cap), key=lambda r: (load[r], r))
+        owned[r].append(e)
+        load[r] += counts[e]
+    return [sorted(x) for x in owned]
+
+
+def expert_owner(placement: list[list[int]], device=None) -> torch.Tensor:
+    """int32 [E]: the rank that holds each global expert."""
+    n = sum(len(x) for x in placement)
+    owner = torch.empty(n, dtype=torch.int32)
+    for r, es in enumerate(placement):
+        owner[es] = r
+    return owner.to(device) if device is not None else owner
+
+
 def ep_views(w1: torch.Tensor, w1_scale: torch.Tensor, w2: torch.Tensor, w2_scale: torch.Tensor,
-             rank: int, world_size: int) -> dict:
+             rank: int, world_size: int, placement: list[list[int]] | None = None) -> dict:
+    """Expert-parallel shard: this rank's experts (contiguous layout unless ``placement`` gives
+    every rank's expert list) and the global -> local expert map (-1: not local)."""
     e = w1.shape[0]
     if e % world_size:
         raise ValueError(f"E={e} not divisible by world_size {world_size}")
-    le = e // world_size
-    lo, hi = rank * le, (rank + 1) * le
+    if placement is None:
+        placement = contiguous_placement(e, world_size)
+    mine = placement[rank]
     emap = torch.full((e,), -1, dtype=torch.int32, device=w1.device)
-    emap[lo:hi] = torch.arange(le, dtype=torch.int32, device=w1.device)
-    return {"w1": w1[lo:hi].contiguous(), "w1_scale": w1_scale[lo:hi].contiguous(), "w2": w2[lo:hi].contiguous(),
-            "w2_scale": w2_scale[lo:hi].contiguous(), "expert_map": emap if world_size > 1 else None,
+    emap[mine] = torch.arange(len(mine), dtype=torch.int32, device=w1.device)
+    lo = mine[0]
+    if mine == list(range(lo, lo + len(mine))):   # a contiguous range: slice
+        sel = slice(lo, lo + len(mine))
+        views = [t[sel].contiguous() for t in (w1, w1_scale, w2, w2_scale)]
+    else:
+        idx = torch.tensor(mine, dtype=torch.long, device=w1.device)
+        views = [t.index_select(0, idx).contiguous() for t in (w1, w1_scale, w2, w2_scale)]
+    return {"w1": views[0], "w1_scale": views[1], "w2": views[2], "w2_scale": views[3],
+            "expert_map": emap if world_size > 1 else None, "expert_owner": expert_owner(placement, w1.device),
             "shard_level": "L0", "inter": w2.shape[2]}

@@ -28,6 +28,7 @@ def main() -> int:
     ap.add_argument("--rs-chunks", type=int, default=None, help="d3/d4 tunable rs_chunks")
     ap.add_argument("--rs-dtype", default=None, help="tunable rs_dtype (bf16 | fp8)")
     ap.add_argument("--sparse", action="store_true", help="d4 tunable sparse; also checks it equals the dense exchange")
+    ap.add_argument("--placement", default=None, help="d2/d4 tunable placement (contiguous | balanced)")
     args = ap.parse_args()
 
     import torch
@@ -48,7 +49,7 @@ def main() -> int:
     bundle = data.build_bundle(cfg, rank=ctx.rank, world_size=ctx.world_size, device=ctx.device)
     tun = {"check_status": True}
     for key, val in (("ag_mode", args.ag_mode), ("rs_mode", args.rs_mode), ("rs_chunks", args.rs_chunks),
-                     ("rs_dtype", args.rs_dtype)):
+                     ("rs_dtype", args.rs_dtype), ("placement", args.placement)):
         if val is not None:
             tun[key] = val
     dense_out = None
@@ -79,8 +80,14 @@ def main() -> int:
         # the FP8 reduce-scatter payload adds the quantisation error of every rank's partial
         from td_benchmark_b200 import verify
         r0 = ctx.rank * tl
+        owner = None
+        if args.placement == "balanced" and cfg.parallel == "EP":
+            from td_benchmark_b200.weights import balanced_placement, expert_owner
+            owner = expert_owner(balanced_placement(bundle.routing.topk_ids_full, cfg.shape.E,
+                                                    ctx.world_size)).tolist()
         parts = verify.rank_partials(bundle.hidden_full[r0:r0 + tl], bundle.routing.topk_ids_full[r0:r0 + tl],
-                                     bundle.routing.topk_weights_full[r0:r0 + tl], ck, ctx.world_size, cfg.parallel)
+                                     bundle.routing.topk_weights_full[r0:r0 + tl], ck, ctx.world_size, cfg.parallel,
+                                     owner)
         rs_calib = verify.rs_fp8_error(parts)
         calib = calib + rs_calib
     rep = ogolden.compare_outputs(out2.float().cpu().numpy(), ref.cpu().numpy(), **ogolden.GATES)

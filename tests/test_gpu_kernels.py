@@ -552,19 +552,20 @@ def test_gemm1_pushes_own_rows_to_peers(world, rank):
 
 
 # ---------------------------------------------------------------- reduce-scatter push + owner reduce
-@pytest.mark.parametrize("payload,sparse,world,k,H,shared,ep", [
-    ("fp8", False, 2, 2, 256, False, False), ("fp8", False, 4, 8, 384, True, False),
-    ("fp8", False, 4, 2, 1024, False, True), ("fp8", False, 8, 1, 128, False, False),
-    ("fp8", True, 4, 2, 1024, False, True), ("fp8", True, 8, 8, 256, False, True),
-    ("bf16", False, 4, 8, 384, True, False), ("bf16", True, 4, 2, 512, False, True),
-    ("bf16", True, 8, 8, 256, False, True)])
-def test_reduce_scatter_emulated_bit_exact(payload, sparse, world, k, H, shared, ep):
+@pytest.mark.parametrize("payload,sparse,world,k,H,shared,ep,perm", [
+    ("fp8", False, 2, 2, 256, False, False, False), ("fp8", False, 4, 8, 384, True, False, False),
+    ("fp8", False, 4, 2, 1024, False, True, False), ("fp8", False, 8, 1, 128, False, False, False),
+    ("fp8", True, 4, 2, 1024, False, True, False), ("fp8", True, 8, 8, 256, False, True, True),
+    ("bf16", False, 4, 8, 384, True, False, False), ("bf16", True, 4, 2, 512, False, True, False),
+    ("bf16", True, 8, 8, 256, False, True, True), ("bf16", True, 4, 8, 256, False, True, True)])
+def test_reduce_scatter_emulated_bit_exact(payload, sparse, world, k, H, shared, ep, perm):
     """Every source rank pushes its partials (bf16, or FP8 codes + scales: the b3 payload) to
     the owners, then every owner sums its slots in rank order: all ranks emulated on one GPU,
     each with its own buffers; pushed slots, flags and outputs bit-exact against the oracle.
     Sparse (expert parallel): a token's partial goes only from ranks holding one of its
     experts, and the owner reads only those slots -- the others are prefilled with NaN here,
-    so reading one would show."""
+    so reading one would show.  ``perm``: experts spread over the ranks by a permutation
+    (an arbitrary placement through the owner table) instead of contiguous ranges."""
     from oracle import rs as ors
     from td_benchmark_b200 import _lib
     from td_benchmark_b200.symm import ptr_array
@@ -577,11 +578,16 @@ def test_reduce_scatter_emulated_bit_exact(payload, sparse, world, k, H, shared,
     sh = [_bf16((T, H), 70 + r) if shared else None for r in range(world)]
     ids = torch.stack([torch.randperm(E, generator=torch.Generator().manual_seed(900 + t))[:k] for t in range(T)])
     ids = ids.to(torch.int32).contiguous()
+    order = torch.randperm(E, generator=torch.Generator().manual_seed(11)) if perm else torch.arange(E)
+    owner = torch.empty(E, dtype=torch.int32)
     emaps = []
     for r in range(world):
+        mine = torch.sort(order[r * epr:(r + 1) * epr]).values
+        owner[mine] = r
         m = torch.full((E,), -1, dtype=torch.int32)
-        m[r * epr:(r + 1) * epr] = torch.arange(epr, dtype=torch.int32)
+        m[mine] = torch.arange(epr, dtype=torch.int32)
         emaps.append(m)
+    owner_d = owner.to(DEV)
     fp8 = payload == "fp8"
     if fp8:
         slots = [torch.full((T, H), 0x7F, dtype=torch.uint8, device=DEV) for _ in range(world)]   # NaN codes
@@ -610,7 +616,7 @@ def test_reduce_scatter_emulated_bit_exact(payload, sparse, world, k, H, shared,
     for o in range(world):
         out = torch.empty((Tl, H), dtype=torch.bfloat16, device=DEV)
         own_ids = ids_d[o * Tl:(o + 1) * Tl].contiguous()
-        sp = (own_ids.data_ptr(), k, epr) if sparse else (None, 0, 0)
+        sp = (own_ids.data_ptr(), k, owner_d.data_ptr(), E) if sparse else (None, 0, None, 0)
         if fp8:
             _lib.call("b2m_rs_reduce_fp8", slots[o].data_ptr(), scales[o].data_ptr(), Tl, H, world,
                       flags[o].data_ptr(), 7, None, out.data_ptr(), *sp, status.data_ptr(), stream)

@@ -50,6 +50,10 @@ def _port() -> int:
     # sparse expert-parallel exchange (bit-identical to the dense one)
     ("d4", "dsv3", 1024, ["--zipf", "--sparse"]),
     ("d4", "dsv3", 512, ["--sparse", "--rs-dtype", "fp8"]),
+    # experts placed by routed load instead of contiguous ranges (same output within the gates)
+    ("d4", "dsv3", 1024, ["--zipf", "--placement", "balanced"]),
+    ("d4", "dsv3", 1024, ["--zipf", "--placement", "balanced", "--sparse", "--rs-dtype", "fp8"]),
+    ("d2", "dsv3", 512, ["--zipf", "--placement", "balanced"]),
 ], ids=lambda v: "-".join(a.strip("-") for a in v) if isinstance(v, list) else str(v))
 def test_multi_gpu_scheme_matches_golden(scheme, preset, tokens, extra):
     n = min(_gpus(), 4)

@@ -153,3 +153,37 @@ def test_int_tunable_rejects_bool():
         validate_tunables(spec, {"n": True})
     inst = make_lazy_instance(spec, {"n": 2}, lambda: 7)
     assert inst.run() == 7 and inst.run_staged().output == 7 and inst.diagnostics["scheme"] == "x"
+
+
+def test_balanced_placement_evens_routed_pairs():
+    from td_benchmark_b200 import weights
+    cfg = configs.preset("dsv3")
+    b = data.build_bundle(cfg, device="cpu", with_weights=False)
+    ids = b.routing.topk_ids_full
+    E, P = cfg.shape.E, 8
+    pl = weights.balanced_placement(ids, E, P)
+    assert sorted(e for es in pl for e in es) == list(range(E)) and all(len(es) == E // P for es in pl)
+    counts = torch.bincount(ids.flatten().long(), minlength=E)
+    per_rank = [int(counts[es].sum()) for es in pl]
+    contiguous = [int(counts[r * E // P:(r + 1) * E // P].sum()) for r in range(P)]
+    mean = ids.numel() / P
+    assert max(per_rank) <= 1.05 * mean < max(contiguous)      # Zipf routing: contiguous is skewed
+    assert weights.balanced_placement(ids, E, P) == pl            # deterministic
+    owner = weights.expert_owner(pl)
+    assert all(int(owner[e]) == r for r, es in enumerate(pl) for e in es)
+
+
+def test_ep_views_with_a_placement_gather_the_rank_experts():
+    from td_benchmark_b200 import weights
+    E = 8
+    w1 = torch.arange(E * 256 * 128, dtype=torch.float32).view(E, 256, 128).to(torch.float8_e4m3fn)
+    s1 = torch.arange(E * 2, dtype=torch.float32).view(E, 2, 1)
+    w2 = torch.zeros((E, 128, 128), dtype=torch.float8_e4m3fn)
+    s2 = torch.arange(E, dtype=torch.float32).view(E, 1, 1)
+    pl = [[1, 6], [0, 7], [2, 5], [3, 4]]
+    v = weights.ep_views(w1, s1, w2, s2, 2, 4, placement=pl)
+    assert torch.equal(v["w1_scale"], s1[[2, 5]]) and torch.equal(v["w2_scale"], s2[[2, 5]])
+    assert v["expert_map"].tolist() == [-1, -1, 0, -1, -1, 1, -1, -1]
+    assert v["expert_owner"].tolist() == [1, 0, 2, 3, 3, 2, 0, 1]
+    c = weights.ep_views(w1, s1, w2, s2, 1, 4)
+    assert torch.equal(c["w1_scale"], s1[2:4]) and c["expert_owner"].tolist() == [0, 0, 1, 1, 2, 2, 3, 3]
