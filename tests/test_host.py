@@ -187,3 +187,35 @@ def test_ep_views_with_a_placement_gather_the_rank_experts():
     assert v["expert_owner"].tolist() == [1, 0, 2, 3, 3, 2, 0, 1]
     c = weights.ep_views(w1, s1, w2, s2, 1, 4)
     assert torch.equal(c["w1_scale"], s1[2:4]) and c["expert_owner"].tolist() == [0, 0, 1, 1, 2, 2, 3, 3]
+
+
+def test_sweep_and_peaks_modules_parse_their_arguments():
+    """The user-facing measurement modules start and print their usage without a GPU."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    for mod in ("td_benchmark_b200.sweep", "td_benchmark_b200.peaks"):
+        res = subprocess.run([sys.executable, "-m", mod, "--help"], capture_output=True, text=True, cwd=root)
+        assert res.returncode == 0 and "usage" in res.stdout, (mod, res.stderr[-500:])
+
+
+def test_sweep_variant_table():
+    import torch.distributed as dist
+    from td_benchmark_b200 import sweep
+    from td_benchmark_b200.context import DistContext
+
+    own = not dist.is_initialized()
+    if own:
+        dist.init_process_group("gloo", init_method="tcp://127.0.0.1:0", rank=0, world_size=1)
+    try:
+        ctx = DistContext()
+        assert sweep._exchange("nccl", ctx).name == "nccl"
+        ex = sweep._exchange("ce4", ctx)
+        assert ex.rs_mode == "ce" and ex.chunks_req == 4
+        assert sweep._exchange("sparse", ctx).sparse and sweep._exchange("fp8rs", ctx).rs_mode == "fp8"
+        with pytest.raises(ValueError):
+            sweep._exchange("ring", ctx)
+    finally:
+        if own:
+            dist.destroy_process_group()
