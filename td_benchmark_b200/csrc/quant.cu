@@ -122,6 +122,9 @@ __global__ void __launch_bounds__(kQuantThreads)
   for (int64_t v = static_cast<int64_t>(blockIdx.x) * kQuantThreads + threadIdx.x; v < total; v += stride) {
     const int64_t t = v / vec;
     const int64_t c = v - t * vec;
+    bool any = false;  // expert parallel: rows of tokens with no local pair are not read
+    for (int j = 0; j < d.top_k && !any; ++j) any = __ldg(d.pair_pos + t * d.top_k + j) >= 0;
+    if (!any) continue;
     const uint4 val = __ldg(reinterpret_cast<const uint4*>(xq + t * cols) + c);
     for (int j = 0; j < d.top_k; ++j) {
       const int32_t pos = __ldg(d.pair_pos + t * d.top_k + j);

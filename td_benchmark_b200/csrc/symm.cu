@@ -252,7 +252,12 @@ __global__ void __launch_bounds__(kThreads)
       ready |= 1u << src;
     }
     int32_t pos[8];
-    for (int j = 0; j < top_k && j < 8; ++j) pos[j] = __ldg(pair_pos + t * top_k + j);
+    bool any = false;
+    for (int j = 0; j < top_k && j < 8; ++j) {
+      pos[j] = __ldg(pair_pos + t * top_k + j);
+      any = any || pos[j] >= 0;
+    }
+    if (!any) continue;  // no pair of this token is local (expert parallel): its row is not read
     for (int64_t c = lane; c < vec; c += 32) {
       const uint4 v = __ldcg(reinterpret_cast<const uint4*>(xq + t * cols + c * 16));
       for (int j = 0; j < top_k && j < 8; ++j)

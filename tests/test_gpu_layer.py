@@ -130,6 +130,17 @@ def test_host_pipeline_matches_direct_forward():
     layer.check()
     for w, o in zip(want, outs):
         assert torch.equal(w.cpu(), o)
+    # whole-tensor copies (chunk_bytes=0) and traced steps give the same results
+    for kw in ({"chunk_bytes": 0}, {"trace": True, "chunk_bytes": 64 << 10}):
+        pipe2 = HostPipeline(layer, **kw)
+        outs2 = [torch.empty(want[0].shape, dtype=torch.bfloat16).pin_memory() for _ in xs]
+        for x, o in zip(xs, outs2):
+            pipe2.submit(x.cpu().pin_memory(), ids.cpu().pin_memory(), wts.cpu().pin_memory(), o)
+        pipe2.drain()
+        assert all(torch.equal(w.cpu(), o) for w, o in zip(want, outs2))
+        if kw.get("trace"):
+            sp = pipe2.spans()
+            assert sp["steps"] == len(xs) and sp["forward_ms"] > 0 and sp["h2d_ms"] > 0 and sp["d2h_ms"] > 0
     out_dev = torch.empty_like(want[0])
     assert layer.forward(xs[2], ids, wts, out=out_dev) is out_dev and torch.equal(out_dev, want[2])
     with pytest.raises(ValueError):
