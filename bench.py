@@ -191,8 +191,20 @@ def rank_work(layer, topk_ids, inter: int, shared_inter: int, rs_fp8: bool = Fal
         rows = int(hit.sum().item())
     ag = rows * row_fp8
     rs = rows * (row_fp8 if rs_fp8 else 2 * H)
+    if getattr(ex, "rs_mode", None) == "gemm":
+        # the down GEMM sends each computed pair row (not a per-token partial) to its token's owner
+        tok = torch_arange_like(ids) // layer.top_k
+        remote = (tok // layer.T_local) != ex.rank
+        if layer.expert_map is not None:
+            remote &= layer.expert_map[ids] >= 0
+        rs = int(remote.sum().item()) * 2 * H
     return {"flops": flops, "weight_bytes": wbytes, "nvlink_bytes": float(ag + rs), "ag_bytes": ag, "rs_bytes": rs,
             "pairs": pairs, "experts_hit": hit}
+
+
+def torch_arange_like(t):
+    import torch
+    return torch.arange(t.numel(), device=t.device)
 
 
 def torch_unique_count(t) -> int:

@@ -56,7 +56,8 @@ namespace b2m {
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 128;
-constexpr int STAGES = 4;
+constexpr int STAGES = 4;          // operand stages of the grouped GEMMs
+constexpr int SCATTER_STAGES = 3;  // the down GEMM storing into owners: 3 stages + the row staging tile
 constexpr int SRING = 8;     // scale ring depth (decoupled from the operand stages)
 constexpr int GROUP_M = 16;  // tile raster: bands of GROUP_M M-blocks x all N tiles
 constexpr int A_BYTES = BM * BK;  // 16 KB
@@ -68,9 +69,10 @@ constexpr int NUM_EPI_THREADS = NUM_EPI_WARPS * 32;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t IDESC = idesc_e4m3_f32(BM, BN);
 
-struct Control {
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+template <int S>
+struct ControlT {
+  uint64_t full[S];
+  uint64_t empty[S];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t amax_bar[2];
@@ -82,10 +84,22 @@ struct Control {
   alignas(16) float as[SRING][BM];  // A row scales of K block kbg (slot kbg % SRING)
   alignas(16) float bs[SRING][4];   // B block scales of that K block: tile rows [0,128) and [128,256)
   float amax[2][2][BM];              // [tile parity][column half][row]
+  uint64_t stg_free[2];              // row staging: every epilogue thread may overwrite it ([tile parity])
+  uint64_t stg_full[2];              // row staging: every epilogue thread has written its row piece
 };
 
-constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + sizeof(Control) + 1024;
-static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+// Row staging of the scattering down GEMM: the tile's 128 bf16 output rows (256 columns)
+// with 16 bytes of padding per row so that the epilogue's 16-byte stores (32 lanes on 32
+// consecutive rows) spread over all banks.
+constexpr int STG_ROW_BYTES = BN * 2 + 16;
+constexpr int STG_BYTES = BM * STG_ROW_BYTES;
+
+template <int S>
+constexpr size_t smem_bytes() {
+  return size_t(S) * STAGE_BYTES + sizeof(ControlT<S>) + (S == SCATTER_STAGES ? STG_BYTES + 128 : 0) + 1024;
+}
+static_assert(smem_bytes<STAGES>() <= 227 * 1024, "shared memory budget");
+static_assert(smem_bytes<SCATTER_STAGES>() <= 227 * 1024, "shared memory budget (scattering down GEMM)");
 
 struct GemmParams {
   const int32_t* sorted_ids;
@@ -260,9 +274,9 @@ __device__ __forceinline__ void push_rows(const GemmParams& p, int lane) {
 }
 
 // ---------------------------------------------------------------- warp 0: B (+A for the down GEMM)
-template <bool kGateUp>
+template <bool kGateUp, int S>
 __device__ __forceinline__ void stage_producer(const CUtensorMap* map_a, const CUtensorMap* map_b,
-                                               const GemmParams& p, uint8_t* smem, Control* C, TileWalk tw,
+                                               const GemmParams& p, uint8_t* smem, ControlT<S>* C, TileWalk tw,
                                                int lane) {
   volatile int* abort = &C->abort;
   uint32_t kbg = 0;
@@ -292,8 +306,8 @@ __device__ __forceinline__ void stage_producer(const CUtensorMap* map_a, const C
       }
       const float s0 = __shfl_sync(0xffffffffu, pre0, kb & 31);
       const float s1 = __shfl_sync(0xffffffffu, pre1, kb & 31);
-      const int s = kbg % STAGES;
-      const uint32_t ph = (kbg / STAGES) & 1;
+      const int s = kbg % S;
+      const uint32_t ph = (kbg / S) & 1;
       const int r = kbg % SRING;
       const uint32_t rph = (kbg / SRING) & 1;
       int ok = 1;
@@ -319,12 +333,12 @@ __device__ __forceinline__ void stage_producer(const CUtensorMap* map_a, const C
       __syncwarp();
     }
   }
-  // Drain: the copies of the last STAGES stages (and SRING scale slots) must have
+  // Drain: the copies of the last S stages (and SRING scale slots) must have
   // landed before the CTA exits.
   if (lane == 0) {
-    const uint32_t first = kbg > STAGES ? kbg - STAGES : 0;
+    const uint32_t first = kbg > S ? kbg - S : 0;
     for (uint32_t i = first; i < kbg; ++i)
-      mbar_wait(&C->full[i % STAGES], (i / STAGES) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
+      mbar_wait(&C->full[i % S], (i / S) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
     const uint32_t rfirst = kbg > SRING ? kbg - SRING : 0;
     for (uint32_t i = rfirst; i < kbg; ++i)
       mbar_wait(&C->sfull[i % SRING], (i / SRING) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_DRAIN, nullptr);
@@ -333,7 +347,8 @@ __device__ __forceinline__ void stage_producer(const CUtensorMap* map_a, const C
 }
 
 // ---------------------------------------------------------------- warp 1 lane 0: MMA issue
-__device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, Control* C, TileWalk tw,
+template <int S>
+__device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, ControlT<S>* C, TileWalk tw,
                                            uint32_t tmem_base) {
   volatile int* abort = &C->abort;
   uint32_t kbg = 0;
@@ -343,8 +358,8 @@ __device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, C
     tile_coords(tile, tw, mb, nt);
     if (__ldg(p.expert_ids + mb) < 0) continue;
     for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
-      const int s = kbg % STAGES;
-      const uint32_t ph = (kbg / STAGES) & 1;
+      const int s = kbg % S;
+      const uint32_t ph = (kbg / S) & 1;
       const int b = kbg & 1;
       const uint32_t tph = (kbg >> 1) & 1;
       if (!mbar_wait(&C->tempty[b], tph ^ 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_MMA, abort) ||
@@ -379,7 +394,8 @@ template <bool kGateUp>
 __device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)[2][BM], uint64_t* amax_bar,
                                            float (&acc)[128], int64_t prow, int nt, int h, int r, int pair,
                                            float wrow, bool valid, uint32_t tiles_done, int lane,
-                                           volatile int* abort) {
+                                           volatile int* abort, uint8_t* staging = nullptr,
+                                           uint64_t* stg_free = nullptr, uint64_t* stg_full = nullptr) {
   if (kGateUp) {
     // h = silu(gate) * up, then 1x128 quant across both column halves of the row.
     float amax = 0.0f;
@@ -413,6 +429,49 @@ __device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)
       *reinterpret_cast<uint4*>(dst + i) = w;
     }
     if (h == 0) p.out_scale_t[static_cast<int64_t>(nt) * p.rows_cap + prow] = scale;
+  } else if (staging) {
+    // Scattering down GEMM: whole rows leave through shared memory.  Each thread writes its
+    // 128 columns of row r into the staging tile; then lanes 0-15 of every epilogue warp
+    // each send one of the tile's rows (512 bytes: both column halves) to its owner with a
+    // bulk store -- NVLink carries whole row pieces, and the stores drain while the next
+    // tile's MMAs run.  The staging tile is reused only after this thread's previous bulk
+    // stores have read it and every thread has passed that point (bounded mbarrier waits,
+    // so a warp that aborted cannot leave the others waiting).
+    const int par = tiles_done & 1;
+    const bool issuer = lane < 16;
+    if (issuer) bulk_wait_read_all();
+    mbar_arrive(&stg_free[par]);
+    int ok = mbar_wait(&stg_free[par], (tiles_done >> 1) & 1, p.pipe_timeout_ns, p.status,
+                       B2M_STATUS_TIMEOUT_EPILOGUE, abort);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    if (2 * nt + h < p.n_blocks) {
+      uint8_t* srow = staging + r * STG_ROW_BYTES + h * 256;
+#pragma unroll
+      for (int i = 0; i < 128; i += 8) {
+        uint32_t u[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const __nv_bfloat162 v = __floats2bfloat162_rn(acc[i + 2 * j] * wrow, acc[i + 2 * j + 1] * wrow);
+          u[j] = *reinterpret_cast<const uint32_t*>(&v);
+        }
+        *reinterpret_cast<uint4*>(srow + i * 2) = make_uint4(u[0], u[1], u[2], u[3]);
+      }
+    }
+    fence_proxy_async_smem();  // the bulk stores read these rows through the async proxy
+    mbar_arrive(&stg_full[par]);
+    ok = mbar_wait(&stg_full[par], (tiles_done >> 1) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
+                   abort);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    const int src_lane = h * 16 + (lane & 15);  // the lane of this warp that holds the row this lane sends
+    const int rpair = __shfl_sync(0xffffffffu, pair, src_lane);
+    if (issuer && rpair < p.numel) {
+      const int rr = (r - lane) + src_lane;
+      const int qo = static_cast<int>(rpair / p.rs_pairs_per_owner);
+      __nv_bfloat16* dst =
+          p.rs_dst[qo] + (p.rs_row0 + rpair - qo * p.rs_pairs_per_owner) * p.hidden + static_cast<int64_t>(nt) * BN;
+      bulk_store(dst, staging + rr * STG_ROW_BYTES, 2 * nt + 1 < p.n_blocks ? 512u : 256u);
+      bulk_commit();
+    }
   } else {
     const bool cols_valid = 2 * nt + h < p.n_blocks;
     if (valid && cols_valid) {
@@ -438,9 +497,9 @@ __device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)
 }
 
 // ---------------------------------------------------------------- warps 4-11: promotion + epilogue
-template <bool kGateUp>
-__device__ __forceinline__ void epilogue_warps(const GemmParams& p, Control* C, TileWalk tw, uint32_t tmem_base,
-                                               int warp, int lane) {
+template <bool kGateUp, int S>
+__device__ __forceinline__ void epilogue_warps(const GemmParams& p, ControlT<S>* C, TileWalk tw, uint32_t tmem_base,
+                                               int warp, int lane, uint8_t* staging) {
   volatile int* abort = &C->abort;
   const int q = warp & 3;         // TMEM lane quarter this warp may access
   const int h = (warp - 4) >> 2;  // column half
@@ -529,20 +588,25 @@ __device__ __forceinline__ void epilogue_warps(const GemmParams& p, Control* C, 
     if (!alive) break;
 
     if (!finish_tile<kGateUp>(p, C->amax, C->amax_bar, acc, prow, nt, h, r, pair, wrow, valid, tiles_done, lane,
-                              abort))
+                              abort, staging, C->stg_free, C->stg_full))
       break;
     ++tiles_done;
     tile = tile_after;
   }
+  if (staging && lane < 16) bulk_wait_all();  // the rows this thread sent have landed before the CTA exits
 }
 
-template <bool kGateUp>
+template <bool kGateUp, int S>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                     const __grid_constant__ GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Control* C = reinterpret_cast<Control*>(smem + STAGES * STAGE_BYTES);
+  ControlT<S>* C = reinterpret_cast<ControlT<S>*>(smem + S * STAGE_BYTES);
+  uint8_t* staging = nullptr;
+  if (S == SCATTER_STAGES)
+    staging = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem + S * STAGE_BYTES + sizeof(ControlT<S>)) + 127) & ~uintptr_t(127));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -556,7 +620,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     p.block_order};
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&C->full[s], 1);
       mbar_init(&C->empty[s], 1);
     }
@@ -568,6 +632,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&C->tfull[b], 1);
       mbar_init(&C->tempty[b], NUM_EPI_WARPS);
       mbar_init(&C->amax_bar[b], NUM_EPI_THREADS);
+      mbar_init(&C->stg_free[b], NUM_EPI_THREADS);
+      mbar_init(&C->stg_full[b], NUM_EPI_THREADS);
     }
     mbar_init(&C->mma_done, 1);
     C->abort = 0;
@@ -586,16 +652,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp < 4) {
     reg_dealloc<72>();
     if (warp == 0) {
-      stage_producer<kGateUp>(&map_a, &map_b, p, smem, C, tw, lane);
+      stage_producer<kGateUp, S>(&map_a, &map_b, p, smem, C, tw, lane);
     } else if (warp == 1) {
-      if (lane == 0) mma_thread(p, smem, C, tw, tmem_base);
+      if (lane == 0) mma_thread<S>(p, smem, C, tw, tmem_base);
       __syncwarp();
     } else if (kGateUp && p.push_world > 1) {
       push_rows(p, lane);
     }
   } else {
     reg_alloc<216>();
-    epilogue_warps<kGateUp>(p, C, tw, tmem_base, warp, lane);
+    epilogue_warps<kGateUp, S>(p, C, tw, tmem_base, warp, lane, staging);
   }
 
   tc_fence_before();
@@ -961,11 +1027,12 @@ int ensure_smem_attr(std::atomic<bool> (&done)[64], Kernel kernel, size_t bytes,
   return B2M_OK;
 }
 
-template <bool kGateUp>
+template <bool kGateUp, int S = STAGES>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int num_sms, cudaStream_t s) {
   // num_sms here is the CTA budget (all SMs, or fewer when the caller keeps SMs for comm kernels)
+  constexpr size_t SMEM_BYTES = smem_bytes<S>();
   static std::atomic<bool> attr_done[64];
-  B2M_TRY(ensure_smem_attr(attr_done, moe_gemm_kernel<kGateUp>, SMEM_BYTES, "gemm: cudaFuncSetAttribute"));
+  B2M_TRY(ensure_smem_attr(attr_done, moe_gemm_kernel<kGateUp, S>, SMEM_BYTES, "gemm: cudaFuncSetAttribute"));
   int64_t upper = static_cast<int64_t>(p.max_blocks) * p.num_nt;
   int grid = static_cast<int>(upper < num_sms ? upper : num_sms);
   if (grid < 1) grid = 1;
@@ -984,9 +1051,10 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& 
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return check_cuda(cudaLaunchKernelEx(&cfg, moe_gemm_kernel<kGateUp>, ma, mb, p), "gemm1 push (cooperative) launch");
+    return check_cuda(cudaLaunchKernelEx(&cfg, moe_gemm_kernel<kGateUp, S>, ma, mb, p),
+                      "gemm1 push (cooperative) launch");
   }
-  moe_gemm_kernel<kGateUp><<<grid, NUM_THREADS, SMEM_BYTES, s>>>(ma, mb, p);
+  moe_gemm_kernel<kGateUp, S><<<grid, NUM_THREADS, SMEM_BYTES, s>>>(ma, mb, p);
   return check_cuda(cudaGetLastError(), kGateUp ? "gemm1 launch" : "gemm2 launch");
 }
 
@@ -1208,6 +1276,8 @@ int gemm2_impl(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int3
   }
   if (block_pairs)
     return launch_gemm_pair<false>(ma, mb, p, block_pairs, num_sms, static_cast<cudaStream_t>(stream));
+  if (sc)  // rows leave through the staging tile as whole-row bulk stores
+    return launch_gemm<false, SCATTER_STAGES>(ma, mb, p, num_sms, static_cast<cudaStream_t>(stream));
   return launch_gemm<false>(ma, mb, p, num_sms, static_cast<cudaStream_t>(stream));
 }
 

@@ -270,11 +270,13 @@ class P2PExchange:
            NVLink traffic runs under the GEMM; ``b2m_signal`` publishes the flags after it
            and the owner sums sources and top-k rows in one pass (``b2m_rs_combine``).  Not
            with a tensor-parallel shared expert (its partials must join before the push).
-           Correct but slower as built: every epilogue thread stores 16 bytes of a different
-           row per instruction, and such small remote writes stall the GEMM (DeepSeek-V3
-           EP8: down GEMM 1424 us instead of 448, layer 2464 vs 1648 us; Mixtral TP2 1015
-           vs 995 us).  Rows would have to leave through shared memory as whole-row bulk
-           copies, for which the GEMM has no shared memory to spare.
+           The GEMM runs with 3 operand stages so that a 66 KB staging tile fits beside
+           them: each finished tile's rows are written there, and one thread per row sends
+           the row's 512 bytes to its owner with a bulk copy that drains under the next
+           tile's MMAs.  (Storing 16 bytes of a different row per thread and instruction
+           straight from registers stalled the GEMM: DeepSeek-V3 EP8 down GEMM 1424 us
+           instead of 448.)  Under expert parallelism this is sparse by construction: only
+           the pairs this rank computed cross, each to its token's owner.
       "sm" (default) -- after the whole down GEMM, ``b2m_combine_push`` stores each
            token's partial into its owner's slot with SM stores and publishes the flags.
       "ce" -- the down GEMM runs in ``chunks`` column chunks on all SMs; after each chunk
@@ -320,8 +322,10 @@ class P2PExchange:
         P, T, H, Tl = self.world_size, layer.T, layer.H, layer.T_local
         if self.sparse:
             # sends decided per (token, rank) by SM stores: no contiguous-block copies
-            if not layer.ep or self.ag_mode in ("ce", "push") or self.rs_mode not in ("sm", "fp8"):
-                raise ValueError("sparse exchange needs expert parallelism, ag_mode 'sm'/'auto' and rs_mode 'sm'/'fp8'")
+            # (rs_mode 'gemm' is sparse already: each pair row goes only to its token's owner)
+            if not layer.ep or self.ag_mode in ("ce", "push") or self.rs_mode == "ce":
+                raise ValueError("sparse exchange needs expert parallelism, ag_mode 'sm'/'auto' and rs_mode "
+                                 "'sm'/'fp8'/'gemm'")
             if layer.E % P:
                 raise ValueError(f"sparse exchange needs E={layer.E} divisible by world_size={P}")
             self.ag_mode = "sm"

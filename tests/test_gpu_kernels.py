@@ -332,15 +332,17 @@ def test_combine_bit_exact(T, k, H, shared):
     assert np.array_equal(out.view(torch.int16).cpu().numpy().astype(np.uint16), exp)
 
 
-@pytest.mark.parametrize("world,src,paired", [(2, 1, False), (4, 0, False), (4, 3, True)])
-def test_gemm2_scatter_and_rs_combine(world, src, paired):
+@pytest.mark.parametrize("world,src,paired,H", [(2, 1, False, 512), (4, 0, False, 640), (4, 3, True, 512),
+                                                 (2, 0, False, 384)])
+def test_gemm2_scatter_and_rs_combine(world, src, paired, H):
     """Down GEMM storing into owner buffers (owners emulated by buffers on this GPU): every
     pair row lands bit-identical to b2m_gemm2's row at owner p // ppo, row row0 + p - q*ppo;
-    the owner combine equals a sequential fp32 sum over sources and top-k rows."""
+    the owner combine equals a sequential fp32 sum over sources and top-k rows.  H = 640 and
+    384 end on a half column tile (a 256-byte row piece instead of 512)."""
     from td_benchmark_b200 import _lib
     from td_benchmark_b200.symm import ptr_array
 
-    T, H, I, E, k = 256, 512, 256, 4, 2
+    T, I, E, k = 256, 256, 4, 2
     x, w1q, w1s, w2q, w2s, ids, wts = _gemm_problem(T, H, I, E, k, 77 + world, False)
     xq, xs = ops.quant_g128(x.to(DEV))
     w1i, w1is = ops.w1_interleave(w1q.to(DEV), w1s.to(DEV))

@@ -50,6 +50,7 @@ def _port() -> int:
     # sparse expert-parallel exchange (bit-identical to the dense one)
     ("d4", "dsv3", 1024, ["--zipf", "--sparse"]),
     ("d4", "dsv3", 512, ["--sparse", "--rs-dtype", "fp8"]),
+    ("d4", "dsv3", 1024, ["--zipf", "--sparse", "--rs-mode", "gemm"]),
     # experts placed by routed load instead of contiguous ranges (same output within the gates)
     ("d4", "dsv3", 1024, ["--zipf", "--placement", "balanced"]),
     ("d4", "dsv3", 1024, ["--zipf", "--placement", "balanced", "--sparse", "--rs-dtype", "fp8"]),
