@@ -1,4 +1,6 @@
 // Top-k combine (+ shared expert add) and the gate/up weight interleave used at set-up.
+#include <atomic>
+
 #include "b2m_common.cuh"
 #include "b2m_host.h"
 
@@ -7,9 +9,12 @@ namespace {
 
 constexpr int kCombineThreads = 256;
 
-// out[t, :] = bf16(sum_j staged[t*k + j, :] + shared[t, :]): one warp per token, so the
-// token's expert ids and map entries are read once (a warp-uniform pair mask) and the
-// lanes walk the row 8 columns at a time.
+constexpr int64_t kCombineChunk = 1024;  // columns of one work unit (4 warp-wide steps of 8 columns per lane)
+
+// out[t, :] = bf16(sum_j staged[t*k + j, :] + shared[t, :]).  A warp takes one unit -- a
+// token's 1024-column chunk -- at a time, so the grid (every resident warp) finishes in
+// near-equal shares instead of in waves of whole tokens; the token's expert ids and map
+// entries give a warp-uniform pair mask, and the lanes walk the chunk 8 columns at a time.
 __global__ void __launch_bounds__(kCombineThreads)
     combine_kernel(const __nv_bfloat16* __restrict__ staged, int64_t tokens, int top_k, int64_t hidden,
                    const int32_t* __restrict__ topk_ids, const int32_t* __restrict__ expert_map,
@@ -17,10 +22,13 @@ __global__ void __launch_bounds__(kCombineThreads)
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kCombineThreads + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kCombineThreads) >> 5;
-  for (int64_t t = warp; t < tokens; t += nwarps) {
+  const int64_t chunks = (hidden + kCombineChunk - 1) / kCombineChunk;
+  for (int64_t u = warp; u < tokens * chunks; u += nwarps) {
+    const int64_t t = u / chunks;
+    const int64_t c_end = min(hidden, (u - t * chunks + 1) * kCombineChunk);
     const uint32_t mask = local_pair_mask(topk_ids, expert_map, t, top_k, lane);
 #pragma unroll 2
-    for (int64_t c = lane * 8; c < hidden; c += 256)
+    for (int64_t c = (u - t * chunks) * kCombineChunk + lane * 8; c < c_end; c += 256)
       *reinterpret_cast<uint4*>(out + t * ld_out + c) =
           combine_vec(staged, t, top_k, hidden, c, mask, topk_ids, expert_map, shared);
   }
@@ -77,8 +85,18 @@ extern "C" int b2m_combine(const void* staged, int64_t tokens, int32_t top_k, in
   if (!staged || !out || (expert_map && !topk_ids)) return fail(B2M_ERR_ARG, "combine: null pointer");
   if (!aligned16(staged) || !aligned16(out) || (shared && !aligned16(shared)))
     return fail(B2M_ERR_ARG, "combine: pointers must be 16-byte aligned");
-  int64_t blocks = (tokens * 32 + kCombineThreads - 1) / kCombineThreads;  // a warp per token
-  if (blocks > int64_t(num_sms) * 8) blocks = int64_t(num_sms) * 8;
+  // every resident warp, or fewer when there are fewer units
+  static std::atomic<int> resident{0};  // blocks per SM (the same on every sm_100 device)
+  int per_sm = resident.load(std::memory_order_relaxed);
+  if (per_sm == 0) {
+    B2M_TRY(check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, combine_kernel, kCombineThreads, 0),
+                       "combine: occupancy"));
+    per_sm = per_sm > 0 ? per_sm : 1;
+    resident.store(per_sm, std::memory_order_relaxed);
+  }
+  const int64_t units = tokens * ((hidden + kCombineChunk - 1) / kCombineChunk);
+  int64_t blocks = (units * 32 + kCombineThreads - 1) / kCombineThreads;
+  if (blocks > int64_t(num_sms) * per_sm) blocks = int64_t(num_sms) * per_sm;
   combine_kernel<<<static_cast<unsigned>(blocks), kCombineThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, topk_ids, expert_map,
       static_cast<const __nv_bfloat16*>(shared), static_cast<__nv_bfloat16*>(out), ld_out);
