@@ -150,15 +150,11 @@ int b2m_w1_interleave(const void* w1, const float* w1_scale, int32_t num_experts
  * rows_cap/128 entries.
  * block_pairs (nullable): the pair list of b2m_align.  When given, the GEMM runs on
  * CTA pairs (cta_group::2, M = 256 over two consecutive blocks of one expert, half
- * of each B tile staged per CTA); otherwise one CTA per 128-row block.
- * sorted_token_ids / numel (nullable / ignored when NULL): b2m_align's sorted ids and pad
- * id.  When given (and without block_pairs), a block whose rows [64, 128) are all pads
- * runs as an M = 64 tile and its rows [64, 128) of out_q / out_scale_t are left unwritten
- * (b2m_gemm2 runs such blocks as M = 64 tiles too, so it never reads them). */
+ * of each B tile staged per CTA); otherwise one CTA per 128-row block. */
 int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden, const void* w1,
               const float* w1_scale, int32_t num_experts, int32_t inter, const int32_t* expert_ids,
-              const int32_t* num_tokens_post_padded, const int32_t* block_pairs, const int32_t* sorted_token_ids,
-              int64_t numel, void* out_q, float* out_scale_t, int32_t* dev_status, void* stream);
+              const int32_t* num_tokens_post_padded, const int32_t* block_pairs, void* out_q, float* out_scale_t,
+              int32_t* dev_status, void* stream);
 
 /* b2m_gemm1 for a tensor-parallel layer whose A rows are stored by the source ranks while
  * it runs, so the all-gather overlaps the GEMM (replaces the all-gather + gate/up GEMM of
@@ -190,9 +186,7 @@ int b2m_gemm1_wait(const void* a_sorted, const float* a_scale_t, int64_t rows_ca
  * w(pair) = topk_weights[pair] (flat [T*k] fp32), or 1 when topk_weights is NULL.
  * a_fp8 / a_scale_t: K3's out_q / out_scale_t; w2: e4m3 [E, hidden, I];
  * w2_scale: fp32 [E, ceil(hidden/128), I/128]; out: bf16 [numel, hidden] indexed by pair.
- * hidden % 128 == 0, I % 128 == 0.  block_pairs as for b2m_gemm1.  Without block_pairs,
- * a block whose rows [64, 128) are all pads runs as an M = 64 tile (rows [64, 128) of A
- * are not read).
+ * hidden % 128 == 0, I % 128 == 0.  block_pairs as for b2m_gemm1.
  * Only output columns [col_begin, col_end) are computed (col_begin a multiple of 256,
  * col_end a multiple of 256 or hidden; col_end <= 0 means hidden): the reduce-scatter
  * of one column chunk can then overlap the GEMM of the next, as the reference's N-split

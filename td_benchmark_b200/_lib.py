@@ -26,7 +26,7 @@ SIGNATURES: dict[str, list] = {
     "b2m_align": [_p, _i64, _i32, _i32, _p, _p, _i64, _p, _i64, _p, _p, _p, _p],
     "b2m_block_order": [_p, _p, _i64, _i32, _i64, _i32, _i32, _p, _i64, _p, _p],
     "b2m_w1_interleave": [_p, _p, _i32, _i32, _i64, _p, _p, _p],
-    "b2m_gemm1": [_p, _p, _i64, _i64, _p, _p, _i32, _i32, _p, _p, _p, _p, _i64, _p, _p, _p, _p],
+    "b2m_gemm1": [_p, _p, _i64, _i64, _p, _p, _i32, _i32, _p, _p, _p, _p, _p, _p, _p],
     "b2m_gemm1_wait": [_p, _p, _i64, _i64, _p, _p, _i32, _i32, _p, _p, _p, _p, _i64, _i32, _i64, _p, _c.c_uint32, _p,
                        _i64, _p, _p, _p, _p, _i32, _i32, _p, _p, _p, _p],
     "b2m_gemm2": [_p, _p, _i64, _i32, _p, _p, _i32, _i64, _p, _p, _p, _p, _i64, _p, _p, _i64, _i64, _i32, _p, _p],

@@ -68,7 +68,6 @@ constexpr int NUM_EPI_WARPS = 8;
 constexpr int NUM_EPI_THREADS = NUM_EPI_WARPS * 32;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t IDESC = idesc_e4m3_f32(BM, BN);
-constexpr uint32_t IDESC_HALF = idesc_e4m3_f32(BM / 2, BN);  // M = 64: blocks whose rows [64, 128) are all pads
 
 template <int S>
 struct ControlT {
@@ -157,19 +156,7 @@ struct GemmParams {
   int32_t* push_counters;   // [push_world], zero between calls
   int32_t push_world;
   int32_t push_rank;
-  // 1: a block whose rows [64, 128) are all pads runs as an M = 64 tile (needs sorted_ids).
-  int32_t half_rows;
 };
-
-// The rows of an expert's segment are its pairs followed by pads (sorted ids ascend from the
-// segment start; pads hold numel), so row 64 being a pad means rows [64, 128) all are.  Such
-// a block runs as an M = 64 tile: half the MMA rows and half the accumulator to promote.
-// TMEM layout of the M = 64 accumulator (cta_group::1): row i sits in lane 32 * (i / 16) +
-// i % 16 for columns [0, 128) and 16 lanes higher for columns [128, 256), at TMEM column
-// (n % 128), so it fills all four lane quarters and 128 columns.
-__device__ __forceinline__ bool half_tile(const GemmParams& p, int mb) {
-  return p.half_rows && __ldg(p.sorted_ids + static_cast<int64_t>(mb) * BM + BM / 2) >= p.numel;
-}
 
 // silu(x) = x * sigmoid(x).  The gate/up intermediate is requantised to e4m3 right
 // after, so the fast exponential and reciprocal are far inside its tolerance.
@@ -370,7 +357,6 @@ __device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, C
     int mb, nt;
     tile_coords(tile, tw, mb, nt);
     if (__ldg(p.expert_ids + mb) < 0) continue;
-    const uint32_t idesc = half_tile(p, mb) ? IDESC_HALF : IDESC;
     for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
       const int s = kbg % S;
       const uint32_t ph = (kbg / S) & 1;
@@ -386,7 +372,7 @@ __device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, C
       const uint64_t bdesc = smem_desc_sw128(smem_u32(smem + s * STAGE_BYTES + A_BYTES));
       const uint32_t d = tmem_base + static_cast<uint32_t>(b * BN);
 #pragma unroll
-      for (int k = 0; k < BK / 32; ++k) mma_e4m3(d, adesc + 2 * k, bdesc + 2 * k, idesc, k > 0 ? 1u : 0u);
+      for (int k = 0; k < BK / 32; ++k) mma_e4m3(d, adesc + 2 * k, bdesc + 2 * k, IDESC, k > 0 ? 1u : 0u);
       mma_commit(&C->empty[s]);
       mma_commit(&C->tfull[b]);
     }
@@ -403,43 +389,21 @@ __device__ __forceinline__ void mma_thread(const GemmParams& p, uint8_t* smem, C
 // its 128 promoted fp32 columns.  Gate/up: h = silu(gate) * up, 1x128 requant across the
 // row's two column halves (partial amax exchanged through shared memory), codes + scale
 // stored at sorted row prow.  Down: routed weight, bf16, stored at the pair's row.
-// Half (M = 64) tiles: row r < 64, acc[0, 64) holds tile columns (lane / 16) * 128 + 64 h +
-// [0, 64) (gate/up: lanes 0-15 gate, lanes 16-31 the same row's up columns).
 // Returns false when the amax exchange timed out.
 template <bool kGateUp>
 __device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)[2][BM], uint64_t* amax_bar,
                                            float (&acc)[128], int64_t prow, int nt, int h, int r, int pair,
                                            float wrow, bool valid, uint32_t tiles_done, int lane,
-                                           volatile int* abort, bool half, uint8_t* staging = nullptr,
+                                           volatile int* abort, uint8_t* staging = nullptr,
                                            uint64_t* stg_free = nullptr, uint64_t* stg_full = nullptr) {
-  const int nb = lane >> 4;  // half tiles: the 128-column block of this lane's columns
   if (kGateUp) {
-    // h = silu(gate) * up, then 1x128 quant across both column halves of the row.  Half
-    // tiles: lane l < 16 holds gate columns 64h + [0, 64) of row r and lane l + 16 the up
-    // columns; the low lane makes outputs 64h + [0, 32), the high lane 64h + [32, 64), each
-    // swapping the 32 values the other needs.
+    // h = silu(gate) * up, then 1x128 quant across both column halves of the row.
     float amax = 0.0f;
-    int nout = 64, col = 64 * h;
-    if (half) {
-      const bool lo = lane < 16;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float other = __shfl_xor_sync(0xffffffffu, lo ? acc[32 + j] : acc[j], 16);
-        const float g = lo ? acc[j] : other;
-        const float u = lo ? other : acc[32 + j];
-        acc[j] = silu(g) * u;
-        amax = fmaxf(amax, fabsf(acc[j]));
-      }
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 16));
-      nout = 32;
-      col += 32 * nb;
-    } else {
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float v = silu(acc[i]) * acc[64 + i];
-        acc[i] = v;
-        amax = fmaxf(amax, fabsf(v));
-      }
+    for (int i = 0; i < 64; ++i) {
+      const float v = silu(acc[i]) * acc[64 + i];
+      acc[i] = v;
+      amax = fmaxf(amax, fabsf(v));
     }
     const int par = tiles_done & 1;
     amax_x[par][h][r] = amax;
@@ -450,10 +414,9 @@ __device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)
     amax = fmaxf(amax_x[par][0][r], amax_x[par][1][r]);
     const float scale = fmaxf(amax / 448.0f, 1e-12f);
     const float inv = 1.0f / scale;  // one IEEE division per row; codes use x * (1/scale)
-    uint8_t* dst = p.out_q + prow * p.inter + nt * 128 + col;
+    uint8_t* dst = p.out_q + prow * p.inter + nt * 128 + 64 * h;
 #pragma unroll
     for (int i = 0; i < 64; i += 16) {
-      if (i >= nout) break;
       uint4 w;
       w.x = pack4_e4m3(clamp448(acc[i + 0] * inv), clamp448(acc[i + 1] * inv), clamp448(acc[i + 2] * inv),
                        clamp448(acc[i + 3] * inv));
@@ -465,7 +428,7 @@ __device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)
                        clamp448(acc[i + 15] * inv));
       *reinterpret_cast<uint4*>(dst + i) = w;
     }
-    if (h == 0 && (!half || lane < 16)) p.out_scale_t[static_cast<int64_t>(nt) * p.rows_cap + prow] = scale;
+    if (h == 0) p.out_scale_t[static_cast<int64_t>(nt) * p.rows_cap + prow] = scale;
   } else if (staging) {
     // Scattering down GEMM: whole rows leave through shared memory.  Each thread writes its
     // 128 columns of row r into the staging tile; then lanes 0-15 of every epilogue warp
@@ -475,17 +438,16 @@ __device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)
     // stores have read it and every thread has passed that point (bounded mbarrier waits,
     // so a warp that aborted cannot leave the others waiting).
     const int par = tiles_done & 1;
-    if (lane < 16) bulk_wait_read_all();  // the lanes that may have sent rows of the last tile
+    const bool issuer = lane < 16;
+    if (issuer) bulk_wait_read_all();
     mbar_arrive(&stg_free[par]);
     int ok = mbar_wait(&stg_free[par], (tiles_done >> 1) & 1, p.pipe_timeout_ns, p.status,
                        B2M_STATUS_TIMEOUT_EPILOGUE, abort);
     if (!__all_sync(0xffffffffu, ok)) return false;
-    if (2 * nt + (half ? nb : h) < p.n_blocks) {
-      uint8_t* srow = staging + r * STG_ROW_BYTES + (half ? nb * 256 + h * 128 : h * 256);
-      const int ncols = half ? 64 : 128;
+    if (2 * nt + h < p.n_blocks) {
+      uint8_t* srow = staging + r * STG_ROW_BYTES + h * 256;
 #pragma unroll
       for (int i = 0; i < 128; i += 8) {
-        if (i >= ncols) break;
         uint32_t u[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -500,13 +462,10 @@ __device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)
     ok = mbar_wait(&stg_full[par], (tiles_done >> 1) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
                    abort);
     if (!__all_sync(0xffffffffu, ok)) return false;
-    // Senders: one lane per row -- lanes 0-15 of every warp (full tiles: warp (q, h) sends
-    // rows 32q + 16h + [0, 16)), or lanes 0-15 of the h = 0 warps (half tiles: their own rows).
-    const bool issuer = lane < 16 && (!half || h == 0);
-    const int src_lane = half ? lane : h * 16 + (lane & 15);  // the lane of this warp holding the sent row
+    const int src_lane = h * 16 + (lane & 15);  // the lane of this warp that holds the row this lane sends
     const int rpair = __shfl_sync(0xffffffffu, pair, src_lane);
     if (issuer && rpair < p.numel) {
-      const int rr = half ? r : (r - lane) + src_lane;
+      const int rr = (r - lane) + src_lane;
       const int qo = static_cast<int>(rpair / p.rs_pairs_per_owner);
       __nv_bfloat16* dst =
           p.rs_dst[qo] + (p.rs_row0 + rpair - qo * p.rs_pairs_per_owner) * p.hidden + static_cast<int64_t>(nt) * BN;
@@ -514,18 +473,16 @@ __device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)
       bulk_commit();
     }
   } else {
-    const bool cols_valid = 2 * nt + (half ? nb : h) < p.n_blocks;
+    const bool cols_valid = 2 * nt + h < p.n_blocks;
     if (valid && cols_valid) {
       __nv_bfloat16* row = p.out_bf16 + static_cast<int64_t>(pair) * p.hidden;
       if (p.rs_world > 0) {
         const int q = static_cast<int>(pair / p.rs_pairs_per_owner);
         row = p.rs_dst[q] + (p.rs_row0 + pair - q * p.rs_pairs_per_owner) * p.hidden;
       }
-      __nv_bfloat16* dst = row + nt * BN + (half ? 128 * nb + 64 * h : 128 * h);
-      const int ncols = half ? 64 : 128;
+      __nv_bfloat16* dst = row + nt * BN + 128 * h;
 #pragma unroll
       for (int i = 0; i < 128; i += 8) {
-        if (i >= ncols) break;
         uint32_t u[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -540,90 +497,24 @@ __device__ __forceinline__ bool finish_tile(const GemmParams& p, float (*amax_x)
 }
 
 // ---------------------------------------------------------------- warps 4-11: promotion + epilogue
-// One tile of one epilogue thread: the K loop (per K block, wait for the accumulator, load
-// this thread's columns from TMEM, release the buffer, promote with the block's scales) and
-// the tile's end.  kHalf: the tile runs as M = 64 (the thread's row is 16q + lane % 16 and it
-// promotes 64 columns); a compile-time path, so the two shapes do not share registers.
-// Returns false on a timeout or abort.
-template <bool kGateUp, bool kHalf, int S>
-__device__ __forceinline__ bool epilogue_tile(const GemmParams& p, ControlT<S>* C, uint32_t tmem_base, int q, int h,
-                                              int lane, int mb, int nt, int pair, uint32_t& kbg,
-                                              uint32_t tiles_done, uint8_t* staging, volatile int* abort) {
-  const int row = kHalf ? q * 16 + (lane & 15) : q * 32 + lane;
-  const int64_t prow = static_cast<int64_t>(mb) * BM + row;
-  const bool valid = pair < p.numel;
-  float wrow = 1.0f;
-  if (!kGateUp && valid && p.topk_weights) wrow = __ldg(p.topk_weights + pair);
-  const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-  // Column chunks owned by this thread (32 fp32 columns each) and which stage scale they use.
-  // Full tiles: gate/up chunks 64h + {0, 32} and 128 + 64h + {0, 32}, down 128h + {0..96};
-  // half tiles: TMEM columns 64h + {0, 32}, scale of the lane's 128-column block.
-  const uint32_t c0 = kHalf ? 64 * h : (kGateUp ? 64 * h : 128 * h);
-  const uint32_t c1 = c0 + 32;
-  const uint32_t c2 = kGateUp ? 128 + 64 * h : c0 + 64;
-  const uint32_t c3 = c2 + 32;
-  const int sidx_lo = kHalf ? (lane >> 4) : (kGateUp ? 0 : h);
-  const int sidx_hi = kGateUp ? 1 : h;
-
-  float acc[128];
-#pragma unroll
-  for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
-
-  for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
-    const int rs = kbg % SRING;
-    const int b = kbg & 1;
-    int ok = mbar_wait(&C->tfull[b], (kbg >> 1) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE, abort);
-    ok = ok && mbar_wait(&C->sfull[rs], (kbg / SRING) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
-                         abort);
-    if (!__all_sync(0xffffffffu, ok)) return false;
-    tc_fence_after();
-    const float sa = C->as[rs][row];
-    const float s_lo = sa * C->bs[rs][sidx_lo];
-    const float s_hi = sa * C->bs[rs][sidx_hi];
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&C->sempty[rs]);
-    const uint32_t base = tmem_base + lane_off + static_cast<uint32_t>(b * BN);
-    {
-      float v0[32], v1[32];
-      tmem_ld32(base + c0, v0);
-      tmem_ld32(base + c1, v1);
-      tmem_ld_wait();
-      if (kHalf) {  // the M = 64 accumulator fills 128 TMEM columns: this was all of it
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&C->tempty[b]);
-      }
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) fma2(acc[i], acc[i + 1], v0[i], v0[i + 1], s_lo);
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) fma2(acc[32 + i], acc[33 + i], v1[i], v1[i + 1], s_lo);
-    }
-    if (!kHalf) {
-      float v2[32], v3[32];
-      tmem_ld32(base + c2, v2);
-      tmem_ld32(base + c3, v3);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&C->tempty[b]);
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) fma2(acc[64 + i], acc[65 + i], v2[i], v2[i + 1], s_hi);
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) fma2(acc[96 + i], acc[97 + i], v3[i], v3[i + 1], s_hi);
-    }
-  }
-  return finish_tile<kGateUp>(p, C->amax, C->amax_bar, acc, prow, nt, h, row, pair, wrow, valid, tiles_done, lane,
-                              abort, kHalf, staging, C->stg_free, C->stg_full);
-}
-
 template <bool kGateUp, int S>
 __device__ __forceinline__ void epilogue_warps(const GemmParams& p, ControlT<S>* C, TileWalk tw, uint32_t tmem_base,
                                                int warp, int lane, uint8_t* staging) {
   volatile int* abort = &C->abort;
   const int q = warp & 3;         // TMEM lane quarter this warp may access
   const int h = (warp - 4) >> 2;  // column half
+  const int r = q * 32 + lane;    // tile row
+  const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
   uint32_t kbg = 0;
   uint32_t tiles_done = 0;
+  bool alive = true;
+  // Column chunks owned by this thread (32 fp32 columns each) and which stage scale they use.
+  const uint32_t c0 = kGateUp ? 64 * h : 128 * h;
+  const uint32_t c1 = c0 + 32;
+  const uint32_t c2 = kGateUp ? 128 + 64 * h : c0 + 64;
+  const uint32_t c3 = c2 + 32;
+  const int sidx_lo = kGateUp ? 0 : h;
+  const int sidx_hi = kGateUp ? 1 : h;
 
   // Row info of the next tile is loaded one tile ahead.
   int64_t tile = blockIdx.x;
@@ -636,26 +527,69 @@ __device__ __forceinline__ void epilogue_warps(const GemmParams& p, ControlT<S>*
     while (t < tw.num_tiles && __ldg(p.expert_ids + mb_of(t)) < 0) t += gridDim.x;
     return t;
   };
-  // This thread's tile row: 32q + lane, or 16q + lane % 16 in a half (M = 64) tile.
-  auto row_of = [&](bool half) { return half ? q * 16 + (lane & 15) : q * 32 + lane; };
   tile = next_valid(tile);
-  bool half_next = tile < tw.num_tiles && half_tile(p, mb_of(tile));
-  int pair_next = (!kGateUp && tile < tw.num_tiles) ? __ldg(p.sorted_ids + mb_of(tile) * BM + row_of(half_next)) : 0;
-  while (tile < tw.num_tiles) {
+  int pair_next = (!kGateUp && tile < tw.num_tiles) ? __ldg(p.sorted_ids + mb_of(tile) * BM + r) : 0;
+  for (; tile < tw.num_tiles && alive;) {
     int mb, nt;
     tile_coords(tile, tw, mb, nt);
-    const bool half = half_next;
+    const int64_t prow = static_cast<int64_t>(mb) * BM + r;
     const int pair = pair_next;
+    const bool valid = pair < p.numel;
+    float wrow = 1.0f;
+    if (!kGateUp && valid && p.topk_weights) wrow = __ldg(p.topk_weights + pair);
     const int64_t tile_after = next_valid(tile + gridDim.x);
-    if (tile_after < tw.num_tiles) {
-      half_next = half_tile(p, mb_of(tile_after));
-      if (!kGateUp) pair_next = __ldg(p.sorted_ids + mb_of(tile_after) * BM + row_of(half_next));
+    if (!kGateUp && tile_after < tw.num_tiles) pair_next = __ldg(p.sorted_ids + mb_of(tile_after) * BM + r);
+
+    float acc[128];
+#pragma unroll
+    for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+
+    for (int kb = 0; kb < p.num_kb; ++kb, ++kbg) {
+      const int rs = kbg % SRING;
+      const int b = kbg & 1;
+      int ok = mbar_wait(&C->tfull[b], (kbg >> 1) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE, abort);
+      ok = ok && mbar_wait(&C->sfull[rs], (kbg / SRING) & 1, p.pipe_timeout_ns, p.status, B2M_STATUS_TIMEOUT_EPILOGUE,
+                           abort);
+      if (!__all_sync(0xffffffffu, ok)) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const float sa = C->as[rs][r];
+      const float s_lo = sa * C->bs[rs][sidx_lo];
+      const float s_hi = sa * C->bs[rs][sidx_hi];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&C->sempty[rs]);
+      const uint32_t base = tmem_base + lane_off + static_cast<uint32_t>(b * BN);
+      {
+        float v0[32], v1[32];
+        tmem_ld32(base + c0, v0);
+        tmem_ld32(base + c1, v1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) fma2(acc[i], acc[i + 1], v0[i], v0[i + 1], s_lo);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) fma2(acc[32 + i], acc[33 + i], v1[i], v1[i + 1], s_lo);
+      }
+      {
+        float v2[32], v3[32];
+        tmem_ld32(base + c2, v2);
+        tmem_ld32(base + c3, v3);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&C->tempty[b]);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) fma2(acc[64 + i], acc[65 + i], v2[i], v2[i + 1], s_hi);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) fma2(acc[96 + i], acc[97 + i], v3[i], v3[i + 1], s_hi);
+      }
     }
-    const bool ok = half ? epilogue_tile<kGateUp, true, S>(p, C, tmem_base, q, h, lane, mb, nt, pair, kbg,
-                                                           tiles_done, staging, abort)
-                         : epilogue_tile<kGateUp, false, S>(p, C, tmem_base, q, h, lane, mb, nt, pair, kbg,
-                                                            tiles_done, staging, abort);
-    if (!ok) break;
+    if (!alive) break;
+
+    if (!finish_tile<kGateUp>(p, C->amax, C->amax_bar, acc, prow, nt, h, r, pair, wrow, valid, tiles_done, lane,
+                              abort, staging, C->stg_free, C->stg_full))
+      break;
     ++tiles_done;
     tile = tile_after;
   }
@@ -985,7 +919,7 @@ __device__ __forceinline__ void pair_epilogue(const GemmParams& p, PairControl* 
     if (!alive) break;
     if (mine) {
       if (!finish_tile<kGateUp>(p, C->amax, C->amax_bar, acc, prow, it.nt, h, r, pair, wrow, valid, tiles_done,
-                                lane, abort, false))
+                                lane, abort))
         break;
       ++tiles_done;
     }
@@ -1164,9 +1098,8 @@ struct SourceWait {
 
 int gemm1_impl(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden, const void* w1,
                const float* w1_scale, int32_t num_experts, int32_t inter, const int32_t* expert_ids,
-               const int32_t* num_tokens_post_padded, const int32_t* block_pairs, const int32_t* sorted_ids,
-               int64_t numel, void* out_q, float* out_scale_t, const SourceWait* sw, int32_t* dev_status,
-               void* stream) {
+               const int32_t* num_tokens_post_padded, const int32_t* block_pairs, void* out_q, float* out_scale_t,
+               const SourceWait* sw, int32_t* dev_status, void* stream) {
   int num_sms = 0;
   B2M_TRY(require_sm100(&num_sms));
   if (hidden <= 0 || hidden % 128 || inter <= 0 || inter % 128 || num_experts <= 0 || rows_cap <= 0 ||
@@ -1202,12 +1135,6 @@ int gemm1_impl(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, i
   p.status = dev_status;
   p.timeout_ns = timeout_ns();
   p.pipe_timeout_ns = 2 * p.timeout_ns;
-  if (sorted_ids) {  // half (M = 64) tiles for blocks whose rows [64, 128) are pads
-    if (numel < 0 || numel >= INT32_MAX) return fail(B2M_ERR_ARG, "gemm1: numel out of range");
-    p.sorted_ids = sorted_ids;
-    p.numel = static_cast<int32_t>(numel);
-    p.half_rows = 1;
-  }
   if (sw) {
     if (block_pairs) return fail(B2M_ERR_UNSUPPORTED, "gemm1_wait: no paired-CTA variant");
     if (!sw->block_order || !sw->sorted_ids || !sw->flags || sw->top_k < 1 || sw->tokens_per_src < 1 ||
@@ -1221,7 +1148,6 @@ int gemm1_impl(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, i
     p.block_order = sw->block_order;
     p.sorted_ids = sw->sorted_ids;
     p.numel = static_cast<int32_t>(sw->numel);
-    p.half_rows = 1;
     p.top_k = sw->top_k;
     p.tokens_per_src = sw->tokens_per_src;
     p.src_flags = sw->flags;
@@ -1256,11 +1182,10 @@ int gemm1_impl(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, i
 extern "C" int b2m_gemm1(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden,
                          const void* w1, const float* w1_scale, int32_t num_experts, int32_t inter,
                          const int32_t* expert_ids, const int32_t* num_tokens_post_padded,
-                         const int32_t* block_pairs, const int32_t* sorted_token_ids, int64_t numel, void* out_q,
-                         float* out_scale_t, int32_t* dev_status, void* stream) {
+                         const int32_t* block_pairs, void* out_q, float* out_scale_t, int32_t* dev_status,
+                         void* stream) {
   return b2m::gemm1_impl(a_sorted, a_scale_t, rows_cap, hidden, w1, w1_scale, num_experts, inter, expert_ids,
-                         num_tokens_post_padded, block_pairs, sorted_token_ids, numel, out_q, out_scale_t, nullptr,
-                         dev_status, stream);
+                         num_tokens_post_padded, block_pairs, out_q, out_scale_t, nullptr, dev_status, stream);
 }
 
 extern "C" int b2m_gemm1_wait(const void* a_sorted, const float* a_scale_t, int64_t rows_cap, int64_t hidden,
@@ -1275,7 +1200,7 @@ extern "C" int b2m_gemm1_wait(const void* a_sorted, const float* a_scale_t, int6
   const b2m::SourceWait sw{block_order, sorted_token_ids, numel, top_k, tokens_per_src, src_flags, epoch,
                            push_pos, push_pairs, push_a, push_s, push_flags, push_counters, world, rank};
   return b2m::gemm1_impl(a_sorted, a_scale_t, rows_cap, hidden, w1, w1_scale, num_experts, inter, expert_ids,
-                         num_tokens_post_padded, nullptr, nullptr, 0, out_q, out_scale_t, &sw, dev_status, stream);
+                         num_tokens_post_padded, nullptr, out_q, out_scale_t, &sw, dev_status, stream);
 }
 
 namespace b2m {
@@ -1320,7 +1245,6 @@ int gemm2_impl(const void* a_fp8, const float* a_scale_t, int64_t rows_cap, int3
   p.ntpp = num_tokens_post_padded;
   p.max_blocks = static_cast<int32_t>(rows_cap / BM);
   p.numel = static_cast<int32_t>(numel);
-  p.half_rows = 1;  // half (M = 64) tiles for blocks whose rows [64, 128) are pads
   p.top_k = 1;
   p.num_kb = inter / BK;
   p.nt_begin = static_cast<int32_t>(col_begin / BN);

@@ -123,7 +123,7 @@ class SharedExpert:
         r = self.route
         bp = r.pairs(self.paired)
         ops.gemm1(self.a, self.as_t, self.w.w1i, self.w.w1i_scale, r.expert_ids, r.ntpp, self.inter_q, self.inter_st,
-                  status, block_pairs=bp, sorted_ids=r.sorted_ids, numel=r.numel)
+                  status, block_pairs=bp)
         ops.gemm2(self.inter_q, self.inter_st, self.w.w2, self.w.w2_scale, r.sorted_ids, r.expert_ids, r.ntpp,
                   r.numel, None, self.out, status, block_pairs=bp)
         return self.out
@@ -715,8 +715,7 @@ class MoELayer:
         hook = getattr(self.exchange, "gemm1", None)
         if hook is None or not hook(self):
             ops.gemm1(self.a_sorted, self.as_t, self.w.w1i, self.w.w1i_scale, r.expert_ids, r.ntpp, self.inter_q,
-                      self.inter_st, self.status, block_pairs=r.pairs(self.paired), sorted_ids=r.sorted_ids,
-                      numel=self.numel)
+                      self.inter_st, self.status, block_pairs=r.pairs(self.paired))
         self._event("gemm1_end")
 
     def gemm2(self, topk_weights: torch.Tensor, cols: tuple[int, int] | None = None, max_ctas: int = 0) -> None:

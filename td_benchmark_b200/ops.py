@@ -170,13 +170,10 @@ def w1_interleave(w1: torch.Tensor, w1_scale: torch.Tensor) -> tuple[torch.Tenso
 def gemm1(a_sorted: torch.Tensor, a_scale_t: torch.Tensor, w1i: torch.Tensor, w1i_scale: torch.Tensor,
           expert_ids: torch.Tensor, ntpp: torch.Tensor, out_q: torch.Tensor | None = None,
           out_scale_t: torch.Tensor | None = None, status: torch.Tensor | None = None,
-          block_pairs: torch.Tensor | None = None, sorted_ids: torch.Tensor | None = None,
-          numel: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+          block_pairs: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Gate/up grouped GEMM + SiLU*mul + 1x128 requant on expert-sorted A.
 
-    a_sorted e4m3 [rows_cap, H], a_scale_t fp32 [H/128, rows_cap] -> (q [rows_cap, I], scale_t [I/128, rows_cap]).
-    With ``sorted_ids`` (and the pad id ``numel``), blocks whose rows [64, 128) are pads run as
-    M = 64 tiles and leave those rows of the output unwritten."""
+    a_sorted e4m3 [rows_cap, H], a_scale_t fp32 [H/128, rows_cap] -> (q [rows_cap, I], scale_t [I/128, rows_cap])."""
     _cuda(a_sorted, "a_sorted")
     rows_cap, hidden = a_sorted.shape
     e, n2, h2 = w1i.shape
@@ -191,8 +188,7 @@ def gemm1(a_sorted: torch.Tensor, a_scale_t: torch.Tensor, w1i: torch.Tensor, w1
         out_scale_t = torch.empty((inter // 128, rows_cap), dtype=torch.float32, device=a_sorted.device)
     _lib.call("b2m_gemm1", a_sorted.data_ptr(), a_scale_t.data_ptr(), rows_cap, hidden, w1i.data_ptr(),
               w1i_scale.data_ptr(), e, inter, expert_ids.data_ptr(), ntpp.data_ptr(), _ptr(block_pairs),
-              _ptr(sorted_ids), numel, out_q.data_ptr(), out_scale_t.data_ptr(), _ptr(status),
-              _stream(a_sorted.device))
+              out_q.data_ptr(), out_scale_t.data_ptr(), _ptr(status), _stream(a_sorted.device))
     return out_q, out_scale_t
 
 

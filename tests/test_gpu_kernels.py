@@ -256,8 +256,7 @@ def test_gemm1_gemm2_against_float64(T, H, I, E, k, zipf, paired):
     a_st = torch.empty((H // 128, rows_cap), dtype=torch.float32, device=DEV)
     ops.dispatch_rows(xq, xs, pp, k, a_sorted, a_st)
     status = ops.new_status(DEV)
-    hq, hst = ops.gemm1(a_sorted, a_st, w1i, w1is, eids, ntpp, status=status, block_pairs=bp, sorted_ids=sorted_ids,
-                        numel=T * k)
+    hq, hst = ops.gemm1(a_sorted, a_st, w1i, w1is, eids, ntpp, status=status, block_pairs=bp)
     staged = ops.gemm2(hq, hst, w2q.to(DEV), w2s.to(DEV), sorted_ids, eids, ntpp, T * k, wts.reshape(-1).to(DEV),
                        status=status, block_pairs=bp)
     torch.cuda.synchronize()
@@ -289,47 +288,6 @@ def test_gemm1_gemm2_against_float64(T, H, I, E, k, zipf, paired):
     y = np.einsum("ri,rni->rn", h_gpu, W2[eid_rows[rows]]) * wts.reshape(-1).numpy()[pairs][:, None]
     got = staged.float().cpu().numpy()[pairs]
     np.testing.assert_allclose(got, y, rtol=2 ** -7, atol=1e-3 * np.abs(y).max())
-
-
-@pytest.mark.parametrize("T,H,I,E,k", [(300, 1024, 384, 16, 4), (64, 256, 512, 8, 2), (1000, 512, 256, 64, 8)])
-def test_half_tiles_match_full_tiles(T, H, I, E, k):
-    """Blocks whose rows [64, 128) are pads run as M = 64 tiles (the gate/up GEMM when given
-    the sorted ids, the down GEMM always): their valid rows come out bit-identical to the
-    M = 128 tiles' rows, the pad rows [64, 128) of such blocks are left as they were, and the
-    down GEMM gives the same output on either intermediate."""
-    x, w1q, w1s, w2q, w2s, ids, wts = _gemm_problem(T, H, I, E, k, 5 * T + E, True)
-    xq, xs = ops.quant_g128(x.to(DEV))
-    w1i, w1is = ops.w1_interleave(w1q.to(DEV), w1s.to(DEV))
-    pp = torch.empty(T * k, dtype=torch.int32, device=DEV)
-    sorted_ids, eids, ntpp = ops.moe_align_block_size(ids.to(DEV), 128, E, pair_pos=pp)
-    rows_cap = eids.numel() * 128
-    a_sorted = torch.empty((rows_cap, H), dtype=torch.float8_e4m3fn, device=DEV)
-    a_st = torch.empty((H // 128, rows_cap), dtype=torch.float32, device=DEV)
-    ops.dispatch_rows(xq, xs, pp, k, a_sorted, a_st)
-    status = ops.new_status(DEV)
-    hq_f, hst_f = ops.gemm1(a_sorted, a_st, w1i, w1is, eids, ntpp, status=status)       # every tile M = 128
-    hq_h = torch.full((rows_cap, I), 0x7F, dtype=torch.uint8, device=DEV)               # e4m3 NaN
-    hst_h = torch.full((I // 128, rows_cap), float("nan"), dtype=torch.float32, device=DEV)
-    ops.gemm1(a_sorted, a_st, w1i, w1is, eids, ntpp, hq_h.view(ops.FP8), hst_h, status, sorted_ids=sorted_ids,
-              numel=T * k)
-    w2d, w2sd, wd = w2q.to(DEV), w2s.to(DEV), wts.reshape(-1).to(DEV).contiguous()
-    st_f = ops.gemm2(hq_f, hst_f, w2d, w2sd, sorted_ids, eids, ntpp, T * k, wd, status=status)
-    st_h = ops.gemm2(hq_h.view(ops.FP8), hst_h, w2d, w2sd, sorted_ids, eids, ntpp, T * k, wd, status=status)
-    torch.cuda.synchronize()
-    ops.check_status(status)
-    n = int(ntpp.item())
-    srt = sorted_ids.cpu().numpy()[:n]
-    blocks = srt.reshape(-1, 128)
-    e_blk = eids.cpu().numpy()[:n // 128]
-    half = (blocks[:, 64] >= T * k) & (e_blk >= 0)
-    assert half.any() and (~half).any()
-    valid = srt < T * k
-    assert np.array_equal(hq_h.cpu().numpy()[:n][valid], hq_f.view(torch.uint8).cpu().numpy()[:n][valid])
-    assert np.array_equal(hst_h.cpu().numpy()[:, :n][:, valid], hst_f.cpu().numpy()[:, :n][:, valid])
-    pad_rows = np.zeros(n, dtype=bool)
-    pad_rows.reshape(-1, 128)[half, 64:] = True
-    assert (hq_h.cpu().numpy()[:n][pad_rows] == 0x7F).all()          # rows [64, 128) of half blocks untouched
-    assert torch.equal(st_h, st_f)
 
 
 @pytest.mark.parametrize("paired", [True, False], ids=["pair", "single"])
