@@ -735,6 +735,9 @@ def main() -> int:
                          "gemm1_flops_per_launch": f1, "layer": layer_roof},
             "parity": parity,
             "clocks": clocks,
+            "stages_us": {"median_per_step_max_over_ranks": {k: round(v, 1) for k, v in stages.items()},
+                          "how": "CUDA events the layer records between its kernels in every timed step; each "
+                                 "stage is keyed by the event that closes it"},
             "comm": comm,
             "cpu_baseline": cpu,
         }

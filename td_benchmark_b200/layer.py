@@ -145,6 +145,7 @@ class NullExchange:
 
     def down_and_scatter(self, layer: "MoELayer", topk_weights, ids, shared_out) -> torch.Tensor:
         layer.gemm2(topk_weights)
+        layer._event("gemm2_end")
         return ops.combine(layer.staged, layer.top_k, ids, layer.expert_map, shared_out, layer.out_local)
 
     def close(self) -> None:
