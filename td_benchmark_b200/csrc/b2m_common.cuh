@@ -454,14 +454,17 @@ __device__ __forceinline__ uint32_t local_pair_mask(const int32_t* __restrict__ 
 }
 
 // Eight columns [c, c + 8) of token t's combined row: the staged rows of its counting
-// pairs summed in ascending j in fp32 (pairs j >= 32 are tested one by one), then the
-// shared expert's row, one rounding to bf16.  All loads of a group of eight pairs are
-// issued before the first add.
-__device__ __forceinline__ uint4 combine_vec(const __nv_bfloat16* __restrict__ staged, int64_t t, int top_k,
-                                             int64_t hidden, int64_t c, uint32_t mask,
-                                             const int32_t* __restrict__ topk_ids,
-                                             const int32_t* __restrict__ expert_map,
-                                             const __nv_bfloat16* __restrict__ shared) {
+// pairs summed in ascending j in fp32, then the shared expert's row, one rounding to bf16.
+// All loads of a group of eight pairs are issued before the first add.  Pairs j < 32 count
+// by `mask`; kWide (top_k > 32) tests pairs j >= 32 one by one through the expert map --
+// a separate instantiation, because that dependent lookup in the loop would otherwise
+// serialise the row loads of every call (a third of the combine's bandwidth).
+template <bool kWide>
+__device__ __forceinline__ uint4 combine_vec_impl(const __nv_bfloat16* __restrict__ staged, int64_t t, int top_k,
+                                                  int64_t hidden, int64_t c, uint32_t mask,
+                                                  const int32_t* __restrict__ topk_ids,
+                                                  const int32_t* __restrict__ expert_map,
+                                                  const __nv_bfloat16* __restrict__ shared) {
   float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   for (int j0 = 0; j0 < top_k; j0 += 8) {
     uint4 u[8];
@@ -469,8 +472,11 @@ __device__ __forceinline__ uint4 combine_vec(const __nv_bfloat16* __restrict__ s
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int jj = j0 + j;
-      use[j] = jj < top_k && (jj < 32 ? ((mask >> jj) & 1u) != 0
-                                      : (!expert_map || __ldg(expert_map + __ldg(topk_ids + t * top_k + jj)) >= 0));
+      if (kWide)
+        use[j] = jj < top_k && (jj < 32 ? ((mask >> jj) & 1u) != 0
+                                        : (!expert_map || __ldg(expert_map + __ldg(topk_ids + t * top_k + jj)) >= 0));
+      else
+        use[j] = jj < top_k && ((mask >> (jj & 31)) & 1u) != 0;
       if (use[j]) u[j] = __ldg(reinterpret_cast<const uint4*>(staged + (t * top_k + jj) * hidden + c));
     }
 #pragma unroll
@@ -479,6 +485,16 @@ __device__ __forceinline__ uint4 combine_vec(const __nv_bfloat16* __restrict__ s
   }
   if (shared) acc_bf16x8(__ldg(reinterpret_cast<const uint4*>(shared + t * hidden + c)), a);
   return pack_bf16x8(a);
+}
+
+// Callers instantiate their kernel for both cases and launch the wide one only when top_k > 32.
+template <bool kWide>
+__device__ __forceinline__ uint4 combine_vec(const __nv_bfloat16* __restrict__ staged, int64_t t, int top_k,
+                                             int64_t hidden, int64_t c, uint32_t mask,
+                                             const int32_t* __restrict__ topk_ids,
+                                             const int32_t* __restrict__ expert_map,
+                                             const __nv_bfloat16* __restrict__ shared) {
+  return combine_vec_impl<kWide>(staged, t, top_k, hidden, c, mask, topk_ids, expert_map, shared);
 }
 
 }  // namespace b2m

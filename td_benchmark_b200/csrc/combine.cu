@@ -15,6 +15,7 @@ constexpr int64_t kCombineChunk = 1024;  // columns of one work unit (4 warp-wid
 // token's 1024-column chunk -- at a time, so the grid (every resident warp) finishes in
 // near-equal shares instead of in waves of whole tokens; the token's expert ids and map
 // entries give a warp-uniform pair mask, and the lanes walk the chunk 8 columns at a time.
+template <bool kWide>
 __global__ void __launch_bounds__(kCombineThreads)
     combine_kernel(const __nv_bfloat16* __restrict__ staged, int64_t tokens, int top_k, int64_t hidden,
                    const int32_t* __restrict__ topk_ids, const int32_t* __restrict__ expert_map,
@@ -30,7 +31,7 @@ __global__ void __launch_bounds__(kCombineThreads)
 #pragma unroll 2
     for (int64_t c = (u - t * chunks) * kCombineChunk + lane * 8; c < c_end; c += 256)
       *reinterpret_cast<uint4*>(out + t * ld_out + c) =
-          combine_vec(staged, t, top_k, hidden, c, mask, topk_ids, expert_map, shared);
+          combine_vec<kWide>(staged, t, top_k, hidden, c, mask, topk_ids, expert_map, shared);
   }
 }
 
@@ -86,18 +87,20 @@ extern "C" int b2m_combine(const void* staged, int64_t tokens, int32_t top_k, in
   if (!aligned16(staged) || !aligned16(out) || (shared && !aligned16(shared)))
     return fail(B2M_ERR_ARG, "combine: pointers must be 16-byte aligned");
   // every resident warp, or fewer when there are fewer units
-  static std::atomic<int> resident{0};  // blocks per SM (the same on every sm_100 device)
-  int per_sm = resident.load(std::memory_order_relaxed);
+  const bool wide = top_k > 32;
+  auto kernel = wide ? combine_kernel<true> : combine_kernel<false>;
+  static std::atomic<int> resident[2] = {0, 0};  // blocks per SM (the same on every sm_100 device)
+  int per_sm = resident[wide].load(std::memory_order_relaxed);
   if (per_sm == 0) {
-    B2M_TRY(check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, combine_kernel, kCombineThreads, 0),
+    B2M_TRY(check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kCombineThreads, 0),
                        "combine: occupancy"));
     per_sm = per_sm > 0 ? per_sm : 1;
-    resident.store(per_sm, std::memory_order_relaxed);
+    resident[wide].store(per_sm, std::memory_order_relaxed);
   }
   const int64_t units = tokens * ((hidden + kCombineChunk - 1) / kCombineChunk);
   int64_t blocks = (units * 32 + kCombineThreads - 1) / kCombineThreads;
   if (blocks > int64_t(num_sms) * per_sm) blocks = int64_t(num_sms) * per_sm;
-  combine_kernel<<<static_cast<unsigned>(blocks), kCombineThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  kernel<<<static_cast<unsigned>(blocks), kCombineThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, topk_ids, expert_map,
       static_cast<const __nv_bfloat16*>(shared), static_cast<__nv_bfloat16*>(out), ld_out);
   return check_cuda(cudaGetLastError(), "combine launch");

@@ -274,6 +274,7 @@ __global__ void __launch_bounds__(kThreads)
 // ---------------------------------------------------------------- reduce-scatter push
 // One warp per token (pair mask read once), lanes over the column window 8 at a time;
 // the combined row goes to the owner's slot for this source.
+template <bool kWide>
 __global__ void __launch_bounds__(kThreads)
     combine_push_kernel(const __nv_bfloat16* __restrict__ staged, int64_t tokens, int top_k, int64_t hidden,
                         int64_t col0, int64_t col1, const int32_t* __restrict__ topk_ids,
@@ -292,7 +293,8 @@ __global__ void __launch_bounds__(kThreads)
     __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(slots.p[owner]) + slot_row * hidden;
 #pragma unroll 2
     for (int64_t c = col0 + lane * 8; c < col1; c += 256)
-      *reinterpret_cast<uint4*>(dst + c) = combine_vec(staged, t, top_k, hidden, c, mask, topk_ids, expert_map, shared);
+      *reinterpret_cast<uint4*>(dst + c) =
+          combine_vec<kWide>(staged, t, top_k, hidden, c, mask, topk_ids, expert_map, shared);
   }
   if (counter) publish_when_grid_done(counter, flags, world, epoch);
 }
@@ -371,6 +373,7 @@ __global__ void __launch_bounds__(kThreads)
 // (hidden bytes) and fp32 scales (hidden / 128) go to the owner's FP8 slot for this source:
 // H + H/32 bytes per row instead of 2H.  One warp per token; in each 256-column step lanes
 // 0-15 hold one 128-group (8 values each) and lanes 16-31 the next.
+template <bool kWide>
 __global__ void __launch_bounds__(kThreads)
     combine_push_fp8_kernel(const __nv_bfloat16* __restrict__ staged, int64_t tokens, int top_k, int64_t hidden,
                             const int32_t* __restrict__ topk_ids, const int32_t* __restrict__ expert_map,
@@ -393,7 +396,7 @@ __global__ void __launch_bounds__(kThreads)
       const int64_t c = c0 + lane * 8;
       const bool in = c < hidden;  // hidden % 128 == 0: a half-warp is all in or all out
       uint4 v = make_uint4(0, 0, 0, 0);
-      if (in) v = combine_vec(staged, t, top_k, hidden, c, mask, topk_ids, expert_map, shared);
+      if (in) v = combine_vec<kWide>(staged, t, top_k, hidden, c, mask, topk_ids, expert_map, shared);
       float f[8];
       bf16x8_to_f32(v, f);
       const float scale = fmaxf(halfwarp_amax(f) / 448.0f, 1e-12f);
@@ -791,7 +794,8 @@ int b2m_combine_push(const void* staged, int64_t tokens, int32_t top_k, int64_t 
   }
   int grid = grid_for(tokens * 32, num_sms, 8);  // a warp per token
   if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
-  combine_push_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  (top_k > 32 ? combine_push_kernel<true> : combine_push_kernel<false>)<<<grid, kThreads, 0,
+                                                                          static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, col_begin, col_end, topk_ids, expert_map,
       static_cast<const __nv_bfloat16*>(shared), world, rank, sl, f, epoch, counter, sparse);
   return check_cuda(cudaGetLastError(), "combine_push launch");
@@ -872,7 +876,8 @@ int b2m_combine_push_fp8(const void* staged, int64_t tokens, int32_t top_k, int6
     sc.p[r] = scale_dst[r];
     f.p[r] = counter ? flag_dst[r] : nullptr;
   }
-  combine_push_fp8_kernel<<<grid_for(tokens * 32, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  (top_k > 32 ? combine_push_fp8_kernel<true> : combine_push_fp8_kernel<false>)<<<
+      grid_for(tokens * 32, num_sms, 8), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(staged), tokens, top_k, hidden, topk_ids, expert_map,
       static_cast<const __nv_bfloat16*>(shared), world, rank, q, sc, f, epoch, counter, sparse);
   return check_cuda(cudaGetLastError(), "combine_push_fp8 launch");
