@@ -332,6 +332,27 @@ def test_combine_bit_exact(T, k, H, shared):
     assert np.array_equal(out.view(torch.int16).cpu().numpy().astype(np.uint16), exp)
 
 
+@pytest.mark.parametrize("k", [8, 40])
+def test_combine_expert_map_bit_exact(k):
+    """Only local pairs count (expert map >= 0), summed in ascending j, then the shared row;
+    k = 40 takes the kernel instantiation that tests pairs j >= 32 one by one."""
+    T, H, E = 96, 512, 64
+    g = torch.Generator().manual_seed(k)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    emap = torch.full((E,), -1, dtype=torch.int32)
+    emap[::3] = torch.arange(len(emap[::3]), dtype=torch.int32)
+    st = _bf16((T * k, H), 11)
+    sh = _bf16((T, H), 12)
+    out = ops.combine(st.to(DEV), k, ids.to(DEV), emap.to(DEV), sh.to(DEV))
+    local = (emap[ids.long()] >= 0).numpy()
+    s3 = st.float().numpy().reshape(T, k, H)
+    acc = np.zeros((T, H), np.float32)
+    for j in range(k):
+        acc = np.where(local[:, j:j + 1], (acc + s3[:, j]).astype(np.float32), acc)
+    acc = (acc + sh.float().numpy()).astype(np.float32)
+    assert np.array_equal(out.view(torch.int16).cpu().numpy().astype(np.uint16), ofp8.f32_to_bf16_bits(acc))
+
+
 @pytest.mark.parametrize("world,src,paired,H", [(2, 1, False, 512), (4, 0, False, 640), (4, 3, True, 512),
                                                  (2, 0, False, 384)])
 def test_gemm2_scatter_and_rs_combine(world, src, paired, H):
