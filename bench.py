@@ -451,9 +451,10 @@ def main() -> int:
     ap.add_argument("--impl", default="b2m", choices=["b2m", "reference"])
     ap.add_argument("--comm", default="p2p", choices=["p2p", "nccl"],
                     help="exchange of the multi-GPU layer: fused peer memory (default) or NCCL")
-    ap.add_argument("--rs-mode", default="sm", choices=["sm", "gemm", "ce"],
-                    help="fused reduce-scatter: SM stores from the combine (default), from the down GEMM's epilogue, "
-                         "or copy-engine push")
+    ap.add_argument("--rs-mode", default="auto", choices=["auto", "sm", "gemm", "ce"],
+                    help="fused reduce-scatter: rows stored to their owners by the down GEMM (gemm), SM stores from "
+                         "the combine (sm), copy-engine push (ce); auto (default): gemm, or sm for a tensor-parallel "
+                         "layer with a shared expert")
     ap.add_argument("--ag-mode", default="auto", choices=["auto", "sm", "ce", "push"],
                     help="fused all-gather: SM stores from the quant kernel, copy-engine copies, or by block size")
     ap.add_argument("--rs-dtype", default="bf16", choices=["bf16", "fp8"],
@@ -495,7 +496,7 @@ def main() -> int:
     exchange = None
     if world > 1 and args.comm == "p2p":
         from td_benchmark_b200.layer import P2PExchange
-        if args.rs_dtype == "fp8" and args.rs_mode != "sm":
+        if args.rs_dtype == "fp8" and args.rs_mode not in ("sm", "auto"):
             raise SystemExit("--rs-dtype fp8 needs --rs-mode sm")
         exchange = P2PExchange(ctx.group, chunks=args.chunks,
                                rs_mode="fp8" if args.rs_dtype == "fp8" else args.rs_mode, ce_streams=args.ce_streams,

@@ -278,7 +278,8 @@ class P2PExchange:
            straight from registers stalled the GEMM: DeepSeek-V3 EP8 down GEMM 1424 us
            instead of 448.)  Under expert parallelism this is sparse by construction: only
            the pairs this rank computed cross, each to its token's owner.
-      "sm" (default) -- after the whole down GEMM, ``b2m_combine_push`` stores each
+      "auto" (default) -- "gemm", or "sm" for a tensor-parallel layer with a shared expert.
+      "sm" -- after the whole down GEMM, ``b2m_combine_push`` stores each
            token's partial into its owner's slot with SM stores and publishes the flags.
       "ce" -- the down GEMM runs in ``chunks`` column chunks on all SMs; after each chunk
            the combine writes the per-owner partials into a local staging buffer (own
@@ -298,12 +299,12 @@ class P2PExchange:
     MAX_CHUNKS = 8
     AG_CE_MIN_BYTES = 6 << 20   # between the measured win (7 MiB blocks) and loss (2 MiB blocks)
 
-    def __init__(self, group=None, chunks: int = 4, rs_mode: str = "sm", ce_streams: int = 2, ag_mode: str = "auto",
+    def __init__(self, group=None, chunks: int = 4, rs_mode: str = "auto", ce_streams: int = 2, ag_mode: str = "auto",
                  sparse: bool = False):
         import torch.distributed as dist
-        if rs_mode not in ("ce", "sm", "gemm", "fp8") or ag_mode not in ("ce", "sm", "auto", "push"):
-            raise ValueError(f"rs_mode must be 'gemm', 'ce', 'sm' or 'fp8' and ag_mode 'push', 'ce', 'sm' or 'auto', "
-                             f"got {rs_mode!r}, {ag_mode!r}")
+        if rs_mode not in ("auto", "ce", "sm", "gemm", "fp8") or ag_mode not in ("ce", "sm", "auto", "push"):
+            raise ValueError(f"rs_mode must be 'auto', 'gemm', 'ce', 'sm' or 'fp8' and ag_mode 'push', 'ce', 'sm' or "
+                             f"'auto', got {rs_mode!r}, {ag_mode!r}")
         self.ag_mode = ag_mode
         self.sparse = sparse
         self.dist = dist
@@ -321,6 +322,8 @@ class P2PExchange:
         from .symm import SymmetricWorkspace, ptr_array
 
         P, T, H, Tl = self.world_size, layer.T, layer.H, layer.T_local
+        if self.rs_mode == "auto":   # the down GEMM's own stores, unless a TP shared expert must join first
+            self.rs_mode = "sm" if (layer.shared is not None and not layer.ep) else "gemm"
         if self.sparse:
             # sends decided per (token, rank) by SM stores: no contiguous-block copies
             # (rs_mode 'gemm' is sparse already: each pair row goes only to its token's owner)

@@ -68,7 +68,7 @@ class MoEOverlapState:
         if self.tp_size == 1:
             return NullExchange()
         if self.exchange == "p2p":
-            return P2PExchange(self.tp_group, rs_mode="fp8" if rs_fp8 else "sm")
+            return P2PExchange(self.tp_group, rs_mode="fp8" if rs_fp8 else "auto")
         return NcclExchange(self.tp_group, rs_dtype="fp8" if rs_fp8 else "bf16")
 
 

@@ -33,8 +33,9 @@ P2P_TUNABLES = {
     "ag_mode": TunableSpec(str, "auto", "all-gather by SM stores from the quant kernel ('sm'), copy engines ('ce'), "
                                         "by block size ('auto'), or (TP) straight into the peers' sorted operand "
                                         "under the gate/up GEMM ('push')"),
-    "rs_mode": TunableSpec(str, "sm", "reduce-scatter by SM stores from the combine ('sm'), from the down GEMM's "
-                                      "epilogue ('gemm') or copy engines ('ce')"),
+    "rs_mode": TunableSpec(str, "auto", "reduce-scatter by SM stores from the combine ('sm'), from the down GEMM's "
+                                        "epilogue ('gemm'), copy engines ('ce'), or 'auto': 'gemm' unless a "
+                                        "tensor-parallel shared expert must join the partials first ('sm')"),
     "rs_chunks": TunableSpec(int, 4, "down-GEMM column chunks of the copy-engine reduce-scatter (1..8)"),
 }
 # expert-parallel schemes (d2, d4)
@@ -49,7 +50,7 @@ EP_SPARSE = {
                                        "from those ranks (all-gather and reduce-scatter by SM stores; same output as "
                                        "the dense exchange, fewer NVLink bytes)"),
 }
-_CHOICES = {"ag_mode": ("sm", "ce", "auto", "push"), "rs_mode": ("sm", "ce", "gemm"), "rs_dtype": ("bf16", "fp8"),
+_CHOICES = {"ag_mode": ("sm", "ce", "auto", "push"), "rs_mode": ("auto", "sm", "ce", "gemm"), "rs_dtype": ("bf16", "fp8"),
             "placement": ("contiguous", "balanced")}
 
 
@@ -118,7 +119,7 @@ def build_layer(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, exchange: Any =
             t.update({k: v for k, v in (tunables or {}).items() if k in P2P_TUNABLES})
             rs_mode = t["rs_mode"]
             if rs_dtype == "fp8":
-                if rs_mode != "sm":
+                if rs_mode not in ("sm", "auto"):
                     raise SchemeConfigError(f"{spec.code}.rs_dtype='fp8' needs rs_mode='sm', got {rs_mode!r}")
                 rs_mode = "fp8"
             exchange = P2PExchange(ctx.group, chunks=t["rs_chunks"], rs_mode=rs_mode, ag_mode=t["ag_mode"],
@@ -138,7 +139,7 @@ def build_instance(spec: SchemeSpec, cfg: Any, ctx: Any, data: Any, scheme_cfg: 
     for name, allowed in _CHOICES.items():
         if name in tunables and tunables[name] not in allowed:
             raise SchemeConfigError(f"{spec.code}.{name}={tunables[name]!r} violates schema: expected one of {allowed}")
-    if tunables.get("rs_dtype") == "fp8" and tunables.get("rs_mode", "sm") != "sm":
+    if tunables.get("rs_dtype") == "fp8" and tunables.get("rs_mode", "auto") not in ("sm", "auto"):
         raise SchemeConfigError(f"{spec.code}.rs_dtype='fp8' violates schema: needs rs_mode='sm', got "
                                 f"{tunables['rs_mode']!r}")
     if "rs_chunks" in tunables and not 1 <= tunables["rs_chunks"] <= 8:

@@ -110,7 +110,7 @@ def test_scheme_registry_and_tunables():
 
 def test_p2p_exchange_tunables():
     spec, _ = REGISTRY["d3"]
-    assert validate_tunables(spec, {}) == {"check_status": False, "rs_dtype": "bf16", "ag_mode": "auto", "rs_mode": "sm",
+    assert validate_tunables(spec, {}) == {"check_status": False, "rs_dtype": "bf16", "ag_mode": "auto", "rs_mode": "auto",
                                            "rs_chunks": 4}
     with pytest.raises(SchemeConfigError, match="violate schema"):
         validate_tunables(REGISTRY["d1"][0], {"ag_mode": "ce"})   # NCCL schemes have no exchange knobs
