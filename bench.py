@@ -459,9 +459,11 @@ def main() -> int:
                     help="fused all-gather: SM stores from the quant kernel, copy-engine copies, or by block size")
     ap.add_argument("--rs-dtype", default="bf16", choices=["bf16", "fp8"],
                     help="reduce-scatter payload: bf16 partials, or 1x128 e4m3 codes + scales (the b3 variant)")
-    ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
-                    help="expert parallel: E/P experts per rank balanced by routed pairs (default) or the reference's "
-                         "contiguous ranges")
+    ap.add_argument("--placement", default="auto", choices=["auto", "balanced", "contiguous"],
+                    help="expert placement under expert parallelism: the reference's contiguous ranges, experts "
+                         "balanced by routed pairs, or auto: balanced from 4 ranks up, contiguous below (measured on "
+                         "the DeepSeek-V3 shape: balancing cuts the most-loaded rank's compute at 4 and 8 ranks, "
+                         "and costs time at 2)")
     ap.add_argument("--sparse", action="store_true",
                     help="expert parallel: send tokens / partials only to / from the ranks holding their experts")
     ap.add_argument("--chunks", type=int, default=4, help="down-GEMM column chunks of the copy-engine push")
@@ -504,6 +506,8 @@ def main() -> int:
     elif world > 1:
         from td_benchmark_b200.layer import NcclExchange
         exchange = NcclExchange(ctx.group, rs_dtype=args.rs_dtype)
+    if args.placement == "auto":
+        args.placement = "balanced" if world >= 4 else "contiguous"
     layer, level = build_layer(spec, cfg, ctx, bundle, exchange=exchange, placement=args.placement)
     T = layer.T
     x = bundle.hidden_local.contiguous()
