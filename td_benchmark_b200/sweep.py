@@ -11,7 +11,8 @@ launched world size; the data bundle of a (T, routing) pair is built once and sh
 its variants.  Variants (expert parallel, scheme d2 / d4):
 
 * ``nccl``   NCCL all-gather + NCCL bf16 reduce-scatter (the unfused comparison);
-* ``fused``  peer-memory exchange with its default transports;
+* ``fused``  peer-memory exchange with its default transports (reduce-scatter from the down GEMM);
+* ``sm``     the same with the reduce-scatter as SM stores from a combine kernel after the down GEMM;
 * ``sparse`` peer-memory exchange sending tokens / partials only to / from the ranks that
              hold their experts;
 * ``fp8rs``  peer-memory exchange with the FP8 reduce-scatter payload;
@@ -71,6 +72,8 @@ def _exchange(variant: str, ctx):
         return NcclExchange(ctx.group)
     if variant == "fused":
         return P2PExchange(ctx.group)
+    if variant == "sm":
+        return P2PExchange(ctx.group, rs_mode="sm")
     if variant == "sparse":
         return P2PExchange(ctx.group, sparse=True)
     if variant in ("fp8rs", "balanced-fp8rs"):

@@ -213,6 +213,7 @@ def test_sweep_variant_table():
         assert sweep._exchange("nccl", ctx).name == "nccl"
         ex = sweep._exchange("ce4", ctx)
         assert ex.rs_mode == "ce" and ex.chunks_req == 4
+        assert sweep._exchange("sm", ctx).rs_mode == "sm" and sweep._exchange("fused", ctx).rs_mode == "auto"
         assert sweep._exchange("sparse", ctx).sparse and sweep._exchange("fp8rs", ctx).rs_mode == "fp8"
         with pytest.raises(ValueError):
             sweep._exchange("ring", ctx)
