@@ -453,8 +453,8 @@ def main() -> int:
                     help="exchange of the multi-GPU layer: fused peer memory (default) or NCCL")
     ap.add_argument("--rs-mode", default="auto", choices=["auto", "sm", "gemm", "ce"],
                     help="fused reduce-scatter: rows stored to their owners by the down GEMM (gemm), SM stores from "
-                         "the combine (sm), copy-engine push (ce); auto (default): gemm, or sm for a tensor-parallel "
-                         "layer with a shared expert")
+                         "the combine (sm), copy-engine push (ce); auto (default): gemm when the pair rows are at most "
+                         "twice the partials' bytes (top_k <= 2 TP, <= 2P EP) or with >= 2048 local tokens, else sm")
     ap.add_argument("--ag-mode", default="auto", choices=["auto", "sm", "ce", "push"],
                     help="fused all-gather: SM stores from the quant kernel, copy-engine copies, or by block size")
     ap.add_argument("--rs-dtype", default="bf16", choices=["bf16", "fp8"],

@@ -278,7 +278,10 @@ class P2PExchange:
            straight from registers stalled the GEMM: DeepSeek-V3 EP8 down GEMM 1424 us
            instead of 448.)  Under expert parallelism this is sparse by construction: only
            the pairs this rank computed cross, each to its token's owner.
-      "auto" (default) -- "gemm", or "sm" for a tensor-parallel layer with a shared expert.
+      "auto" (default) -- "gemm" when a token's pair rows are at most twice the bytes of its
+           partials (top_k <= 2 under TP, top_k <= 2P under EP) or with at least
+           ``RS_GEMM_MIN_TOKENS`` local tokens; otherwise, and for a tensor-parallel layer with a
+           shared expert, "sm".
       "sm" -- after the whole down GEMM, ``b2m_combine_push`` stores each
            token's partial into its owner's slot with SM stores and publishes the flags.
       "ce" -- the down GEMM runs in ``chunks`` column chunks on all SMs; after each chunk
@@ -298,6 +301,12 @@ class P2PExchange:
     name = "p2p"
     MAX_CHUNKS = 8
     AG_CE_MIN_BYTES = 6 << 20   # between the measured win (7 MiB blocks) and loss (2 MiB blocks)
+    # rs_mode 'auto': the down GEMM sends a token's pair rows (top_k per token under TP, top_k / P
+    # per rank under EP) where the SM-store path sends one partial.  It pays off when that is at
+    # most twice the bytes, or with at least this many local tokens (DeepSeek-V3 shape, 4x the
+    # bytes, on 2 B200s: 2-6 % slower than SM stores at 256 and 1024 local tokens, 0.4-2 % faster
+    # at 4096; at 2x the bytes on 4 B200s 6 % faster at 2048).
+    RS_GEMM_MIN_TOKENS = 2048
 
     def __init__(self, group=None, chunks: int = 4, rs_mode: str = "auto", ce_streams: int = 2, ag_mode: str = "auto",
                  sparse: bool = False):
@@ -323,7 +332,10 @@ class P2PExchange:
 
         P, T, H, Tl = self.world_size, layer.T, layer.H, layer.T_local
         if self.rs_mode == "auto":   # the down GEMM's own stores, unless a TP shared expert must join first
-            self.rs_mode = "sm" if (layer.shared is not None and not layer.ep) else "gemm"
+            tp_shared = layer.shared is not None and not layer.ep
+            rows_per_partial = layer.top_k / P if layer.ep else layer.top_k
+            pays = rows_per_partial <= 2 or Tl >= self.RS_GEMM_MIN_TOKENS
+            self.rs_mode = "gemm" if (pays and not tp_shared) else "sm"
         if self.sparse:
             # sends decided per (token, rank) by SM stores: no contiguous-block copies
             # (rs_mode 'gemm' is sparse already: each pair row goes only to its token's owner)

@@ -34,8 +34,9 @@ P2P_TUNABLES = {
                                         "by block size ('auto'), or (TP) straight into the peers' sorted operand "
                                         "under the gate/up GEMM ('push')"),
     "rs_mode": TunableSpec(str, "auto", "reduce-scatter by SM stores from the combine ('sm'), from the down GEMM's "
-                                        "epilogue ('gemm'), copy engines ('ce'), or 'auto': 'gemm' unless a "
-                                        "tensor-parallel shared expert must join the partials first ('sm')"),
+                                        "epilogue ('gemm'), copy engines ('ce'), or 'auto': 'gemm' when the pair rows are "
+                                        "at most twice the partials' bytes (top_k <= 2 TP, <= 2P EP) or with >= "
+                                        "2048 local tokens, else 'sm' (also for a tensor-parallel shared expert)"),
     "rs_chunks": TunableSpec(int, 4, "down-GEMM column chunks of the copy-engine reduce-scatter (1..8)"),
 }
 # expert-parallel schemes (d2, d4)
