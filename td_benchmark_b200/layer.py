@@ -327,15 +327,23 @@ class P2PExchange:
         self.rs_mode = rs_mode
         self.ce_streams = max(1, ce_streams)
 
+    @classmethod
+    def auto_rs_mode(cls, ep: bool, top_k: int, world: int, tokens_local: int, shared: bool) -> str:
+        """The reduce-scatter that ``rs_mode='auto'`` picks: the down GEMM's own stores ('gemm')
+        when a token's pair rows are at most twice the bytes of its partials or there are enough
+        local tokens to hide them, else SM stores ('sm'); always 'sm' for a tensor-parallel
+        layer with a shared expert, whose output must join the partials before they leave."""
+        if shared and not ep:
+            return "sm"
+        rows_per_partial = top_k / world if ep else top_k
+        return "gemm" if (rows_per_partial <= 2 or tokens_local >= cls.RS_GEMM_MIN_TOKENS) else "sm"
+
     def setup(self, layer: "MoELayer") -> None:
         from .symm import SymmetricWorkspace, ptr_array
 
         P, T, H, Tl = self.world_size, layer.T, layer.H, layer.T_local
-        if self.rs_mode == "auto":   # the down GEMM's own stores, unless a TP shared expert must join first
-            tp_shared = layer.shared is not None and not layer.ep
-            rows_per_partial = layer.top_k / P if layer.ep else layer.top_k
-            pays = rows_per_partial <= 2 or Tl >= self.RS_GEMM_MIN_TOKENS
-            self.rs_mode = "gemm" if (pays and not tp_shared) else "sm"
+        if self.rs_mode == "auto":
+            self.rs_mode = self.auto_rs_mode(layer.ep, layer.top_k, P, Tl, layer.shared is not None)
         if self.sparse:
             # sends decided per (token, rank) by SM stores: no contiguous-block copies
             # (rs_mode 'gemm' is sparse already: each pair row goes only to its token's owner)

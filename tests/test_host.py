@@ -220,3 +220,18 @@ def test_sweep_variant_table():
     finally:
         if own:
             dist.destroy_process_group()
+
+
+def test_auto_reduce_scatter_choice():
+    """rs_mode='auto' follows the measured break-even: DeepSeek-V3 (top-8) EP2 takes the down GEMM's
+    stores at 4096 local tokens but SM stores at 1024 and 256; EP4/EP8 (pair rows <= 2x the
+    partials) and Mixtral TP (top-2) take them at any size; a TP shared expert never does."""
+    from td_benchmark_b200.layer import P2PExchange as X
+    assert X.auto_rs_mode(True, 8, 2, 4096, True) == "gemm"
+    assert X.auto_rs_mode(True, 8, 2, 1024, True) == "sm"
+    assert X.auto_rs_mode(True, 8, 2, 256, False) == "sm"
+    assert X.auto_rs_mode(True, 8, 4, 2048, True) == "gemm"
+    assert X.auto_rs_mode(True, 8, 8, 64, True) == "gemm"
+    assert X.auto_rs_mode(False, 2, 8, 512, False) == "gemm"
+    assert X.auto_rs_mode(False, 8, 4, 64, False) == "sm"
+    assert X.auto_rs_mode(False, 2, 2, 4096, True) == "sm"
